@@ -1,0 +1,145 @@
+/*
+ * bsk_capi.h — C ABI of the B200 (sm_100a) BlackwellSparseK operator family.
+ *
+ * Library: libbsk_sm100.so (periodicdent42_b200/libbsk_sm100.so). Plain pointers and sizes only.
+ *
+ * Conventions shared by every entry point:
+ *  - Return 0 (BSK_OK) on success, a negative BSK_ERR_* code otherwise; bsk_last_error() returns a
+ *    thread-local message for the last failure on the calling thread.
+ *  - Device pointers are borrowed; outputs are preallocated by the caller. Nothing is synchronised:
+ *    work is enqueued on `stream` (a cudaStream_t, NULL = legacy default stream) of the current device.
+ *  - Arguments are validated on the host before any launch (shapes, strides, 16-byte alignment needed
+ *    by TMA, BSR index ranges when `check_indices` is requested through bsk_spmm_bsr_validate).
+ *  - Every device-side wait is bounded. A wait that runs out records a code in a per-device error word
+ *    (read and cleared by bsk_device_error) and the kernel returns early with its output incomplete.
+ *  - There is no CPU fallback: without a usable sm_100 device every compute entry point fails with
+ *    BSK_ERR_NO_DEVICE.
+ */
+#ifndef BSK_CAPI_H_
+#define BSK_CAPI_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BSK_OK 0
+#define BSK_ERR_INVALID_ARG (-1)
+#define BSK_ERR_UNSUPPORTED (-2)
+#define BSK_ERR_CUDA (-3)
+#define BSK_ERR_DEVICE_TIMEOUT (-4)
+#define BSK_ERR_NO_DEVICE (-5)
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+int bsk_version(void);
+
+/* Message for the last failing call on this thread ("" if none). */
+const char* bsk_last_error(void);
+
+/* Number of SMs of the current device, or a negative error code. */
+int bsk_device_sm_count(void);
+
+/*
+ * Dense GEMM, fp16 x fp16 -> fp32:  C[M,N] = A[M, k_begin:k_end] * B[k_begin:k_end, N].
+ *   A   : fp16, row-major [M, K], row stride lda (elements, multiple of 8, 16-B aligned base)
+ *   B   : fp16, column-major [K, N] (equivalently B^T row-major [N, K]), column stride ldb
+ *   C   : fp32, row-major [M, N], row stride ldc; overwritten (not accumulated)
+ *   k_begin/k_end select the K range (split-K shards); k_begin must be a multiple of 8.
+ * Replaces the reference's standalone CUTLASS Sm90 program
+ * (BlackwellSparseK/src/gemm_h100_599tflops_final.cu:38-67, run at :144-151), which had no callable
+ * entry point.
+ */
+int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc, int M, int N,
+                    int K, int k_begin, int k_end, void* stream);
+
+/*
+ * FP8 GEMM, e4m3 x e4m3 -> bf16:  D[M,N] = bf16( (A_q[M,K] * B_q[K,N]) * scale_a * scale_b ).
+ *   A   : e4m3 bytes, row-major [M, K] (lda multiple of 16)
+ *   B   : e4m3 bytes, column-major [K, N] (B^T row-major [N, K], ldb multiple of 16)
+ *   scale_a, scale_b : device pointers to one fp32 each (per-tensor dequantisation scales)
+ *   D   : bf16, row-major [M, N], row stride ldd
+ * No reference counterpart exists (the reference only declares e4m3 typedefs,
+ * BlackwellSparseK/.archive/src_experiments/blackwell_sparsek/kernels/attention_fmha.cu:32-42); the
+ * semantics follow torch._scaled_mm(A_q, B_q, scale_a, scale_b, out_dtype=bfloat16).
+ */
+int bsk_gemm_e4m3_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, const float* scale_a,
+                       const float* scale_b, void* D, int64_t ldd, int M, int N, int K, void* stream);
+
+/*
+ * BSR block-sparse x dense SpMM, fp16 x fp16 -> fp32:  C[M,N] = A_bsr[M,K] * B[K,N].
+ *   row_ptr : int32 [Mb+1] block-row pointer (torch crow_indices() narrowed to int32)
+ *   col_idx : int32 [nnzb] block-column indices (torch col_indices()), any order within a row
+ *   vals    : fp16 [nnzb, bs_r, bs_c] row-major blocks (torch values())
+ *   B       : fp16 row-major [K, N], row stride ldb (multiple of 8)
+ *   C       : fp32 row-major [M, N], row stride ldc; block-rows [row_begin, row_end) are overwritten
+ *             (rows without nonzero blocks are written as zeros), other rows are untouched.
+ *   Supported block shape: bs_r = bs_c = 128.
+ * Replaces extern "C" launch_bsr_spmm_async (BlackwellSparseK/src/kernel_launch.cu:33-61), bound by
+ * BlackwellSparseK/python/bsk_bindings.cpp:13-43 and called at :122-129; dense B replaces the
+ * "dense B as BSR" arguments built in BlackwellSparseK/python/ops.py:104-107.
+ */
+int bsk_spmm_bsr_f16f32(const int32_t* row_ptr, const int32_t* col_idx, const void* vals, int bs_r, int bs_c,
+                        int Mb, int nnzb, const void* B, int64_t ldb, float* C, int64_t ldc, int M, int N, int K,
+                        int row_begin, int row_end, void* stream);
+
+/*
+ * Host-side check of a BSR index structure held in HOST memory (row_ptr[0] == 0, non-decreasing,
+ * row_ptr[Mb] == nnzb, 0 <= col_idx < Kb). Returns BSK_OK or BSK_ERR_INVALID_ARG with a message.
+ * The reference performs no such check (BlackwellSparseK/python/ops.py:56-69 validates shapes only).
+ */
+int bsk_bsr_validate_host(const int32_t* row_ptr, const int32_t* col_idx, int Mb, int Kb, int nnzb);
+
+/*
+ * Block-sparse attention forward, bf16:  O = softmax(scale * Q K^T, restricted to the block mask) V
+ *   Q, K, V, O : bf16 contiguous [B, H, S, D], D = 128
+ *   row_ptr    : int32 [B*H*(S/blk) + 1], col_idx int32 [nnz]: for (b,h) pair p and query block-row i
+ *                the nonzero key blocks are col_idx[row_ptr[p*(S/blk)+i] .. row_ptr[p*(S/blk)+i+1]).
+ *                col_idx values are within-sequence block indices (0 .. S/blk-1).
+ *   blk        : 128. A key block with index equal to the query block index is masked elementwise-causally
+ *                (key position > query position excluded) when `causal_diag` is non-zero.
+ *   bh_begin/bh_end : the (b,h) pairs to compute (sharding); other pairs of O are untouched.
+ *   Query rows whose mask row is empty are written as zeros.
+ * Replaces extern "C" launch_attention_forward
+ * (BlackwellSparseK/.archive/src_experiments/blackwell_sparsek/kernels/attention_fmha.cu:386-426), which
+ * had no block mask, and its binding attention_forward_cuda (.../kernels/kernel_bindings.cpp:66-102).
+ */
+int bsk_bsattn_fwd_bf16(const void* Q, const void* K, const void* V, void* O, const int32_t* row_ptr,
+                        const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale, int causal_diag,
+                        int bh_begin, int bh_end, void* stream);
+
+/*
+ * Drop-in for the reference's launcher signature (BlackwellSparseK/src/kernel_launch.cu:33-61).
+ * A is BSR with blocks of (M/A_M_blocks) x (K/A_K_blocks); B must be the all-blocks pattern the reference
+ * Python layer builds (BlackwellSparseK/python/ops.py:104-107), whose value buffer is the dense row-major
+ * [K, N] matrix. BM/BN/BK are accepted and ignored (the sm_100 kernel picks its own tiles). Returns
+ * nothing, like the reference; failures are reported through bsk_last_error().
+ */
+void launch_bsr_spmm_async(const int* A_row_ptr, const int* A_col_idx, const void* A_vals, int A_M_blocks,
+                           int A_K_blocks, int A_nnzb, const int* B_row_ptr, const int* B_col_idx, const void* B_vals,
+                           int B_K_blocks, int B_N_blocks, int B_nnzb, float* C, int M, int N, int K, int ldc, int BM,
+                           int BN, int BK, void* stream);
+
+/*
+ * Reads and clears the per-device error word of the current device. *out = 0 when no kernel reported
+ * anything; otherwise bits [0,8) kind (1 wait timeout, 2 bounds), [8,16) kernel id, [16,32) site.
+ * Synchronises the device.
+ */
+int bsk_device_error(uint32_t* out);
+
+/* Per-wait limit in nanoseconds used by subsequent launches on this thread (default 2e9). */
+int bsk_set_wait_timeout_ns(uint64_t ns);
+
+/*
+ * Failure-detection self-test: launches one CTA that waits on an mbarrier nothing will complete, with
+ * the given limit (1e3 .. 1e10 ns). Returns BSK_ERR_DEVICE_TIMEOUT when the bounded wait ran out and the
+ * kernel returned, which is the expected outcome. No reference counterpart (the reference has no
+ * device-side failure detection).
+ */
+int bsk_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BSK_CAPI_H_ */

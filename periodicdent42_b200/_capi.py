@@ -1,0 +1,155 @@
+"""ctypes binding of the C ABI in include/bsk_capi.h (libbsk_sm100.so).
+
+This is the path the parity tests and the benchmark use to call the kernels exactly as a foreign
+caller would (plain pointers, sizes and a cudaStream_t). There is no fallback: if the library is
+missing or the device is not an sm_100 part, calls raise ``BskError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+
+LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libbsk_sm100.so")
+
+BSK_OK = 0
+BSK_ERR_INVALID_ARG = -1
+BSK_ERR_UNSUPPORTED = -2
+BSK_ERR_CUDA = -3
+BSK_ERR_DEVICE_TIMEOUT = -4
+BSK_ERR_NO_DEVICE = -5
+
+# Every symbol include/bsk_capi.h declares, with (restype, argtypes).
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int
+_i64 = ctypes.c_int64
+_u64 = ctypes.c_uint64
+_f32 = ctypes.c_float
+SIGNATURES = {
+    "bsk_version": (_i32, []),
+    "bsk_last_error": (ctypes.c_char_p, []),
+    "bsk_device_sm_count": (_i32, []),
+    "bsk_gemm_f16f32": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "bsk_gemm_e4m3_bf16": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp]),
+    "bsk_spmm_bsr_f16f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _i32, _i32, _i32,
+                                   _i32, _i32, _vp]),
+    "bsk_bsr_validate_host": (_i32, [_vp, _vp, _i32, _i32, _i32]),
+    "bsk_bsattn_fwd_bf16": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32,
+                                   _i32, _vp]),
+    "launch_bsr_spmm_async": (None, [_vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _i32,
+                                     _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "bsk_device_error": (_i32, [ctypes.POINTER(ctypes.c_uint32)]),
+    "bsk_set_wait_timeout_ns": (_i32, [_u64]),
+    "bsk_selftest_wait_timeout": (_i32, [_u64, _vp]),
+}
+
+
+class BskError(RuntimeError):
+    def __init__(self, code: int, what: str, msg: str):
+        super().__init__(f"{what} failed with code {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib() -> ctypes.CDLL:
+    """Load libbsk_sm100.so once and attach the declared signatures."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not os.path.exists(LIB_PATH):
+                    raise ImportError(f"{LIB_PATH} is missing: build it with `python -m periodicdent42_b200.build`")
+                l = ctypes.CDLL(LIB_PATH)
+                for name, (res, args) in SIGNATURES.items():
+                    f = getattr(l, name)
+                    f.restype = res
+                    f.argtypes = args
+                _lib = l
+    return _lib
+
+
+def last_error() -> str:
+    return lib().bsk_last_error().decode(errors="replace")
+
+
+def check(rc: int, what: str) -> None:
+    if rc != BSK_OK:
+        raise BskError(rc, what, last_error())
+
+
+def _ptr(t) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+def _stream(stream) -> int:
+    if stream is None:
+        import torch
+
+        return torch.cuda.current_stream().cuda_stream
+    return int(stream) if isinstance(stream, int) else stream.cuda_stream
+
+
+def gemm_f16f32(A, Bt, C, k_begin: int = 0, k_end: int | None = None, stream=None) -> None:
+    """C[M,N] fp32 = A[M,K] fp16 @ B[K,N], B passed as Bt = B^T row-major [N,K] (column-major B)."""
+    M, K = A.shape
+    N = Bt.shape[0]
+    k_end = K if k_end is None else k_end
+    check(lib().bsk_gemm_f16f32(_ptr(A), A.stride(0), _ptr(Bt), Bt.stride(0), _ptr(C), C.stride(0), M, N, K,
+                                k_begin, k_end, _stream(stream)), "bsk_gemm_f16f32")
+
+
+def gemm_e4m3_bf16(Aq, Bqt, scale_a, scale_b, D, stream=None) -> None:
+    """D[M,N] bf16 = (Aq[M,K] @ Bq[K,N]) * scale_a * scale_b, Bq passed as Bqt [N,K] (column-major B)."""
+    M, K = Aq.shape
+    N = Bqt.shape[0]
+    check(lib().bsk_gemm_e4m3_bf16(_ptr(Aq), Aq.stride(0), _ptr(Bqt), Bqt.stride(0), _ptr(scale_a), _ptr(scale_b),
+                                   _ptr(D), D.stride(0), M, N, K, _stream(stream)), "bsk_gemm_e4m3_bf16")
+
+
+def spmm_bsr_f16f32(row_ptr, col_idx, vals, B, C, M: int, row_begin: int = 0, row_end: int | None = None,
+                    stream=None) -> None:
+    """C = A_bsr @ B for block-rows [row_begin, row_end); int32 indices, vals [nnzb, br, bc] fp16."""
+    nnzb, br, bc = vals.shape
+    Mb = row_ptr.numel() - 1
+    K, N = B.shape
+    row_end = Mb if row_end is None else row_end
+    check(lib().bsk_spmm_bsr_f16f32(_ptr(row_ptr), _ptr(col_idx), _ptr(vals), br, bc, Mb, nnzb, _ptr(B), B.stride(0),
+                                    _ptr(C), C.stride(0), M, N, K, row_begin, row_end, _stream(stream)),
+          "bsk_spmm_bsr_f16f32")
+
+
+def bsattn_fwd_bf16(Q, K, V, O, row_ptr, col_idx, scale: float, causal_diag: bool = True, bh_begin: int = 0,
+                    bh_end: int | None = None, blk: int = 128, stream=None) -> None:
+    """O = block-sparse softmax(scale * Q K^T) V over the BSR block mask (row_ptr, col_idx)."""
+    B, H, S, D = Q.shape
+    bh_end = B * H if bh_end is None else bh_end
+    check(lib().bsk_bsattn_fwd_bf16(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(row_ptr), _ptr(col_idx), B, H, S, D, blk,
+                                    float(scale), int(bool(causal_diag)), bh_begin, bh_end, _stream(stream)),
+          "bsk_bsattn_fwd_bf16")
+
+
+def device_error() -> int:
+    """Read and clear the device error word (synchronises the device)."""
+    w = ctypes.c_uint32(0)
+    check(lib().bsk_device_error(ctypes.byref(w)), "bsk_device_error")
+    return w.value
+
+
+def set_wait_timeout_ns(ns: int) -> None:
+    check(lib().bsk_set_wait_timeout_ns(int(ns)), "bsk_set_wait_timeout_ns")
+
+
+def selftest_wait_timeout(ns: int, stream=None) -> int:
+    """Returns the status code of the failure-detection probe (BSK_ERR_DEVICE_TIMEOUT is the expected one)."""
+    return lib().bsk_selftest_wait_timeout(int(ns), _stream(stream))
+
+
+def bsr_validate_host(row_ptr, col_idx, Kb: int) -> None:
+    """Validate a BSR index structure held in host (CPU, int32, contiguous) tensors."""
+    Mb = row_ptr.numel() - 1
+    nnzb = col_idx.numel()
+    check(lib().bsk_bsr_validate_host(_ptr(row_ptr), _ptr(col_idx) if nnzb else None, Mb, Kb, nnzb),
+          "bsk_bsr_validate_host")

@@ -1,0 +1,439 @@
+// Host side of the C ABI (include/bsk_capi.h): argument validation, per-device set-up, TMA tensor-map
+// encoding and kernel launches. One translation unit holds every kernel of the library so that the
+// device error word below is a single symbol.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <mutex>
+#include <string>
+
+#include "bsk_capi.h"
+#include "gemm_sm100.cuh"
+#include "bsattn_sm100.cuh"
+
+namespace {
+
+// Per-device error word written by bounded waits and device-side index checks.
+__device__ uint32_t g_bsk_err_word;
+
+thread_local std::string t_last_error;
+thread_local uint64_t t_timeout_ns = 2000000000ull;
+
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return set_error(BSK_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  std::once_flag once;
+  int status = BSK_OK;
+  std::string init_error;
+  int sm_count = 0;
+  uint32_t* err_word = nullptr;
+};
+DeviceState g_devices[kMaxDevices];
+
+std::once_flag g_encode_once;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+template <class K>
+cudaError_t allow_smem(K kernel, int bytes) {
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+void init_device(DeviceState& st, int dev) {
+  int major = 0, minor = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  if (e != cudaSuccess) {
+    st.status = BSK_ERR_NO_DEVICE;
+    st.init_error = std::string("device query failed: ") + cudaGetErrorString(e);
+    return;
+  }
+  if (major != 10 || minor != 0) {
+    st.status = BSK_ERR_UNSUPPORTED;
+    char b[128];
+    snprintf(b, sizeof(b), "device %d is sm_%d%d; this library is built for sm_100a (B200) only", dev, major,
+             minor);
+    st.init_error = b;
+    return;
+  }
+  cudaDeviceGetAttribute(&st.sm_count, cudaDevAttrMultiProcessorCount, dev);
+  using namespace bsk;
+  const cudaError_t errs[] = {
+      allow_smem(gemm_sm100_kernel<2, Mainloop::Dense, Epi::F32>, kGemmSmemBytes),
+      allow_smem(gemm_sm100_kernel<1, Mainloop::Dense, Epi::BF16Scaled>, kGemmSmemBytes),
+      allow_smem(gemm_sm100_kernel<2, Mainloop::Bsr, Epi::F32>, kGemmSmemBytes),
+      allow_smem(bsattn_sm100_kernel, kAttnSmemBytes),
+  };
+  for (cudaError_t x : errs) {
+    if (x != cudaSuccess) {
+      st.status = BSK_ERR_CUDA;
+      st.init_error = std::string("cudaFuncSetAttribute failed: ") + cudaGetErrorString(x);
+      return;
+    }
+  }
+  void* p = nullptr;
+  e = cudaGetSymbolAddress(&p, g_bsk_err_word);
+  if (e != cudaSuccess) {
+    st.status = BSK_ERR_CUDA;
+    st.init_error = std::string("cudaGetSymbolAddress(error word) failed: ") + cudaGetErrorString(e);
+    return;
+  }
+  st.err_word = static_cast<uint32_t*>(p);
+  e = cudaMemset(st.err_word, 0, sizeof(uint32_t));
+  if (e != cudaSuccess) {
+    st.status = BSK_ERR_CUDA;
+    st.init_error = std::string("clearing the error word failed: ") + cudaGetErrorString(e);
+  }
+}
+
+int device_state(DeviceState** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return set_error(BSK_ERR_NO_DEVICE, "no CUDA device: %s", cudaGetErrorString(e));
+  int count = 0;
+  e = cudaGetDeviceCount(&count);
+  if (e != cudaSuccess || count == 0) return set_error(BSK_ERR_NO_DEVICE, "no CUDA device available");
+  if (dev < 0 || dev >= kMaxDevices) return set_error(BSK_ERR_NO_DEVICE, "device ordinal %d out of range", dev);
+  DeviceState& st = g_devices[dev];
+  std::call_once(st.once, [&] { init_device(st, dev); });
+  if (st.status != BSK_OK) return set_error(st.status, "%s", st.init_error.c_str());
+  *out = &st;
+  return BSK_OK;
+}
+
+int encoder(PFN_cuTensorMapEncodeTiled_v12000* fn) {
+  std::call_once(g_encode_once, [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+  });
+  if (!g_encode) return set_error(BSK_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable from the driver");
+  *fn = g_encode;
+  return BSK_OK;
+}
+
+// Row-major 2-D (or, with `planes`, 3-D) tensor map with 128-B swizzle.
+int make_map(CUtensorMap* m, CUtensorMapDataType dt, int elem_bytes, const void* base, uint64_t inner,
+             uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer, const char* what) {
+  PFN_cuTensorMapEncodeTiled_v12000 enc;
+  if (int rc = encoder(&enc)) return rc;
+  if (reinterpret_cast<uintptr_t>(base) % 16 != 0)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: base address must be 16-byte aligned", what);
+  if (row_stride_bytes % 16 != 0)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: row stride (%llu bytes) must be a multiple of 16", what,
+                     (unsigned long long)row_stride_bytes);
+  if (inner == 0 || outer == 0) return set_error(BSK_ERR_INVALID_ARG, "%s: empty tensor map", what);
+  if (box_inner * elem_bytes > 128)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: box inner extent exceeds the 128-B swizzle span", what);
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = enc(m, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return set_error(BSK_ERR_INVALID_ARG, "%s: cuTensorMapEncodeTiled failed (%d)", what, (int)r);
+  return BSK_OK;
+}
+
+int launch_status(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  return BSK_OK;
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+int pick_group_m(int num_m_tiles) { return num_m_tiles < 16 ? num_m_tiles : 16; }
+
+}  // namespace
+
+extern "C" {
+
+int bsk_version(void) { return (0 << 16) | (1 << 8) | 0; }
+
+const char* bsk_last_error(void) { return t_last_error.c_str(); }
+
+int bsk_device_sm_count(void) {
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  return st->sm_count;
+}
+
+int bsk_set_wait_timeout_ns(uint64_t ns) {
+  if (ns < 1000ull || ns > 60000000000ull)
+    return set_error(BSK_ERR_INVALID_ARG, "wait timeout %llu ns outside [1e3, 6e10]", (unsigned long long)ns);
+  t_timeout_ns = ns;
+  return BSK_OK;
+}
+
+int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc, int M, int N,
+                    int K, int k_begin, int k_end, void* stream) {
+  using namespace bsk;
+  if (M < 0 || N < 0 || K < 0) return set_error(BSK_ERR_INVALID_ARG, "gemm_f16f32: negative extent");
+  if (k_begin < 0 || k_end > K || k_begin > k_end)
+    return set_error(BSK_ERR_INVALID_ARG, "gemm_f16f32: bad K range [%d, %d) for K=%d", k_begin, k_end, K);
+  if (k_begin % 8 != 0) return set_error(BSK_ERR_INVALID_ARG, "gemm_f16f32: k_begin must be a multiple of 8");
+  if (lda < K || ldb < K || ldc < N)
+    return set_error(BSK_ERR_INVALID_ARG, "gemm_f16f32: leading dimensions smaller than the extents");
+  if (lda % 8 || ldb % 8) return set_error(BSK_ERR_INVALID_ARG, "gemm_f16f32: lda and ldb must be multiples of 8");
+  if (!A || !B || !C) return set_error(BSK_ERR_INVALID_ARG, "gemm_f16f32: null pointer");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  if (M == 0 || N == 0) return BSK_OK;
+  const int kr = k_end - k_begin;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (kr == 0) {
+    cudaError_t e = cudaMemset2DAsync(C, ldc * sizeof(float), 0, (size_t)N * sizeof(float), M, s);
+    return e == cudaSuccess ? BSK_OK : cuda_fail(e, "gemm_f16f32: zero fill");
+  }
+  const __half* Ah = static_cast<const __half*>(A) + k_begin;
+  const __half* Bh = static_cast<const __half*>(B) + k_begin;
+  CUtensorMap ta, tb;
+  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Ah, kr, M, lda * 2, 64, kGemmBM, "A")) return rc;
+  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Bh, kr, N, ldb * 2, 64, kGemmBN, "B")) return rc;
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.num_m_tiles = (M + kGemmBM - 1) / kGemmBM;
+  a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
+  a.num_k_blocks = (kr + 63) / 64;
+  a.group_m = pick_group_m(a.num_m_tiles);
+  a.out = C;
+  a.ldo = ldc;
+  a.vec_ok = aligned16(C) && (ldc % 4 == 0);
+  a.err = st->err_word;
+  a.timeout_ns = t_timeout_ns;
+  const int tiles = a.num_m_tiles * a.num_n_tiles;
+  const int grid = tiles < st->sm_count ? tiles : st->sm_count;
+  gemm_sm100_kernel<2, Mainloop::Dense, Epi::F32><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
+  return launch_status("gemm_f16f32 launch");
+}
+
+int bsk_gemm_e4m3_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, const float* scale_a,
+                       const float* scale_b, void* D, int64_t ldd, int M, int N, int K, void* stream) {
+  using namespace bsk;
+  if (M < 0 || N < 0 || K < 0) return set_error(BSK_ERR_INVALID_ARG, "gemm_e4m3: negative extent");
+  if (lda < K || ldb < K || ldd < N)
+    return set_error(BSK_ERR_INVALID_ARG, "gemm_e4m3: leading dimensions smaller than the extents");
+  if (lda % 16 || ldb % 16) return set_error(BSK_ERR_INVALID_ARG, "gemm_e4m3: lda and ldb must be multiples of 16");
+  if (!A || !B || !D || !scale_a || !scale_b) return set_error(BSK_ERR_INVALID_ARG, "gemm_e4m3: null pointer");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  if (M == 0 || N == 0) return BSK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0) {
+    cudaError_t e = cudaMemset2DAsync(D, ldd * 2, 0, (size_t)N * 2, M, s);
+    return e == cudaSuccess ? BSK_OK : cuda_fail(e, "gemm_e4m3: zero fill");
+  }
+  CUtensorMap ta, tb;
+  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, lda, 128, kGemmBM, "A")) return rc;
+  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, ldb, 128, kGemmBN, "B")) return rc;
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.num_m_tiles = (M + kGemmBM - 1) / kGemmBM;
+  a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
+  a.num_k_blocks = (K + 127) / 128;
+  a.group_m = pick_group_m(a.num_m_tiles);
+  a.out = D;
+  a.ldo = ldd;
+  a.vec_ok = aligned16(D) && (ldd % 8 == 0);
+  a.scale_a = scale_a;
+  a.scale_b = scale_b;
+  a.err = st->err_word;
+  a.timeout_ns = t_timeout_ns;
+  const int tiles = a.num_m_tiles * a.num_n_tiles;
+  const int grid = tiles < st->sm_count ? tiles : st->sm_count;
+  gemm_sm100_kernel<1, Mainloop::Dense, Epi::BF16Scaled><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
+  return launch_status("gemm_e4m3 launch");
+}
+
+int bsk_bsr_validate_host(const int32_t* row_ptr, const int32_t* col_idx, int Mb, int Kb, int nnzb) {
+  if (Mb < 0 || Kb < 0 || nnzb < 0) return set_error(BSK_ERR_INVALID_ARG, "bsr: negative extent");
+  if (!row_ptr) return set_error(BSK_ERR_INVALID_ARG, "bsr: null row_ptr");
+  if (nnzb > 0 && !col_idx) return set_error(BSK_ERR_INVALID_ARG, "bsr: null col_idx");
+  if (row_ptr[0] != 0) return set_error(BSK_ERR_INVALID_ARG, "bsr: row_ptr[0] = %d, expected 0", row_ptr[0]);
+  for (int r = 0; r < Mb; ++r)
+    if (row_ptr[r + 1] < row_ptr[r])
+      return set_error(BSK_ERR_INVALID_ARG, "bsr: row_ptr decreases at block-row %d", r);
+  if (row_ptr[Mb] != nnzb)
+    return set_error(BSK_ERR_INVALID_ARG, "bsr: row_ptr[Mb] = %d but nnzb = %d", row_ptr[Mb], nnzb);
+  for (int j = 0; j < nnzb; ++j)
+    if (col_idx[j] < 0 || col_idx[j] >= Kb)
+      return set_error(BSK_ERR_INVALID_ARG, "bsr: col_idx[%d] = %d outside [0, %d)", j, col_idx[j], Kb);
+  return BSK_OK;
+}
+
+int bsk_spmm_bsr_f16f32(const int32_t* row_ptr, const int32_t* col_idx, const void* vals, int bs_r, int bs_c,
+                        int Mb, int nnzb, const void* B, int64_t ldb, float* C, int64_t ldc, int M, int N, int K,
+                        int row_begin, int row_end, void* stream) {
+  using namespace bsk;
+  if (bs_r != 128 || bs_c != 128)
+    return set_error(BSK_ERR_UNSUPPORTED, "spmm_bsr: block shape %dx%d unsupported (the sm_100 kernel needs 128x128)",
+                     bs_r, bs_c);
+  if (M < 0 || N < 0 || K < 0 || Mb < 0 || nnzb < 0) return set_error(BSK_ERR_INVALID_ARG, "spmm_bsr: negative extent");
+  if (M != Mb * bs_r) return set_error(BSK_ERR_INVALID_ARG, "spmm_bsr: M=%d != Mb*bs_r=%d", M, Mb * bs_r);
+  if (K % bs_c) return set_error(BSK_ERR_INVALID_ARG, "spmm_bsr: K=%d not a multiple of the block width", K);
+  if (row_begin < 0 || row_end > Mb || row_begin > row_end)
+    return set_error(BSK_ERR_INVALID_ARG, "spmm_bsr: bad block-row range [%d, %d) for Mb=%d", row_begin, row_end, Mb);
+  if (ldb < N || ldc < N) return set_error(BSK_ERR_INVALID_ARG, "spmm_bsr: leading dimensions smaller than N");
+  if (ldb % 8) return set_error(BSK_ERR_INVALID_ARG, "spmm_bsr: ldb must be a multiple of 8");
+  if (!row_ptr || !C || (N > 0 && K > 0 && !B) || (nnzb > 0 && (!col_idx || !vals)))
+    return set_error(BSK_ERR_INVALID_ARG, "spmm_bsr: null pointer");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  if (row_end == row_begin || N == 0) return BSK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0 || nnzb == 0) {
+    float* c0 = C + static_cast<int64_t>(row_begin) * bs_r * ldc;
+    cudaError_t e = cudaMemset2DAsync(c0, ldc * sizeof(float), 0, (size_t)N * sizeof(float),
+                                      (size_t)(row_end - row_begin) * bs_r, s);
+    return e == cudaSuccess ? BSK_OK : cuda_fail(e, "spmm_bsr: zero fill");
+  }
+  CUtensorMap ta, tb;
+  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, vals, 128, (uint64_t)nnzb * 128, 256, 64, 128,
+                        "A values"))
+    return rc;
+  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, N, K, ldb * 2, 64, 64, "B")) return rc;
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.num_m_tiles = row_end - row_begin;
+  a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
+  a.num_k_blocks = 0;
+  a.group_m = pick_group_m(a.num_m_tiles);
+  a.out = C;
+  a.ldo = ldc;
+  a.vec_ok = aligned16(C) && (ldc % 4 == 0);
+  a.row_ptr = row_ptr;
+  a.col_idx = col_idx;
+  a.row_begin = row_begin;
+  a.nnzb = nnzb;
+  a.kb_count = K / bs_c;
+  a.err = st->err_word;
+  a.timeout_ns = t_timeout_ns;
+  const int tiles = a.num_m_tiles * a.num_n_tiles;
+  const int grid = tiles < st->sm_count ? tiles : st->sm_count;
+  gemm_sm100_kernel<2, Mainloop::Bsr, Epi::F32><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
+  return launch_status("spmm_bsr launch");
+}
+
+void launch_bsr_spmm_async(const int* A_row_ptr, const int* A_col_idx, const void* A_vals, int A_M_blocks,
+                           int A_K_blocks, int A_nnzb, const int* B_row_ptr, const int* B_col_idx, const void* B_vals,
+                           int B_K_blocks, int B_N_blocks, int B_nnzb, float* C, int M, int N, int K, int ldc, int BM,
+                           int BN, int BK, void* stream) {
+  (void)B_row_ptr;
+  (void)B_col_idx;
+  (void)BM;
+  (void)BN;
+  (void)BK;
+  if (A_M_blocks <= 0 || A_K_blocks <= 0 || M % A_M_blocks || K % A_K_blocks) {
+    set_error(BSK_ERR_INVALID_ARG, "launch_bsr_spmm_async: M/K not divisible by the block counts");
+    return;
+  }
+  if (B_nnzb != B_K_blocks * B_N_blocks) {
+    set_error(BSK_ERR_UNSUPPORTED, "launch_bsr_spmm_async: only the dense all-blocks B pattern is supported");
+    return;
+  }
+  const int rc = bsk_spmm_bsr_f16f32(A_row_ptr, A_col_idx, A_vals, M / A_M_blocks, K / A_K_blocks, A_M_blocks,
+                                     A_nnzb, B_vals, N, C, ldc, M, N, K, 0, A_M_blocks, stream);
+  if (rc == BSK_OK) t_last_error.clear();
+}
+
+int bsk_bsattn_fwd_bf16(const void* Q, const void* K, const void* V, void* O, const int32_t* row_ptr,
+                        const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale, int causal_diag,
+                        int bh_begin, int bh_end, void* stream) {
+  using namespace bsk;
+  if (D != kAttnD) return set_error(BSK_ERR_UNSUPPORTED, "bsattn: head_dim %d unsupported (needs %d)", D, kAttnD);
+  if (blk != kAttnBlk) return set_error(BSK_ERR_UNSUPPORTED, "bsattn: block size %d unsupported (needs %d)", blk, kAttnBlk);
+  if (B < 0 || H < 0 || S < 0) return set_error(BSK_ERR_INVALID_ARG, "bsattn: negative extent");
+  if (S % blk) return set_error(BSK_ERR_INVALID_ARG, "bsattn: S=%d not a multiple of the block size %d", S, blk);
+  if (bh_begin < 0 || bh_end > B * H || bh_begin > bh_end)
+    return set_error(BSK_ERR_INVALID_ARG, "bsattn: bad (b,h) range [%d, %d)", bh_begin, bh_end);
+  if (!(scale > 0.0f) || !(scale < 1e30f)) return set_error(BSK_ERR_INVALID_ARG, "bsattn: scale must be positive and finite");
+  if (!Q || !K || !V || !O || !row_ptr || !col_idx) return set_error(BSK_ERR_INVALID_ARG, "bsattn: null pointer");
+  if (!aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O))
+    return set_error(BSK_ERR_INVALID_ARG, "bsattn: Q/K/V/O must be 16-byte aligned");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  if (bh_end == bh_begin || S == 0) return BSK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint64_t rows = (uint64_t)B * H * S;
+  CUtensorMap tq, tk, tv;
+  if (int rc = make_map(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Q, D, rows, D * 2, 64, kAttnBlk, "Q")) return rc;
+  if (int rc = make_map(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, D, rows, D * 2, 64, kAttnBlk, "K")) return rc;
+  if (int rc = make_map(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, V, D, rows, D * 2, 64, kAttnBlk, "V")) return rc;
+  AttnArgs a{};
+  a.O = static_cast<__nv_bfloat16*>(O);
+  a.row_ptr = row_ptr;
+  a.col_idx = col_idx;
+  a.S = S;
+  a.nqb = S / blk;
+  a.bh_begin = bh_begin;
+  a.num_items = (bh_end - bh_begin) * a.nqb;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.causal_diag = causal_diag;
+  a.err = st->err_word;
+  a.timeout_ns = t_timeout_ns;
+  const int grid = a.num_items < st->sm_count ? a.num_items : st->sm_count;
+  bsattn_sm100_kernel<<<grid, kAttnThreads, kAttnSmemBytes, s>>>(tq, tk, tv, a);
+  return launch_status("bsattn launch");
+}
+
+int bsk_device_error(uint32_t* out) {
+  if (!out) return set_error(BSK_ERR_INVALID_ARG, "device_error: null output");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return cuda_fail(e, "device_error: synchronize");
+  e = cudaMemcpy(out, st->err_word, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "device_error: read");
+  e = cudaMemset(st->err_word, 0, sizeof(uint32_t));
+  if (e != cudaSuccess) return cuda_fail(e, "device_error: clear");
+  return BSK_OK;
+}
+
+int bsk_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
+  if (timeout_ns < 1000ull || timeout_ns > 10000000000ull)
+    return set_error(BSK_ERR_INVALID_ARG, "selftest: timeout outside [1e3, 1e10] ns");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "selftest: pre-sync");
+  e = cudaMemsetAsync(st->err_word, 0, sizeof(uint32_t), s);
+  if (e != cudaSuccess) return cuda_fail(e, "selftest: clear");
+  bsk::wait_probe_kernel<<<1, 32, 0, s>>>(st->err_word, timeout_ns);
+  if (int rc = launch_status("selftest launch")) return rc;
+  uint32_t word = 0;
+  e = cudaMemcpyAsync(&word, st->err_word, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, "selftest: read back");
+  cudaMemsetAsync(st->err_word, 0, sizeof(uint32_t), s);
+  cudaStreamSynchronize(s);
+  if ((word & 0xFF) == bsk::kErrWaitTimeout && ((word >> 8) & 0xFF) == bsk::kKidWaitProbe)
+    return set_error(BSK_ERR_DEVICE_TIMEOUT, "bounded wait ran out after %llu ns (expected)",
+                     (unsigned long long)timeout_ns);
+  return set_error(BSK_ERR_CUDA, "selftest: the probe kernel did not report a timeout (word=0x%08x)", word);
+}
+
+}  // extern "C"

@@ -1,0 +1,352 @@
+// Persistent, warp-specialised tcgen05 GEMM for sm_100a, shared by three operators:
+//   * dense fp16 x fp16 -> fp32       (A [M,K] row-major, B given as B^T [N,K] row-major, i.e. column-major B)
+//   * dense e4m3 x e4m3 -> bf16       (same layouts, per-tensor scales applied in the epilogue)
+//   * BSR fp16 x dense fp16 -> fp32   (A = 128x128 nonzero blocks, B [K,N] row-major, gathered by column index)
+//
+// One CTA per SM; 6 warps:
+//   warp 0     TMA producer: fills a 4-stage shared-memory ring (A 128 x 128 B, B 256 x 128 B per stage)
+//   warp 1     TMEM owner + MMA issuer: tcgen05.mma 128x256xK into one of two TMEM accumulators
+//   warps 2-5  epilogue: tcgen05.ld the finished accumulator (warp w reads TMEM lanes 32*(w%4)..+31)
+//              and stores it, while the MMA warp fills the other accumulator.
+// Output tile 128 x 256, 2 x 256 fp32 TMEM columns (all 512). Each wait is bounded: a wait that runs
+// out records an error word, raises the CTA abort flag and every role drains and returns.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "ptx_sm100.cuh"
+
+namespace bsk {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBN = 256;
+constexpr int kGemmRowBytes = 128;  // K extent of one stage, in bytes (one 128-B swizzle span)
+constexpr int kGemmStages = 4;
+constexpr int kGemmThreads = 192;
+constexpr int kGemmAStage = kGemmBM * kGemmRowBytes;  // 16 KB
+constexpr int kGemmBStage = kGemmBN * kGemmRowBytes;  // 32 KB
+constexpr int kGemmTmemCols = 512;
+constexpr int kGemmSmemBytes = 1024 /*align slack*/ + kGemmStages * (kGemmAStage + kGemmBStage) + 256;
+
+enum class Mainloop : int { Dense = 0, Bsr = 1 };
+enum class Epi : int { F32 = 0, BF16Scaled = 1 };
+
+// Kernel ids recorded in the device error word.
+enum : uint32_t { kKidGemmF16 = 1, kKidGemmE4m3 = 2, kKidSpmmBsr = 3, kKidBsAttn = 4, kKidWaitProbe = 5 };
+
+struct GemmArgs {
+  int M, N;                  // output extent (rows / cols of C that exist)
+  int num_m_tiles, num_n_tiles;
+  int num_k_blocks;          // dense: stages per tile
+  int group_m;               // tile rasterisation group (M tiles per group)
+  void* out;                 // C (fp32) or D (bf16)
+  int64_t ldo;               // elements
+  int vec_ok;                // 16-byte aligned rows: vector stores allowed
+  const float* scale_a;      // e4m3 only
+  const float* scale_b;
+  const int* row_ptr;        // BSR only: block-row pointer (int32)
+  const int* col_idx;        // BSR only: block-column index per nonzero block
+  int row_begin;             // BSR only: first block-row of this launch
+  int nnzb;                  // BSR only: number of nonzero blocks (clamp for row_ptr)
+  int kb_count;              // BSR only: number of block-columns (K / 128)
+  uint32_t* err;
+  uint64_t timeout_ns;
+};
+
+__device__ __forceinline__ void gemm_tile_coords(int tile, const GemmArgs& a, int& mt, int& nt) {
+  const int per_group = a.group_m * a.num_n_tiles;
+  const int g = tile / per_group;
+  const int first_m = g * a.group_m;
+  const int gm = min(a.num_m_tiles - first_m, a.group_m);
+  const int t = tile - g * per_group;
+  mt = first_m + t % gm;
+  nt = t / gm;
+}
+
+// Nonzero-block range of block-row r, clamped to [0, nnzb] so a corrupt row_ptr can neither loop long
+// nor read outside the value array. Returns true when clamping changed nothing.
+__device__ __forceinline__ bool bsr_row_range(const GemmArgs& a, int r, int& j0, int& j1) {
+  const int p0 = __ldg(&a.row_ptr[r]);
+  const int p1 = __ldg(&a.row_ptr[r + 1]);
+  j0 = min(max(p0, 0), a.nnzb);
+  j1 = min(max(p1, j0), a.nnzb);
+  return j0 == p0 && j1 == p1;
+}
+
+__device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+  asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+template <int kElemBytes, Mainloop kML, Epi kEpi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                      const GemmArgs a) {
+  constexpr int BK = kGemmRowBytes / kElemBytes;  // elements of K per stage (64 fp16 / 128 e4m3)
+  constexpr int MMA_K = 32 / kElemBytes;          // K per tcgen05.mma (16 fp16 / 32 e4m3)
+  constexpr int K_STEPS = BK / MMA_K;             // 4
+  constexpr bool kMNB = (kML == Mainloop::Bsr);   // B operand MN-major (row-major [K,N] source)
+  constexpr uint32_t IDESC = ptx::instr_desc(kGemmBM, kGemmBN, 0, 0, 0, kMNB ? 1 : 0);
+  constexpr uint32_t STAGE_TX = kGemmAStage + kGemmBStage;
+  constexpr int BSR_STEPS = 128 / BK;             // stages per 128-wide nonzero block
+  constexpr uint32_t KID = kML == Mainloop::Bsr ? kKidSpmmBsr : (kElemBytes == 1 ? kKidGemmE4m3 : kKidGemmF16);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kGemmStages * kGemmAStage;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kGemmStages * kGemmBStage);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kGemmStages;
+  uint64_t* tfull = bars + 2 * kGemmStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kGemmStages; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&tfull[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&tempty[s]), 4);
+    }
+    ptx::mbar_init(ptx::smem_u32(drain), 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), kGemmTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  WaitCtl ctl{abort_flag, a.err, a.timeout_ns, KID};
+  const int num_tiles = a.num_m_tiles * a.num_n_tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    uint32_t stage = 0, phase = 0;
+    uint32_t issued = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      int mt, nt;
+      gemm_tile_coords(tile, a, mt, nt);
+      const int n0 = nt * kGemmBN;
+      if constexpr (kML == Mainloop::Dense) {
+        const int m0 = mt * kGemmBM;
+        for (int kb = 0; kb < a.num_k_blocks; ++kb) {
+          ok = warp_wait_bounded(ptx::smem_u32(&empty[stage]), phase ^ 1, ctl, 1);
+          if (!ok) break;
+          if (lane == 0) {
+            const uint32_t fb = ptx::smem_u32(&full[stage]);
+            ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
+            ptx::tma_load_2d(ptx::smem_u32(sA + stage * kGemmAStage), &tmA, fb, kb * BK, m0);
+            ptx::tma_load_2d(ptx::smem_u32(sB + stage * kGemmBStage), &tmB, fb, kb * BK, n0);
+          }
+          ++issued;
+          if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
+        }
+      } else {
+        const int r = a.row_begin + mt;
+        int j0, j1;
+        if (!bsr_row_range(a, r, j0, j1) && lane == 0) atomicCAS(a.err, 0u, kErrBounds | (KID << 8) | (7u << 16));
+        for (int jb = j0; jb < j1 && ok; jb += 32) {
+          // warp-level prefetch of the next 32 column indices of this block-row
+          const int cidx = (jb + lane < j1) ? __ldg(&a.col_idx[jb + lane]) : 0;
+          const int cnt = min(32, j1 - jb);
+          for (int jj = 0; jj < cnt && ok; ++jj) {
+            int kblk = __shfl_sync(0xffffffffu, cidx, jj);
+            if (kblk < 0 || kblk >= a.kb_count) {  // out-of-range column: flag it; the load reads zero fill
+              if (lane == 0) atomicCAS(a.err, 0u, kErrBounds | (KID << 8) | (8u << 16));
+              kblk = a.kb_count;
+            }
+            for (int s = 0; s < BSR_STEPS; ++s) {
+              ok = warp_wait_bounded(ptx::smem_u32(&empty[stage]), phase ^ 1, ctl, 1);
+              if (!ok) break;
+              if (lane == 0) {
+                const uint32_t fb = ptx::smem_u32(&full[stage]);
+                ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
+                // A: nonzero block (jb+jj), K slice s -> 128 rows x 128 B, K-major
+                ptx::tma_load_2d(ptx::smem_u32(sA + stage * kGemmAStage), &tmA, fb, s * BK, (jb + jj) * 128);
+                // B: rows [kblk*128 + s*BK, +BK) of B[K,N], 4 slabs of 64 columns (MN-major atoms)
+                const uint32_t bdst = ptx::smem_u32(sB + stage * kGemmBStage);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  ptx::tma_load_2d(bdst + q * (BK * 128), &tmB, fb, n0 + q * 64, kblk * 128 + s * BK);
+              }
+              ++issued;
+              if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
+            }
+          }
+        }
+      }
+    }
+    // Drain: every load this warp issued must have landed before the CTA may exit.
+    if (lane == 0) {
+      const uint32_t first = issued > kGemmStages ? issued - kGemmStages : 0;
+      for (uint32_t i = first; i < issued; ++i) {
+        WaitCtl dctl = ctl;
+        volatile int never = 0;
+        dctl.abort = &never;
+        wait_bounded(ptx::smem_u32(&full[i % kGemmStages]), (i / kGemmStages) & 1, dctl, 2);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    uint32_t stage = 0, phase = 0;
+    uint32_t acc = 0, acc_phase = 0;
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      int mt, nt;
+      gemm_tile_coords(tile, a, mt, nt);
+      int nk;
+      if constexpr (kML == Mainloop::Dense) {
+        nk = a.num_k_blocks;
+      } else {
+        int j0, j1;
+        bsr_row_range(a, a.row_begin + mt, j0, j1);
+        nk = (j1 - j0) * BSR_STEPS;
+      }
+      ok = warp_wait_bounded(ptx::smem_u32(&tempty[acc]), acc_phase ^ 1, ctl, 3);
+      if (!ok) break;
+      ptx::tc_fence_after();
+      const uint32_t d_tmem = tmem_base + acc * kGemmBN;
+      for (int kb = 0; kb < nk; ++kb) {
+        ok = warp_wait_bounded(ptx::smem_u32(&full[stage]), phase, ctl, 4);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        if (lane == 0) {
+          const uint32_t a0 = ptx::smem_u32(sA + stage * kGemmAStage);
+          const uint32_t b0 = ptx::smem_u32(sB + stage * kGemmBStage);
+#pragma unroll
+          for (int k = 0; k < K_STEPS; ++k) {
+            const uint64_t ad = ptx::smem_desc(a0 + k * 32, 16, 1024);
+            const uint64_t bd = kMNB ? ptx::smem_desc(b0 + k * (MMA_K * 128), BK * 128, 1024)
+                                     : ptx::smem_desc(b0 + k * 32, 16, 1024);
+            if constexpr (kElemBytes == 1)
+              ptx::mma_f8_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+            else
+              ptx::mma_f16_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+          }
+          ptx::mma_commit(ptx::smem_u32(&empty[stage]));
+        }
+        __syncwarp();
+        if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      if (lane == 0) ptx::mma_commit(ptx::smem_u32(&tfull[acc]));
+      __syncwarp();
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+    // Drain: all MMAs this thread issued complete before TMEM is released.
+    if (lane == 0) {
+      ptx::mma_commit(ptx::smem_u32(drain));
+      WaitCtl dctl = ctl;
+      volatile int never = 0;
+      dctl.abort = &never;
+      wait_bounded(ptx::smem_u32(drain), 0, dctl, 5);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5)
+    const int q = warp & 3;
+    uint32_t acc = 0, acc_phase = 0;
+    float scale = 1.0f;
+    if constexpr (kEpi == Epi::BF16Scaled) scale = __ldg(a.scale_a) * __ldg(a.scale_b);
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mt, nt;
+      gemm_tile_coords(tile, a, mt, nt);
+      int m0, nk = 1;
+      if constexpr (kML == Mainloop::Dense) {
+        m0 = mt * kGemmBM;
+      } else {
+        const int r = a.row_begin + mt;
+        m0 = r * kGemmBM;
+        int j0, j1;
+        bsr_row_range(a, r, j0, j1);
+        nk = j1 - j0;
+      }
+      const int n0 = nt * kGemmBN;
+      if (!warp_wait_bounded(ptx::smem_u32(&tfull[acc]), acc_phase, ctl, 6)) break;
+      ptx::tc_fence_after();
+      const int row = m0 + 32 * q + lane;
+      const bool row_ok = row < a.M;
+      const uint32_t t_row = tmem_base + acc * kGemmBN + (static_cast<uint32_t>(32 * q) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kGemmBN; c += 32) {
+        uint32_t r[32];
+        __syncwarp();
+        if (nk > 0) {
+          ptx::tmem_ld_32x32b_x32(t_row + c, r);
+          ptx::tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        const int col0 = n0 + c;
+        if (row_ok) {
+        if constexpr (kEpi == Epi::F32) {
+          float* dst = reinterpret_cast<float*>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
+          if (a.vec_ok && col0 + 32 <= a.N) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) st_global_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < a.N) dst[i] = __uint_as_float(r[i]);
+          }
+        } else {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * i]) * scale,
+                                                     __uint_as_float(r[2 * i + 1]) * scale);
+            pk[i] = *reinterpret_cast<uint32_t*>(&h);
+          }
+          if (a.vec_ok && col0 + 32 <= a.N) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+              st_global_v4(reinterpret_cast<float*>(dst + 8 * v), pk[4 * v], pk[4 * v + 1], pk[4 * v + 2],
+                           pk[4 * v + 3]);
+          } else {
+            for (int i = 0; i < 32; ++i)
+              if (col0 + i < a.N) {
+                const uint32_t w = pk[i >> 1];
+                const unsigned short hb = (i & 1) ? static_cast<unsigned short>(w >> 16)
+                                                  : static_cast<unsigned short>(w & 0xFFFF);
+                reinterpret_cast<unsigned short*>(dst)[i] = hb;
+              }
+          }
+        }
+        }  // row_ok
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&tempty[acc]));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  if (warp == 1) ptx::tmem_dealloc(tmem_base, kGemmTmemCols);
+}
+
+}  // namespace bsk

@@ -1,0 +1,72 @@
+"""Dense fp16 -> fp32 GEMM through the C ABI vs the reference's torch path and an fp64 recompute.
+Tolerance: normwise relative error <= 1e-3 against fp64 (operator family's fp16/bf16 bar)."""
+import pytest
+import torch
+
+from oracle import reference_path as ref
+from periodicdent42_b200 import _capi
+from periodicdent42_b200 import workloads as wl
+
+pytestmark = pytest.mark.gpu
+TOL = 1e-3
+
+
+def _run(A, Bt, k_begin=0, k_end=None):
+    dev = torch.device("cuda", 0)
+    Ad, Btd = A.to(dev), Bt.to(dev)
+    C = torch.full((A.shape[0], Bt.shape[0]), float("nan"), device=dev)
+    _capi.gemm_f16f32(Ad, Btd, C, k_begin, k_end)
+    torch.cuda.synchronize()
+    return C.cpu()
+
+
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 128), (384, 768, 1024), (200, 136, 72), (1, 8, 8),
+                                   (130, 260, 136), (1000, 520, 264)])
+def test_gemm_shapes(no_device_error, M, N, K):
+    g = torch.Generator().manual_seed(M * 7 + N * 3 + K)
+    A = (torch.rand(M, K, generator=g) * 2 - 1).half()
+    Bt = (torch.rand(N, K, generator=g) * 2 - 1).half()
+    C = _run(A, Bt)
+    assert torch.isfinite(C).all()
+    err = ref.normwise_rel_err(C, ref.dense_fp64(A, Bt))
+    assert err <= TOL, err
+    ok, m = ref.validate_correctness(C, ref.dense_ref(A, Bt), rtol=1e-4, atol=1e-4)
+    assert ok, m
+
+
+def test_gemm_config1_1024(no_device_error):
+    A, Bt = wl.dense_inputs(wl.DENSE_SMALL, "cpu")
+    C = _run(A, Bt)
+    err = ref.normwise_rel_err(C, ref.dense_fp64(A, Bt))
+    assert err <= TOL, err
+    ok, m = ref.validate_correctness(C, ref.dense_ref(A, Bt), rtol=1e-4, atol=1e-3)
+    assert ok, m
+
+
+def test_gemm_split_k_range(no_device_error):
+    g = torch.Generator().manual_seed(5)
+    A = torch.randn(256, 1024, generator=g).half()
+    Bt = torch.randn(512, 1024, generator=g).half()
+    parts = [_run(A, Bt, a, b) for a, b in [(0, 384), (384, 1000), (1000, 1024)]]
+    C = sum(parts)
+    err = ref.normwise_rel_err(C, ref.dense_fp64(A, Bt))
+    assert err <= TOL, err
+    # one shard alone equals the product over its K range
+    err0 = ref.normwise_rel_err(parts[1], ref.dense_fp64(A[:, 384:1000], Bt[:, 384:1000]))
+    assert err0 <= TOL, err0
+
+
+def test_gemm_deterministic(no_device_error):
+    g = torch.Generator().manual_seed(9)
+    A = torch.randn(512, 2048, generator=g).half()
+    Bt = torch.randn(1024, 2048, generator=g).half()
+    assert torch.equal(_run(A, Bt), _run(A, Bt))
+
+
+def test_gemm_rejects_bad_args(cuda_dev):
+    A = torch.zeros(128, 100, dtype=torch.float16, device=cuda_dev)  # lda 100 not a multiple of 8
+    Bt = torch.zeros(128, 100, dtype=torch.float16, device=cuda_dev)
+    C = torch.zeros(128, 128, device=cuda_dev)
+    with pytest.raises(_capi.BskError) as e:
+        _capi.gemm_f16f32(A, Bt, C)
+    assert e.value.code == _capi.BSK_ERR_INVALID_ARG
