@@ -1,0 +1,479 @@
+#!/usr/bin/env python
+"""Benchmark of the BlackwellSparseK operator family on B200.
+
+Headline (the JSON line's metric/value): dense fp16 x fp16 -> fp32 GEMM, M = N = 8192, K = 237568,
+A row-major, B column-major, entries N(0,1)/K^(1/4) from seed 1, TFLOPS for the whole job.
+The line also carries the other three operators at their workloads under "ops":
+  fp8   e4m3 GEMM 8192 x 8192 x 16384, per-tensor scales, bf16 out
+  bsr   BSR SpMM 8192^3, 128x128 blocks, 16 nonzero blocks per block-row (nonzero-block FLOPs)
+  attn  block-sparse attention fwd B=2, H=32, S=16384, D=128, sliding window 4 + 8 random blocks
+Multi-GPU (torchrun, one rank per GPU, NCCL): total work is fixed ("scaling": "strong"):
+  dense / fp8 sharded by N (no communication), bsr by balanced block-row nnz, attn by (b,h) pairs.
+  ``--dense-mode splitk`` shards the dense GEMM by K and reduces with reduce_scatter instead.
+The reference arm (``--impl reference``) times the reference's CPU torch path on the host cores.
+
+Timing: W warm-up steps, then K steps between a barrier + synchronize on both sides, CUDA events on the
+launching stream, max over ranks. Inputs (7.8 GB for the headline) are far larger than L2.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import torch
+import torch.distributed as dist
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+from periodicdent42_b200 import _capi  # noqa: E402
+from periodicdent42_b200 import sharding  # noqa: E402
+from periodicdent42_b200 import workloads as wl  # noqa: E402
+
+METRIC = "fp16/fp8 GEMM & BSR TFLOPS per B200, % tensor peak, 1-8 GPU scaling"
+UNIT = "TFLOPS"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ----------------------------------------------------------------------------------------- plumbing
+def parse_args():
+    p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=30)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--ops", default="dense,fp8,bsr,attn", help="comma list; dense is the headline")
+    p.add_argument("--dense-mode", choices=["nshard", "splitk"], default="nshard")
+    p.add_argument("--shape", default=None, help="M,N,K override of the dense GEMM (profiling a small case)")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--no-e2e", action="store_true")
+    p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--op-steps", type=int, default=20, help="timed steps of the fp8 / bsr / attn measurements")
+    p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
+    return p.parse_args()
+
+
+class Ctx:
+    def __init__(self):
+        self.world = int(os.environ.get("WORLD_SIZE", "1"))
+        self.rank = int(os.environ.get("RANK", "0"))
+        self.local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+        self.dev = None
+        self.stream = None
+
+    def init_gpu(self):
+        torch.cuda.set_device(self.local_rank)
+        self.dev = torch.device("cuda", self.local_rank)
+        if self.world > 1:
+            from datetime import timedelta
+
+            dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=self.dev)
+        self.stream = torch.cuda.current_stream()
+
+    def barrier(self):
+        if self.world > 1:
+            dist.barrier(device_ids=[self.local_rank])
+
+    def max(self, x: float) -> float:
+        if self.world == 1:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=self.dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.world > 1 and dist.is_initialized():
+            dist.destroy_process_group()
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {k: float(d[k]) for k in ("hbm_gbs", "bf16_tflops", "bf16_tflops_sustained")}, "measured"
+    except (OSError, KeyError, ValueError):
+        return dict(FALLBACK_PEAKS), "fallback"
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of each kernel from the committed ncu summaries (profiles/traffic.json)."""
+    try:
+        with open(os.path.join(REPO, "profiles", "traffic.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+class Clocks:
+    """nvidia-smi sampler (100 ms) running across the run; each timed region records its host-time window and
+    the summary is taken over the samples inside the headline window (falling back to all samples under
+    load when the window holds fewer than 3)."""
+    QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.idx = set(gpu_indices)
+        self.proc = None
+        self.windows = {}
+        self.path = os.path.join("/tmp", f"bsk_clocks_{os.getpid()}.csv")
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                          "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def mark(self, name, t0, t1):
+        self.windows[name] = (t0, t1)
+
+    @staticmethod
+    def _f(x):
+        try:
+            return float(x)
+        except ValueError:
+            return float("nan")
+
+    def _rows(self):
+        import datetime as _dt
+
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                p = [x.strip() for x in line.split(",")]
+                if len(p) < 10:
+                    continue
+                try:
+                    if int(p[1]) not in self.idx:
+                        continue
+                    ts = _dt.datetime.strptime(p[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    continue
+                rows.append((ts, p))
+        return rows
+
+    def summary(self, rows):
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for _, r in rows:
+            for n, v in zip(names, r[6:10]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        sm = [self._f(r[2]) for _, r in rows]
+        return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm), "sm_max_mhz": max(self._f(r[3]) for _, r in rows),
+                "power_w_max": max(self._f(r[4]) for _, r in rows), "samples": len(rows), "reasons": sorted(reasons)}
+
+    def stop(self, headline="dense"):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = self._rows()
+        os.unlink(self.path)
+        if not rows:
+            return None
+        out = {}
+        for name, (t0, t1) in self.windows.items():
+            win = [x for x in rows if t0 <= x[0] <= t1]
+            if win:
+                out[name] = self.summary(win)
+        head = out.get(headline)
+        if head is None or head["samples"] < 3:
+            load = [x for x in rows if self._f(x[1][4]) > 200.0] or rows
+            head = dict(self.summary(load), window="all samples under load")
+        else:
+            head = dict(head, window=f"{headline} timed region")
+        head["per_region"] = out
+        return head
+
+
+CLOCKS = None
+
+
+def time_region(ctx: Ctx, fn, steps: int, warmup: int, name: str = ""):
+    """Warm-up, then `steps` calls between barrier+synchronize; returns (max-over-ranks ms per step)."""
+    for _ in range(warmup):
+        fn()
+    ctx.barrier()
+    torch.cuda.synchronize()
+    t0 = time.time()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record(ctx.stream)
+    for _ in range(steps):
+        fn()
+    e.record(ctx.stream)
+    torch.cuda.synchronize()
+    if CLOCKS is not None and name:
+        CLOCKS.mark(name, t0, time.time())
+    ctx.barrier()
+    return ctx.max(s.elapsed_time(e) / steps)
+
+
+# ----------------------------------------------------------------------------------------- dense GEMM
+def dense_cfg(args) -> wl.DenseCfg:
+    if args.shape:
+        M, N, K = (int(x) for x in args.shape.split(","))
+        return wl.DenseCfg(M, N, K, 1, "scaled_normal")
+    return wl.DENSE_BIG
+
+
+def bench_dense(ctx: Ctx, args, res: dict):
+    cfg = dense_cfg(args)
+    A, Bt = wl.dense_inputs(cfg, ctx.dev)
+    if args.dense_mode == "nshard":
+        n0, n1 = sharding.dense_nshard(cfg.N, ctx.world, ctx.rank)
+        Bt_r = Bt[n0:n1]
+        C_r = torch.empty(cfg.M, n1 - n0, device=ctx.dev)
+
+        def step():
+            _capi.gemm_f16f32(A, Bt_r, C_r, stream=ctx.stream)
+        launches = 1
+        comm = None
+    else:
+        k0, k1 = sharding.dense_ksplit(cfg.K, ctx.world, ctx.rank)
+        Cp = torch.empty(cfg.M, cfg.N, device=ctx.dev)
+        out = torch.empty(cfg.M // ctx.world, cfg.N, device=ctx.dev)
+
+        def step():
+            _capi.gemm_f16f32(A, Bt, Cp, k0, k1, stream=ctx.stream)
+            if ctx.world > 1:
+                dist.reduce_scatter_tensor(out, Cp)
+        launches = 1
+        comm = "reduce_scatter (NCCL)"
+    ms = time_region(ctx, step, args.steps, args.warmup, "dense")
+    total_flops = cfg.flops
+    tflops = total_flops / (ms * 1e-3) / 1e12
+    res["dense"] = {"ms": ms, "tflops": tflops, "flops": total_flops, "launches_per_step": launches,
+                    "mode": args.dense_mode, "comm": comm,
+                    "per_rank_flops": total_flops / ctx.world}
+    # e2e through the public API: host (pinned) inputs -> device, GEMM, result -> host, every step
+    if not args.no_e2e and args.dense_mode == "nshard":
+        import periodicdent42_b200 as bsk
+
+        A_h = torch.empty(A.shape, dtype=A.dtype, pin_memory=True)
+        A_h.copy_(A)
+        Bt_h = torch.empty(Bt_r.shape, dtype=Bt.dtype, pin_memory=True)
+        Bt_h.copy_(Bt_r)
+        C_h = torch.empty(cfg.M, Bt_r.shape[0], dtype=torch.float32, pin_memory=True)
+        A_d = torch.empty_like(A)
+        Bt_d = torch.empty_like(Bt_r)
+        del A, Bt, Bt_r
+
+        def e2e_step():
+            A_d.copy_(A_h, non_blocking=True)
+            Bt_d.copy_(Bt_h, non_blocking=True)
+            C = bsk.gemm(A_d, Bt_d.t())
+            C_h.copy_(C, non_blocking=True)
+        ms_e2e = time_region(ctx, e2e_step, args.e2e_steps, 1, "dense_e2e")
+        res["dense"]["e2e"] = {"value": total_flops / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
+                               "h2d_bytes_per_step": A_h.numel() * 2 + Bt_h.numel() * 2,
+                               "d2h_bytes_per_step": C_h.numel() * 4, "ms_per_step": ms_e2e,
+                               "steps": args.e2e_steps}
+        del A_d, Bt_d, A_h, Bt_h, C_h
+    torch.cuda.empty_cache()
+
+
+# ----------------------------------------------------------------------------------------- FP8 GEMM
+def bench_fp8(ctx: Ctx, args, res: dict):
+    cfg = wl.FP8
+    Aq, Bqt, sa, sb = wl.fp8_inputs(cfg, ctx.dev)
+    n0, n1 = sharding.dense_nshard(cfg.N, ctx.world, ctx.rank)
+    Bq_r = Bqt[n0:n1]
+    D = torch.empty(cfg.M, n1 - n0, dtype=torch.bfloat16, device=ctx.dev)
+
+    def step():
+        _capi.gemm_e4m3_bf16(Aq, Bq_r, sa, sb, D, stream=ctx.stream)
+    # 0.5 GB inputs: flush L2 between steps by rotating through 4 input copies is not needed at
+    # 268 MB per operand (> 126 MB L2); each step re-reads both operands from HBM.
+    ms = time_region(ctx, step, args.op_steps, args.warmup, "fp8")
+    res["fp8"] = {"ms": ms, "tflops": cfg.flops / (ms * 1e-3) / 1e12, "flops": cfg.flops, "launches_per_step": 1}
+    del Aq, Bqt, D
+    torch.cuda.empty_cache()
+
+
+# ----------------------------------------------------------------------------------------- BSR SpMM
+def bench_bsr(ctx: Ctx, args, res: dict):
+    cfg = wl.BSR
+    crow, col, vals, B = wl.bsr_inputs(cfg, ctx.dev)
+    Mb = cfg.M // cfg.block
+    r0, r1 = sharding.bsr_block_rows(crow.cpu(), ctx.world, ctx.rank)
+    rp32 = crow.to(torch.int32)
+    ci32 = col.to(torch.int32)
+    C = torch.empty(cfg.M, cfg.N, device=ctx.dev)
+
+    def step():
+        _capi.spmm_bsr_f16f32(rp32, ci32, vals, B, C, cfg.M, r0, r1, stream=ctx.stream)
+    ms = time_region(ctx, step, args.op_steps, args.warmup, "bsr")
+    res["bsr"] = {"ms": ms, "tflops": cfg.flops / (ms * 1e-3) / 1e12, "flops": cfg.flops, "launches_per_step": 1,
+                  "nnzb": int(crow[-1].item()), "block_rows": [r0, r1], "Mb": Mb}
+    del crow, col, vals, B, C
+    torch.cuda.empty_cache()
+
+
+# ----------------------------------------------------------------------------------------- attention
+def bench_attn(ctx: Ctx, args, res: dict):
+    cfg = wl.ATTN
+    q, k, v = wl.attn_inputs(cfg, ctx.dev)
+    rp, ci = wl.attn_mask_bsr(cfg)
+    nqb = cfg.S // cfg.block
+    P = cfg.B * cfg.H
+    b0, b1 = sharding.attn_pairs(rp, nqb, P, ctx.world, ctx.rank)
+    rp32 = rp.to(torch.int32).to(ctx.dev)
+    ci32 = ci.to(torch.int32).to(ctx.dev)
+    O = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(cfg.D)
+
+    def step():
+        _capi.bsattn_fwd_bf16(q, k, v, O, rp32, ci32, scale, True, b0, b1, stream=ctx.stream)
+    ms = time_region(ctx, step, args.op_steps, args.warmup, "attn")
+    flops = wl.attn_flops(rp, cfg.block, cfg.D)
+    res["attn"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "flops": flops, "launches_per_step": 1,
+                   "nnz_blocks": int(rp[-1].item()), "pairs": [b0, b1]}
+    del q, k, v, O
+    torch.cuda.empty_cache()
+
+
+# ----------------------------------------------------------------------------------------- CPU baseline
+def cpu_dense_sample(cfg: wl.DenseCfg, k_slice: int, seconds: float, threads: int | None = None):
+    """The reference's CPU torch path (oracle: torch.matmul on fp32-upcast operands) on a K slice of the
+    headline shape; repeats until `seconds` of CPU work. Returns (TFLOPS, reps, cores)."""
+    from oracle import reference_path as ref
+
+    torch.set_num_threads(threads or os.cpu_count() or 1)
+    A, Bt = wl.dense_inputs(wl.DenseCfg(cfg.M, cfg.N, cfg.K, cfg.seed, cfg.dist), "cpu", k_slice=k_slice)
+    flops = 2.0 * cfg.M * cfg.N * k_slice
+    ref.dense_ref(A[:256], Bt[:256])  # warm the BLAS threads
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        ref.dense_ref(A, Bt)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or reps >= 50:
+            break
+    return flops * reps / el / 1e12, reps, torch.get_num_threads()
+
+
+def run_reference(args):
+    """--impl reference: the reference's CPU torch path, rank 0 only, bounded sample per step."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    from oracle import reference_path as ref
+
+    cfg = dense_cfg(args)
+    k_slice = min(4096, cfg.K)
+    torch.set_num_threads(os.cpu_count() or 1)
+    A, Bt = wl.dense_inputs(cfg, "cpu", k_slice=k_slice)
+    flops = 2.0 * cfg.M * cfg.N * k_slice
+    for _ in range(args.warmup):
+        ref.dense_ref(A, Bt)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        ref.dense_ref(A, Bt)
+    el = (time.perf_counter() - t0) / args.steps
+    tf = flops / el / 1e12
+    sample = f"{cfg.M}x{cfg.N}x{k_slice} K-slice of the {cfg.M}x{cfg.N}x{cfg.K} GEMM, torch.matmul on fp32-upcast operands"
+    line = {"metric": METRIC, "value": tf, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": el * 1e3, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"dense fp16->fp32 GEMM M={cfg.M} N={cfg.N} K={cfg.K} (CPU sample K={k_slice})",
+                       "parallelism": "host cores"},
+            "cpu_baseline": {"value": tf, "unit": UNIT, "cores": torch.get_num_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": tf, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------------------- main
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        return run_reference(args)
+    if not torch.cuda.is_available():
+        print(json.dumps({"metric": METRIC, "error": "no CUDA device"}))
+        return 1
+    ctx = Ctx()
+    ctx.init_gpu()
+    _capi.lib()
+    peaks, peak_src = load_peaks()
+    ops = [o.strip() for o in args.ops.split(",") if o.strip()]
+    res = {}
+    global CLOCKS
+    clocks = Clocks(range(ctx.world)) if ctx.rank == 0 else None
+    CLOCKS = clocks
+    if clocks:
+        clocks.start()
+    try:
+        for op in ops:
+            {"dense": bench_dense, "fp8": bench_fp8, "bsr": bench_bsr, "attn": bench_attn}[op](ctx, args, res)
+    finally:
+        clk = clocks.stop() if clocks else None
+    err_word = _capi.device_error()
+    cpu = None
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline and "dense" in res:
+        tf, reps, cores = cpu_dense_sample(dense_cfg(args), min(4096, dense_cfg(args).K), args.cpu_seconds)
+        cpu = {"value": tf, "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": f"{reps} x torch.matmul(fp32) on the 8192x8192x4096 K-slice of the headline shape"}
+    if ctx.rank == 0:
+        d = res.get("dense")
+        traffic = load_traffic()
+        peak_t = peaks["bf16_tflops_sustained"]
+        line = {"metric": METRIC, "value": d["tflops"] if d else None, "unit": UNIT, "n_gpus": ctx.world,
+                "steps": args.steps, "warmup": args.warmup, "ms_per_step": d["ms"] if d else None,
+                "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+                "data": "synthetic (seeded device RNG, BASELINE shapes and distributions)",
+                "config": {"workload": "dense fp16->fp32 GEMM M=8192 N=8192 K=237568 (A row-major, B col-major)"
+                           if not args.shape else f"dense fp16->fp32 GEMM {args.shape} (profiling case)",
+                           "parallelism": f"{args.dense_mode} x{ctx.world}",
+                           "l2": "inputs larger than L2 (7.8 GB per step)"}}
+        if d:
+            kern = traffic.get("gemm_f16f32")
+            per_launch_flops = d["per_rank_flops"]
+            line["roofline"] = {"bound": "tensor", "achieved": per_launch_flops / (d["ms"] * 1e-3) / 1e12,
+                                "peak": peak_t, "unit": "TFLOP/s",
+                                "frac": per_launch_flops / (d["ms"] * 1e-3) / 1e12 / peak_t,
+                                "peak_kind": f"{peak_src} bf16 sustained (cuBLAS, power-capped loop)",
+                                "peak_burst": peaks["bf16_tflops"],
+                                "traffic": (kern["read_bytes_per_unit_k"] * dense_cfg(args).K + kern["write_bytes_per_launch"]
+                                            if kern and ctx.world == 1 else None),
+                                "traffic_source": kern["source"] if kern and ctx.world == 1 else None,
+                                "algorithmic_bytes": (dense_cfg(args).M + dense_cfg(args).N // ctx.world)
+                                * dense_cfg(args).K * 2 + dense_cfg(args).M * dense_cfg(args).N // ctx.world * 4}
+            line["e2e"] = d.get("e2e")
+            line["gpu_launches"] = args.steps * d["launches_per_step"]
+        line["cpu_baseline"] = cpu
+        line["clocks"] = clk
+        opsum = {}
+        for name in ("fp8", "bsr", "attn"):
+            if name in res:
+                r = res[name]
+                pk = peak_t * (2 if name == "fp8" else 1)
+                opsum[name] = {"tflops": r["tflops"], "ms": r["ms"],
+                               "frac_of_peak": r["tflops"] / ctx.world / pk,
+                               "peak": pk, "peak_basis": ("2 x " if name == "fp8" else "") + "measured bf16 sustained"}
+                for kk in ("nnzb", "nnz_blocks"):
+                    if kk in r:
+                        opsum[name][kk] = r[kk]
+        line["ops"] = opsum
+        line["device_error_word"] = err_word
+        print(json.dumps(line), flush=True)
+    ctx.close()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
