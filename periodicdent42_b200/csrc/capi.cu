@@ -7,12 +7,14 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <string>
 
 #include "bsk_capi.h"
 #include "gemm_sm100.cuh"
+#include "gemm_pair_sm100.cuh"
 #include "bsattn_sm100.cuh"
 
 namespace {
@@ -44,6 +46,8 @@ struct DeviceState {
   int status = BSK_OK;
   std::string init_error;
   int sm_count = 0;
+  int pair_clusters_f16 = 0;   // co-resident 2-CTA clusters of the pair GEMM kernels
+  int pair_clusters_e4m3 = 0;
   uint32_t* err_word = nullptr;
 };
 DeviceState g_devices[kMaxDevices];
@@ -54,6 +58,34 @@ PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 template <class K>
 cudaError_t allow_smem(K kernel, int bytes) {
   return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+// How many 2-CTA clusters of `kernel` can be resident at once (persistent grids are sized to this).
+template <class K>
+int max_clusters(K kernel, int threads, int smem) {
+  cudaLaunchConfig_t cfg = {};
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(kernel), &cfg) != cudaSuccess) return -1;
+  return n;
+}
+
+// Tile policy of the dense GEMMs: CTA-pair 256 x 256 tiles unless M fits one 128-row tile;
+// BSK_GEMM_TILE=pair|single overrides (diagnostics).
+bool use_pair_tiles(int M) {
+  const char* v = getenv("BSK_GEMM_TILE");
+  if (v && strcmp(v, "single") == 0) return false;
+  if (v && strcmp(v, "pair") == 0) return true;
+  return M > 128;
 }
 
 void init_device(DeviceState& st, int dev) {
@@ -80,6 +112,8 @@ void init_device(DeviceState& st, int dev) {
       allow_smem(gemm_sm100_kernel<1, Mainloop::Dense, Epi::BF16Scaled>, kGemmSmemBytes),
       allow_smem(gemm_sm100_kernel<2, Mainloop::Bsr, Epi::F32>, kGemmSmemBytes),
       allow_smem(bsattn_sm100_kernel, kAttnSmemBytes),
+      allow_smem(gemm_pair_sm100_kernel<2, Epi::F32>, kPairSmemBytes),
+      allow_smem(gemm_pair_sm100_kernel<1, Epi::BF16Scaled>, kPairSmemBytes),
   };
   for (cudaError_t x : errs) {
     if (x != cudaSuccess) {
@@ -87,6 +121,13 @@ void init_device(DeviceState& st, int dev) {
       st.init_error = std::string("cudaFuncSetAttribute failed: ") + cudaGetErrorString(x);
       return;
     }
+  }
+  st.pair_clusters_f16 = max_clusters(gemm_pair_sm100_kernel<2, Epi::F32>, kPairThreads, kPairSmemBytes);
+  st.pair_clusters_e4m3 = max_clusters(gemm_pair_sm100_kernel<1, Epi::BF16Scaled>, kPairThreads, kPairSmemBytes);
+  if (st.pair_clusters_f16 <= 0 || st.pair_clusters_e4m3 <= 0) {
+    st.status = BSK_ERR_CUDA;
+    st.init_error = "cudaOccupancyMaxActiveClusters reports no co-resident CTA pair";
+    return;
   }
   void* p = nullptr;
   e = cudaGetSymbolAddress(&p, g_bsk_err_word);
@@ -162,7 +203,11 @@ int launch_status(const char* what) {
 
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-int pick_group_m(int num_m_tiles) { return num_m_tiles < 16 ? num_m_tiles : 16; }
+// M tiles per rasterisation group: concurrent tiles then span ~2048 rows of A and a few B column panels.
+int pick_group_m(int num_m_tiles, bool pair = false) {
+  const int g = pair ? 8 : 16;
+  return num_m_tiles < g ? num_m_tiles : g;
+}
 
 }  // namespace
 
@@ -207,24 +252,32 @@ int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, floa
   }
   const __half* Ah = static_cast<const __half*>(A) + k_begin;
   const __half* Bh = static_cast<const __half*>(B) + k_begin;
+  const bool pair = use_pair_tiles(M);
+  const uint32_t a_rows = pair ? 128 : kGemmBM;  // rows per CTA of the A tile
+  const uint32_t b_rows = pair ? 128 : kGemmBN;  // rows of B^T per CTA
   CUtensorMap ta, tb;
-  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Ah, kr, M, lda * 2, 64, kGemmBM, "A")) return rc;
-  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Bh, kr, N, ldb * 2, 64, kGemmBN, "B")) return rc;
+  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Ah, kr, M, lda * 2, 64, a_rows, "A")) return rc;
+  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Bh, kr, N, ldb * 2, 64, b_rows, "B")) return rc;
   GemmArgs a{};
   a.M = M;
   a.N = N;
-  a.num_m_tiles = (M + kGemmBM - 1) / kGemmBM;
+  a.num_m_tiles = (M + (pair ? kPairBM : kGemmBM) - 1) / (pair ? kPairBM : kGemmBM);
   a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
   a.num_k_blocks = (kr + 63) / 64;
-  a.group_m = pick_group_m(a.num_m_tiles);
+  a.group_m = pick_group_m(a.num_m_tiles, pair);
   a.out = C;
   a.ldo = ldc;
   a.vec_ok = aligned16(C) && (ldc % 4 == 0);
   a.err = st->err_word;
   a.timeout_ns = t_timeout_ns;
   const int tiles = a.num_m_tiles * a.num_n_tiles;
-  const int grid = tiles < st->sm_count ? tiles : st->sm_count;
-  gemm_sm100_kernel<2, Mainloop::Dense, Epi::F32><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
+  if (pair) {
+    const int clusters = tiles < st->pair_clusters_f16 ? tiles : st->pair_clusters_f16;
+    gemm_pair_sm100_kernel<2, Epi::F32><<<2 * clusters, kPairThreads, kPairSmemBytes, s>>>(ta, tb, a);
+  } else {
+    const int grid = tiles < st->sm_count ? tiles : st->sm_count;
+    gemm_sm100_kernel<2, Mainloop::Dense, Epi::F32><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
+  }
   return launch_status("gemm_f16f32 launch");
 }
 
@@ -244,16 +297,17 @@ int bsk_gemm_e4m3_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, c
     cudaError_t e = cudaMemset2DAsync(D, ldd * 2, 0, (size_t)N * 2, M, s);
     return e == cudaSuccess ? BSK_OK : cuda_fail(e, "gemm_e4m3: zero fill");
   }
+  const bool pair = use_pair_tiles(M);
   CUtensorMap ta, tb;
-  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, lda, 128, kGemmBM, "A")) return rc;
-  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, ldb, 128, kGemmBN, "B")) return rc;
+  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, lda, 128, pair ? 128 : kGemmBM, "A")) return rc;
+  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, ldb, 128, pair ? 128 : kGemmBN, "B")) return rc;
   GemmArgs a{};
   a.M = M;
   a.N = N;
-  a.num_m_tiles = (M + kGemmBM - 1) / kGemmBM;
+  a.num_m_tiles = (M + (pair ? kPairBM : kGemmBM) - 1) / (pair ? kPairBM : kGemmBM);
   a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
   a.num_k_blocks = (K + 127) / 128;
-  a.group_m = pick_group_m(a.num_m_tiles);
+  a.group_m = pick_group_m(a.num_m_tiles, pair);
   a.out = D;
   a.ldo = ldd;
   a.vec_ok = aligned16(D) && (ldd % 8 == 0);
@@ -262,8 +316,13 @@ int bsk_gemm_e4m3_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, c
   a.err = st->err_word;
   a.timeout_ns = t_timeout_ns;
   const int tiles = a.num_m_tiles * a.num_n_tiles;
-  const int grid = tiles < st->sm_count ? tiles : st->sm_count;
-  gemm_sm100_kernel<1, Mainloop::Dense, Epi::BF16Scaled><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
+  if (pair) {
+    const int clusters = tiles < st->pair_clusters_e4m3 ? tiles : st->pair_clusters_e4m3;
+    gemm_pair_sm100_kernel<1, Epi::BF16Scaled><<<2 * clusters, kPairThreads, kPairSmemBytes, s>>>(ta, tb, a);
+  } else {
+    const int grid = tiles < st->sm_count ? tiles : st->sm_count;
+    gemm_sm100_kernel<1, Mainloop::Dense, Epi::BF16Scaled><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
+  }
   return launch_status("gemm_e4m3 launch");
 }
 

@@ -1,0 +1,245 @@
+// CTA-pair (cta_group::2) tcgen05 GEMM for the dense fp16 -> fp32 and e4m3 -> bf16 operators.
+//
+// A cluster of two CTAs on two SMs computes one 256 x 256 output tile per step of its persistent loop:
+//   * each CTA's producer warp loads ITS half of A (128 rows) and ITS half of B^T (128 rows) into its own
+//     shared memory (6-stage ring, 32 KB per stage), completing on the even (leader) CTA's "full" barrier;
+//   * one thread of the leader issues tcgen05.mma.cta_group::2 256x256xK, which reads A and B from both
+//     CTAs' shared memory at the same offsets and accumulates rows 0-127 in the leader's TMEM and rows
+//     128-255 in the peer's (2 x 256 fp32 columns each, double-buffered);
+//   * stage releases and "accumulator ready" are committed to both CTAs' barriers (two plain commits,
+//     own address and the peer's mapa address); each CTA's 4 epilogue warps drain their own TMEM and arrive
+//     on the leader's "accumulator free" barrier.
+// Per SM and K step this moves 32 KB through shared memory instead of the 48 KB of a 1-CTA 128 x 256 tile.
+#pragma once
+
+#include "gemm_sm100.cuh"
+
+namespace bsk {
+
+constexpr int kPairBM = 256;
+constexpr int kPairBN = 256;
+constexpr int kPairStages = 6;
+constexpr int kPairStageA = 128 * 128;  // 128 rows x 128 B per CTA
+constexpr int kPairStageB = 128 * 128;
+constexpr int kPairThreads = 192;
+constexpr int kPairTmemCols = 512;
+constexpr int kPairSmemBytes = 1024 + kPairStages * (kPairStageA + kPairStageB) + 256;
+
+template <int kElemBytes, Epi kEpi>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
+    gemm_pair_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                           const GemmArgs a) {
+  constexpr int BK = kGemmRowBytes / kElemBytes;
+  constexpr int MMA_K = 32 / kElemBytes;
+  constexpr int K_STEPS = BK / MMA_K;
+  constexpr uint32_t IDESC = ptx::instr_desc(kPairBM, kPairBN, 0, 0, 0, 0);
+  constexpr uint32_t PAIR_TX = 2 * (kPairStageA + kPairStageB);
+  constexpr uint32_t KID = kElemBytes == 1 ? kKidGemmE4m3 : kKidGemmF16;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + kPairStages * kPairStageA;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + kPairStages * kPairStageB);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + kPairStages;
+  uint64_t* tfull = bars + 2 * kPairStages;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = ptx::cluster_ctarank();  // 0: leader (issues the MMAs)
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&tfull[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&tempty[s]), 8);  // 4 epilogue warps x 2 CTAs
+    }
+    ptx::mbar_init(ptx::smem_u32(drain), 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmA);
+    ptx::prefetch_tmap(&tmB);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc_pair(ptx::smem_u32(tmem_holder), kPairTmemCols);
+    ptx::tmem_relinquish_pair();
+  }
+  ptx::tc_fence_before();
+  ptx::cluster_sync();  // barriers of both CTAs initialised, TMEM of both allocated
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+
+  WaitCtl ctl{abort_flag, a.err, a.timeout_ns, KID};
+  const int num_tiles = a.num_m_tiles * a.num_n_tiles;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    uint32_t stage = 0, phase = 0, issued = 0;
+    bool ok = true;
+    for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+      int mt, nt;
+      gemm_tile_coords(tile, a, mt, nt);
+      const int m_row = mt * kPairBM + static_cast<int>(rank) * 128;
+      const int n_row = nt * kPairBN + static_cast<int>(rank) * 128;
+      for (int kb = 0; kb < a.num_k_blocks; ++kb) {
+        ok = warp_wait_bounded<true>(ptx::smem_u32(&empty[stage]), phase ^ 1, ctl, 1);
+        if (!ok) break;
+        if (lane == 0) {
+          const uint32_t fb_own = ptx::smem_u32(&full[stage]);
+          const uint32_t fb_leader = ptx::mapa_shared(fb_own, 0);
+          if (rank == 0) ptx::mbar_arrive_expect_tx(fb_own, PAIR_TX);
+          ptx::tma_load_2d_pair(ptx::smem_u32(sA + stage * kPairStageA), &tmA, fb_leader, kb * BK, m_row);
+          ptx::tma_load_2d_pair(ptx::smem_u32(sB + stage * kPairStageB), &tmB, fb_leader, kb * BK, n_row);
+        }
+        ++issued;
+        if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+      }
+    }
+    // Drain (leader): the full barriers count both CTAs' bytes, so once they complete every load of the
+    // pair has landed. The peer's loads are covered by the cluster barrier that follows.
+    if (lane == 0 && rank == 0) {
+      const uint32_t first = issued > kPairStages ? issued - kPairStages : 0;
+      WaitCtl dctl = ctl;
+      volatile int never = 0;
+      dctl.abort = &never;
+      for (uint32_t i = first; i < issued; ++i)
+        wait_bounded<true>(ptx::smem_u32(&full[i % kPairStages]), (i / kPairStages) & 1, dctl, 2);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (rank == 0) {
+      // ---------------------------------------------------------------- MMA issuer (leader only)
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        ok = warp_wait_bounded<true>(ptx::smem_u32(&tempty[acc]), acc_phase ^ 1, ctl, 3);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * kPairBN;
+        for (int kb = 0; kb < a.num_k_blocks; ++kb) {
+          ok = warp_wait_bounded<true>(ptx::smem_u32(&full[stage]), phase, ctl, 4);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          if (lane == 0) {
+            const uint32_t a0 = ptx::smem_u32(sA + stage * kPairStageA);
+            const uint32_t b0 = ptx::smem_u32(sB + stage * kPairStageB);
+#pragma unroll
+            for (int k = 0; k < K_STEPS; ++k) {
+              const uint64_t ad = ptx::smem_desc(a0 + k * 32, 16, 1024);
+              const uint64_t bd = ptx::smem_desc(b0 + k * 32, 16, 1024);
+              if constexpr (kElemBytes == 1)
+                ptx::mma_f8_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+              else
+                ptx::mma_f16_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+            }
+            const uint32_t eb = ptx::smem_u32(&empty[stage]);
+            ptx::mma_commit_pair(eb);
+            ptx::mma_commit_pair(ptx::mapa_shared(eb, 1));
+          }
+          __syncwarp();
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        if (lane == 0) {
+          const uint32_t tb = ptx::smem_u32(&tfull[acc]);
+          ptx::mma_commit_pair(tb);
+          ptx::mma_commit_pair(ptx::mapa_shared(tb, 1));
+        }
+        __syncwarp();
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      if (lane == 0) {
+        ptx::mma_commit_pair(ptx::smem_u32(drain));
+        WaitCtl dctl = ctl;
+        volatile int never = 0;
+        dctl.abort = &never;
+        wait_bounded<true>(ptx::smem_u32(drain), 0, dctl, 5);
+      }
+      __syncwarp();
+    }
+  } else {
+    // ------------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
+    const int q = warp & 3;
+    uint32_t acc = 0, acc_phase = 0;
+    float scale = 1.0f;
+    if constexpr (kEpi == Epi::BF16Scaled) scale = __ldg(a.scale_a) * __ldg(a.scale_b);
+    for (int tile = pair; tile < num_tiles; tile += npairs) {
+      int mt, nt;
+      gemm_tile_coords(tile, a, mt, nt);
+      const int n0 = nt * kPairBN;
+      if (!warp_wait_bounded<true>(ptx::smem_u32(&tfull[acc]), acc_phase, ctl, 6)) break;
+      ptx::tc_fence_after();
+      const int row = mt * kPairBM + static_cast<int>(rank) * 128 + 32 * q + lane;
+      const bool row_ok = row < a.M;
+      const uint32_t t_row = tmem_base + acc * kPairBN + (static_cast<uint32_t>(32 * q) << 16);
+#pragma unroll 1
+      for (int c = 0; c < kPairBN; c += 32) {
+        uint32_t r[32];
+        __syncwarp();
+        ptx::tmem_ld_32x32b_x32(t_row + c, r);
+        ptx::tmem_wait_ld();
+        const int col0 = n0 + c;
+        if (row_ok) {
+          if constexpr (kEpi == Epi::F32) {
+            float* dst = reinterpret_cast<float*>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
+            if (a.vec_ok && col0 + 32 <= a.N) {
+#pragma unroll
+              for (int v = 0; v < 8; ++v)
+                st_global_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+            } else {
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < a.N) dst[i] = __uint_as_float(r[i]);
+            }
+          } else {
+            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
+            uint32_t pk[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * i]) * scale,
+                                                       __uint_as_float(r[2 * i + 1]) * scale);
+              pk[i] = *reinterpret_cast<uint32_t*>(&h);
+            }
+            if (a.vec_ok && col0 + 32 <= a.N) {
+#pragma unroll
+              for (int v = 0; v < 4; ++v)
+                st_global_v4(reinterpret_cast<float*>(dst + 8 * v), pk[4 * v], pk[4 * v + 1], pk[4 * v + 2],
+                             pk[4 * v + 3]);
+            } else {
+              for (int i = 0; i < 32; ++i)
+                if (col0 + i < a.N) {
+                  const uint32_t w = pk[i >> 1];
+                  reinterpret_cast<unsigned short*>(dst)[i] =
+                      (i & 1) ? static_cast<unsigned short>(w >> 16) : static_cast<unsigned short>(w & 0xFFFF);
+                }
+            }
+          }
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&tempty[acc]), 0));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  ptx::tc_fence_before();
+  ptx::cluster_sync();  // no CTA leaves while its peer may still read its shared memory or signal its barriers
+  ptx::tc_fence_after();
+  if (warp == 1) ptx::tmem_dealloc_pair(tmem_base, kPairTmemCols);
+}
+
+}  // namespace bsk

@@ -239,6 +239,94 @@ __device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
+// ---------------------------------------------------------------- CTA pairs (cluster of 2, cta_group::2)
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+
+// All threads of both CTAs of the cluster.
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the same shared-memory location in CTA `rank` of this cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
+  return r;
+}
+
+// Arrive on an mbarrier that may live in the peer CTA (shared::cluster address).
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_bar) : "memory");
+}
+
+// Wait on this CTA's barrier whose arrivals may come from the peer CTA.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// TMA load into this CTA's shared memory whose completion is counted on an mbarrier of either CTA of
+// the pair (the leader's, addressed through mapa). No multicast: one destination, this GPU's memory.
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* m, uint32_t cluster_bar,
+                                                 int32_t x, int32_t y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(m)), "r"(cluster_bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// TMEM management for a CTA pair: one warp of EACH CTA of the pair executes these together.
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t dst, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Pair MMA (issued by one thread of the even CTA): A rows split across the two CTAs' shared memory,
+// B columns split likewise, D rows split across the two CTAs' TMEM.
+__device__ __forceinline__ void mma_f16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                             uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the mbarrier at `cluster_bar` (either CTA of the pair) when this thread's prior pair MMAs
+// have completed. Signalling both CTAs takes two commits (own address, then the peer's mapa address).
+__device__ __forceinline__ void mma_commit_pair(uint32_t cluster_bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(cluster_bar)
+               : "memory");
+}
+
 }  // namespace ptx
 
 // ---------------------------------------------------------------- bounded waits
@@ -262,13 +350,20 @@ __device__ __forceinline__ void record_error(const WaitCtl& c, uint32_t kind, ui
 
 // Single-thread bounded wait. Returns false if the wait ran out (the CTA abort flag is then set)
 // or another role of this CTA already gave up.
+// `cluster` selects acquire.cluster (arrivals that come from the peer CTA of a pair).
+template <bool kCluster = false>
+__device__ __forceinline__ bool try_wait_scoped(uint32_t bar, uint32_t parity) {
+  return kCluster ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity);
+}
+
+template <bool kCluster = false>
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, const WaitCtl& c, uint32_t site) {
-  if (ptx::mbar_try_wait(bar, parity)) return true;
+  if (try_wait_scoped<kCluster>(bar, parity)) return true;
   const uint64_t t0 = ptx::globaltimer_ns();
   while (true) {
 #pragma unroll 1
     for (int i = 0; i < 16; ++i)
-      if (ptx::mbar_try_wait(bar, parity)) return true;
+      if (try_wait_scoped<kCluster>(bar, parity)) return true;
     if (*c.abort) return false;
     if (ptx::globaltimer_ns() - t0 > c.timeout_ns) {
       record_error(c, kErrWaitTimeout, site);
@@ -278,9 +373,10 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, cons
 }
 
 // Warp-collective bounded wait: lane 0 waits, the result is broadcast to the warp.
+template <bool kCluster = false>
 __device__ __forceinline__ bool warp_wait_bounded(uint32_t bar, uint32_t parity, const WaitCtl& c, uint32_t site) {
   int ok = 1;
-  if (ptx::lane_id() == 0) ok = wait_bounded(bar, parity, c, site) ? 1 : 0;
+  if (ptx::lane_id() == 0) ok = wait_bounded<kCluster>(bar, parity, c, site) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   return ok != 0;
 }

@@ -39,3 +39,14 @@ def test_fp8_scales_applied(no_device_error):
     D = _run(Aq, Bqt, sa, sb)
     err = ref.normwise_rel_err(D, ref.fp8_fp64(Aq, Bqt, sa, sb))
     assert err <= TOL, err
+
+
+@pytest.mark.parametrize("tile", ["pair", "single"])
+def test_fp8_tile_variants(no_device_error, monkeypatch, tile):
+    monkeypatch.setenv("BSK_GEMM_TILE", tile)
+    g = torch.Generator().manual_seed(17)
+    Aq, sa = wl.quantize_e4m3(torch.randn(640, 1024, generator=g))
+    Bqt, sb = wl.quantize_e4m3(torch.randn(768, 1024, generator=g))
+    D = _run(Aq, Bqt, sa, sb)
+    err = ref.normwise_rel_err(D, ref.fp8_fp64(Aq, Bqt, sa, sb))
+    assert err <= TOL, (tile, err)

@@ -70,3 +70,28 @@ def test_gemm_rejects_bad_args(cuda_dev):
     with pytest.raises(_capi.BskError) as e:
         _capi.gemm_f16f32(A, Bt, C)
     assert e.value.code == _capi.BSK_ERR_INVALID_ARG
+
+
+@pytest.mark.parametrize("tile", ["pair", "single"])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 640), (300, 520, 200), (1024, 1024, 1024)])
+def test_gemm_tile_variants(no_device_error, monkeypatch, tile, M, N, K):
+    """Both the CTA-pair (256x256) and the single-CTA (128x256) kernels against fp64."""
+    monkeypatch.setenv("BSK_GEMM_TILE", tile)
+    g = torch.Generator().manual_seed(M + 3 * N + 7 * K)
+    A = torch.randn(M, K, generator=g).half()
+    Bt = torch.randn(N, K, generator=g).half()
+    C = _run(A, Bt)
+    err = ref.normwise_rel_err(C, ref.dense_fp64(A, Bt))
+    assert err <= TOL, (tile, err)
+
+
+def test_gemm_pair_and_single_agree_bitwise(no_device_error, monkeypatch):
+    """Same K order of accumulation in both kernels: identical fp32 results."""
+    g = torch.Generator().manual_seed(77)
+    A = torch.randn(512, 1024, generator=g).half()
+    Bt = torch.randn(512, 1024, generator=g).half()
+    monkeypatch.setenv("BSK_GEMM_TILE", "pair")
+    c1 = _run(A, Bt)
+    monkeypatch.setenv("BSK_GEMM_TILE", "single")
+    c2 = _run(A, Bt)
+    assert torch.equal(c1, c2)
