@@ -10,7 +10,9 @@ import ctypes
 import os
 import threading
 
-LIB_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "libbsk_sm100.so")
+# BSK_CAPI_LIB selects another build of the library (e.g. one compiled with different tuning macros).
+LIB_PATH = os.environ.get("BSK_CAPI_LIB") or os.path.join(os.path.dirname(os.path.abspath(__file__)),
+                                                          "libbsk_sm100.so")
 
 BSK_OK = 0
 BSK_ERR_INVALID_ARG = -1

@@ -46,8 +46,7 @@ struct DeviceState {
   int status = BSK_OK;
   std::string init_error;
   int sm_count = 0;
-  int pair_clusters_f16 = 0;   // co-resident 2-CTA clusters of the pair GEMM kernels
-  int pair_clusters_e4m3 = 0;
+  int pair_clusters = 0;       // co-resident 2-CTA clusters of the pair GEMM kernels (all share one footprint)
   uint32_t* err_word = nullptr;
 };
 DeviceState g_devices[kMaxDevices];
@@ -79,13 +78,17 @@ int max_clusters(K kernel, int threads, int smem) {
   return n;
 }
 
-// Tile policy of the dense GEMMs: CTA-pair 256 x 256 tiles unless M fits one 128-row tile;
-// BSK_GEMM_TILE=pair|single overrides (diagnostics).
-bool use_pair_tiles(int M) {
+// Tile policy of the dense GEMMs (0 = single-CTA 128x256, 1 = CTA pair 256x256, 2 = CTA pair 256x512):
+// single when M fits one 128-row tile; the wide pair tile when N and K are large enough that its exposed
+// per-tile epilogue (one 512-column accumulator) is amortised; otherwise the double-buffered 256x256 tile.
+// BSK_GEMM_TILE=single|pair|wide overrides (diagnostics and tests).
+int gemm_tile_kind(int M, int N, int K) {
   const char* v = getenv("BSK_GEMM_TILE");
-  if (v && strcmp(v, "single") == 0) return false;
-  if (v && strcmp(v, "pair") == 0) return true;
-  return M > 128;
+  if (v && strcmp(v, "single") == 0) return 0;
+  if (v && strcmp(v, "pair") == 0) return 1;
+  if (v && strcmp(v, "wide") == 0) return 2;
+  if (M <= 128) return 0;
+  return (N >= 512 && K >= 8192) ? 2 : 1;
 }
 
 void init_device(DeviceState& st, int dev) {
@@ -112,8 +115,10 @@ void init_device(DeviceState& st, int dev) {
       allow_smem(gemm_sm100_kernel<1, Mainloop::Dense, Epi::BF16Scaled>, kGemmSmemBytes),
       allow_smem(gemm_sm100_kernel<2, Mainloop::Bsr, Epi::F32>, kGemmSmemBytes),
       allow_smem(bsattn_sm100_kernel, kAttnSmemBytes),
-      allow_smem(gemm_pair_sm100_kernel<2, Epi::F32>, kPairSmemBytes),
-      allow_smem(gemm_pair_sm100_kernel<1, Epi::BF16Scaled>, kPairSmemBytes),
+      allow_smem(gemm_pair_sm100_kernel<2, Epi::F32, 1>, kPairSmemBytes),
+      allow_smem(gemm_pair_sm100_kernel<1, Epi::BF16Scaled, 1>, kPairSmemBytes),
+      allow_smem(gemm_pair_sm100_kernel<2, Epi::F32, 2>, kPairWideSmemBytes),
+      allow_smem(gemm_pair_sm100_kernel<1, Epi::BF16Scaled, 2>, kPairWideSmemBytes),
   };
   for (cudaError_t x : errs) {
     if (x != cudaSuccess) {
@@ -122,9 +127,15 @@ void init_device(DeviceState& st, int dev) {
       return;
     }
   }
-  st.pair_clusters_f16 = max_clusters(gemm_pair_sm100_kernel<2, Epi::F32>, kPairThreads, kPairSmemBytes);
-  st.pair_clusters_e4m3 = max_clusters(gemm_pair_sm100_kernel<1, Epi::BF16Scaled>, kPairThreads, kPairSmemBytes);
-  if (st.pair_clusters_f16 <= 0 || st.pair_clusters_e4m3 <= 0) {
+  {
+    const int c[4] = {max_clusters(gemm_pair_sm100_kernel<2, Epi::F32, 1>, kPairThreads, kPairSmemBytes),
+                      max_clusters(gemm_pair_sm100_kernel<1, Epi::BF16Scaled, 1>, kPairThreads, kPairSmemBytes),
+                      max_clusters(gemm_pair_sm100_kernel<2, Epi::F32, 2>, kPairThreads, kPairWideSmemBytes),
+                      max_clusters(gemm_pair_sm100_kernel<1, Epi::BF16Scaled, 2>, kPairThreads, kPairWideSmemBytes)};
+    st.pair_clusters = c[0];
+    for (int i = 1; i < 4; ++i) st.pair_clusters = c[i] < st.pair_clusters ? c[i] : st.pair_clusters;
+  }
+  if (st.pair_clusters <= 0) {
     st.status = BSK_ERR_CUDA;
     st.init_error = "cudaOccupancyMaxActiveClusters reports no co-resident CTA pair";
     return;
@@ -204,8 +215,8 @@ int launch_status(const char* what) {
 inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // M tiles per rasterisation group: concurrent tiles then span ~2048 rows of A and a few B column panels.
-int pick_group_m(int num_m_tiles, bool pair = false) {
-  const int g = pair ? 8 : 16;
+int pick_group_m(int num_m_tiles, int kind = 0) {
+  const int g = kind == 2 ? 12 : (kind == 1 ? 8 : 16);
   return num_m_tiles < g ? num_m_tiles : g;
 }
 
@@ -252,28 +263,31 @@ int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, floa
   }
   const __half* Ah = static_cast<const __half*>(A) + k_begin;
   const __half* Bh = static_cast<const __half*>(B) + k_begin;
-  const bool pair = use_pair_tiles(M);
-  const uint32_t a_rows = pair ? 128 : kGemmBM;  // rows per CTA of the A tile
-  const uint32_t b_rows = pair ? 128 : kGemmBN;  // rows of B^T per CTA
+  const int kind = gemm_tile_kind(M, N, kr);
+  const uint32_t a_rows = kind ? 128 : kGemmBM;  // rows per CTA of the A tile
+  const uint32_t b_rows = kind ? 128 : kGemmBN;  // rows of B^T per TMA box
   CUtensorMap ta, tb;
   if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Ah, kr, M, lda * 2, 64, a_rows, "A")) return rc;
   if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Bh, kr, N, ldb * 2, 64, b_rows, "B")) return rc;
   GemmArgs a{};
+  const int tm = kind ? kPairBM : kGemmBM, tn = kind == 2 ? 512 : kGemmBN;
   a.M = M;
   a.N = N;
-  a.num_m_tiles = (M + (pair ? kPairBM : kGemmBM) - 1) / (pair ? kPairBM : kGemmBM);
-  a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
+  a.num_m_tiles = (M + tm - 1) / tm;
+  a.num_n_tiles = (N + tn - 1) / tn;
   a.num_k_blocks = (kr + 63) / 64;
-  a.group_m = pick_group_m(a.num_m_tiles, pair);
+  a.group_m = pick_group_m(a.num_m_tiles, kind);
   a.out = C;
   a.ldo = ldc;
   a.vec_ok = aligned16(C) && (ldc % 4 == 0);
   a.err = st->err_word;
   a.timeout_ns = t_timeout_ns;
   const int tiles = a.num_m_tiles * a.num_n_tiles;
-  if (pair) {
-    const int clusters = tiles < st->pair_clusters_f16 ? tiles : st->pair_clusters_f16;
-    gemm_pair_sm100_kernel<2, Epi::F32><<<2 * clusters, kPairThreads, kPairSmemBytes, s>>>(ta, tb, a);
+  const int clusters = tiles < st->pair_clusters ? tiles : st->pair_clusters;
+  if (kind == 2) {
+    gemm_pair_sm100_kernel<2, Epi::F32, 2><<<2 * clusters, kPairThreads, kPairWideSmemBytes, s>>>(ta, tb, a);
+  } else if (kind == 1) {
+    gemm_pair_sm100_kernel<2, Epi::F32, 1><<<2 * clusters, kPairThreads, kPairSmemBytes, s>>>(ta, tb, a);
   } else {
     const int grid = tiles < st->sm_count ? tiles : st->sm_count;
     gemm_sm100_kernel<2, Mainloop::Dense, Epi::F32><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
@@ -297,17 +311,18 @@ int bsk_gemm_e4m3_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, c
     cudaError_t e = cudaMemset2DAsync(D, ldd * 2, 0, (size_t)N * 2, M, s);
     return e == cudaSuccess ? BSK_OK : cuda_fail(e, "gemm_e4m3: zero fill");
   }
-  const bool pair = use_pair_tiles(M);
+  const int kind = gemm_tile_kind(M, N, K);
   CUtensorMap ta, tb;
-  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, lda, 128, pair ? 128 : kGemmBM, "A")) return rc;
-  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, ldb, 128, pair ? 128 : kGemmBN, "B")) return rc;
+  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, lda, 128, kind ? 128 : kGemmBM, "A")) return rc;
+  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, ldb, 128, kind ? 128 : kGemmBN, "B")) return rc;
   GemmArgs a{};
+  const int tm = kind ? kPairBM : kGemmBM, tn = kind == 2 ? 512 : kGemmBN;
   a.M = M;
   a.N = N;
-  a.num_m_tiles = (M + (pair ? kPairBM : kGemmBM) - 1) / (pair ? kPairBM : kGemmBM);
-  a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
+  a.num_m_tiles = (M + tm - 1) / tm;
+  a.num_n_tiles = (N + tn - 1) / tn;
   a.num_k_blocks = (K + 127) / 128;
-  a.group_m = pick_group_m(a.num_m_tiles, pair);
+  a.group_m = pick_group_m(a.num_m_tiles, kind);
   a.out = D;
   a.ldo = ldd;
   a.vec_ok = aligned16(D) && (ldd % 8 == 0);
@@ -316,9 +331,11 @@ int bsk_gemm_e4m3_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, c
   a.err = st->err_word;
   a.timeout_ns = t_timeout_ns;
   const int tiles = a.num_m_tiles * a.num_n_tiles;
-  if (pair) {
-    const int clusters = tiles < st->pair_clusters_e4m3 ? tiles : st->pair_clusters_e4m3;
-    gemm_pair_sm100_kernel<1, Epi::BF16Scaled><<<2 * clusters, kPairThreads, kPairSmemBytes, s>>>(ta, tb, a);
+  const int clusters = tiles < st->pair_clusters ? tiles : st->pair_clusters;
+  if (kind == 2) {
+    gemm_pair_sm100_kernel<1, Epi::BF16Scaled, 2><<<2 * clusters, kPairThreads, kPairWideSmemBytes, s>>>(ta, tb, a);
+  } else if (kind == 1) {
+    gemm_pair_sm100_kernel<1, Epi::BF16Scaled, 1><<<2 * clusters, kPairThreads, kPairSmemBytes, s>>>(ta, tb, a);
   } else {
     const int grid = tiles < st->sm_count ? tiles : st->sm_count;
     gemm_sm100_kernel<1, Mainloop::Dense, Epi::BF16Scaled><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);

@@ -17,22 +17,52 @@
 namespace bsk {
 
 constexpr int kPairBM = 256;
-constexpr int kPairBN = 256;
-constexpr int kPairStages = 6;
-constexpr int kPairStageA = 128 * 128;  // 128 rows x 128 B per CTA
-constexpr int kPairStageB = 128 * 128;
+#ifndef BSK_PAIR_STAGES
+#define BSK_PAIR_STAGES 6
+#endif
+// Back-off ceilings of the waiting roles (ns): the epilogue waits a whole tile, the producer waits on a
+// full ring; the MMA issuer polls tightly.
+#ifndef BSK_EPI_SLEEP_NS
+#define BSK_EPI_SLEEP_NS 4096
+#endif
+#ifndef BSK_PROD_SLEEP_NS
+#define BSK_PROD_SLEEP_NS 512
+#endif
+#ifndef BSK_MMA_SLEEP_NS
+#define BSK_MMA_SLEEP_NS 0
+#endif
 constexpr int kPairThreads = 192;
 constexpr int kPairTmemCols = 512;
-constexpr int kPairSmemBytes = 1024 + kPairStages * (kPairStageA + kPairStageB) + 256;
 
-template <int kElemBytes, Epi kEpi>
+// Shape of the pair tile: kNHalves = 1 -> 256 x 256 with two 256-column TMEM accumulators (the epilogue of
+// one tile overlaps the MMAs of the next); kNHalves = 2 -> 256 x 512 with one 512-column accumulator: two
+// N=256 MMAs per K step share the A operand, so each byte brought into shared memory feeds more FLOPs.
+template <int kNHalves>
+struct PairTile {
+  static constexpr int BN = 256 * kNHalves;
+  static constexpr int kStageA = 128 * 128;             // this CTA's 128 rows of A, 128 B of K
+  static constexpr int kStageB = kNHalves * 128 * 128;  // this CTA's 128 rows of each B^T half
+  static constexpr int kStages = kNHalves == 1 ? BSK_PAIR_STAGES : 4;
+  static constexpr int kAccBufs = 2 / kNHalves;
+  static constexpr int kSmemBytes = 1024 + kStages * (kStageA + kStageB) + 256;
+};
+constexpr int kPairBN = 256;  // narrow variant
+constexpr int kPairSmemBytes = PairTile<1>::kSmemBytes;
+constexpr int kPairWideSmemBytes = PairTile<2>::kSmemBytes;
+
+template <int kElemBytes, Epi kEpi, int kNHalves>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     gemm_pair_sm100_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                            const GemmArgs a) {
+  using T = PairTile<kNHalves>;
+  constexpr int kPairStages = T::kStages;
+  constexpr int kPairStageA = T::kStageA;
+  constexpr int kPairStageB = T::kStageB;
+  constexpr int kTileN = T::BN;
   constexpr int BK = kGemmRowBytes / kElemBytes;
   constexpr int MMA_K = 32 / kElemBytes;
   constexpr int K_STEPS = BK / MMA_K;
-  constexpr uint32_t IDESC = ptx::instr_desc(kPairBM, kPairBN, 0, 0, 0, 0);
+  constexpr uint32_t IDESC = ptx::instr_desc(kPairBM, 256, 0, 0, 0, 0);
   constexpr uint32_t PAIR_TX = 2 * (kPairStageA + kPairStageB);
   constexpr uint32_t KID = kElemBytes == 1 ? kKidGemmE4m3 : kKidGemmF16;
 
@@ -85,91 +115,93 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const int num_tiles = a.num_m_tiles * a.num_n_tiles;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer (both CTAs)
-    uint32_t stage = 0, phase = 0, issued = 0;
-    bool ok = true;
-    for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-      int mt, nt;
-      gemm_tile_coords(tile, a, mt, nt);
-      const int m_row = mt * kPairBM + static_cast<int>(rank) * 128;
-      const int n_row = nt * kPairBN + static_cast<int>(rank) * 128;
-      for (int kb = 0; kb < a.num_k_blocks; ++kb) {
-        ok = warp_wait_bounded<true>(ptx::smem_u32(&empty[stage]), phase ^ 1, ctl, 1);
-        if (!ok) break;
-        if (lane == 0) {
-          const uint32_t fb_own = ptx::smem_u32(&full[stage]);
-          const uint32_t fb_leader = ptx::mapa_shared(fb_own, 0);
-          if (rank == 0) ptx::mbar_arrive_expect_tx(fb_own, PAIR_TX);
-          ptx::tma_load_2d_pair(ptx::smem_u32(sA + stage * kPairStageA), &tmA, fb_leader, kb * BK, m_row);
-          ptx::tma_load_2d_pair(ptx::smem_u32(sB + stage * kPairStageB), &tmB, fb_leader, kb * BK, n_row);
-        }
-        ++issued;
-        if (++stage == kPairStages) { stage = 0; phase ^= 1; }
-      }
-    }
-    // Drain (leader): the full barriers count both CTAs' bytes, so once they complete every load of the
-    // pair has landed. The peer's loads are covered by the cluster barrier that follows.
-    if (lane == 0 && rank == 0) {
-      const uint32_t first = issued > kPairStages ? issued - kPairStages : 0;
-      WaitCtl dctl = ctl;
-      volatile int never = 0;
-      dctl.abort = &never;
-      for (uint32_t i = first; i < issued; ++i)
-        wait_bounded<true>(ptx::smem_u32(&full[i % kPairStages]), (i / kPairStages) & 1, dctl, 2);
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    if (rank == 0) {
-      // ---------------------------------------------------------------- MMA issuer (leader only)
-      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+    // ------------------------------------------------------------------ TMA producer (both CTAs, one thread)
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0, issued = 0;
       bool ok = true;
+      const uint32_t sA0 = ptx::smem_u32(sA), sB0 = ptx::smem_u32(sB);
+      const uint32_t full0 = ptx::smem_u32(full), empty0 = ptx::smem_u32(empty);
+      const uint32_t full0_leader = ptx::mapa_shared(full0, 0);
       for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        ok = warp_wait_bounded<true>(ptx::smem_u32(&tempty[acc]), acc_phase ^ 1, ctl, 3);
-        if (!ok) break;
-        ptx::tc_fence_after();
-        const uint32_t d_tmem = tmem_base + acc * kPairBN;
+        int mt, nt;
+        gemm_tile_coords(tile, a, mt, nt);
+        const int m_row = mt * kPairBM + static_cast<int>(rank) * 128;
+        const int n_row = nt * kTileN + static_cast<int>(rank) * 128;
         for (int kb = 0; kb < a.num_k_blocks; ++kb) {
-          ok = warp_wait_bounded<true>(ptx::smem_u32(&full[stage]), phase, ctl, 4);
+          ok = wait_bounded<true, BSK_PROD_SLEEP_NS>(empty0 + stage * 8, phase ^ 1, ctl, 1);
           if (!ok) break;
-          ptx::tc_fence_after();
-          if (lane == 0) {
-            const uint32_t a0 = ptx::smem_u32(sA + stage * kPairStageA);
-            const uint32_t b0 = ptx::smem_u32(sB + stage * kPairStageB);
+          if (rank == 0) ptx::mbar_arrive_expect_tx(full0 + stage * 8, PAIR_TX);
+          ptx::tma_load_2d_pair(sA0 + stage * kPairStageA, &tmA, full0_leader + stage * 8, kb * BK, m_row);
 #pragma unroll
-            for (int k = 0; k < K_STEPS; ++k) {
-              const uint64_t ad = ptx::smem_desc(a0 + k * 32, 16, 1024);
-              const uint64_t bd = ptx::smem_desc(b0 + k * 32, 16, 1024);
-              if constexpr (kElemBytes == 1)
-                ptx::mma_f8_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0);
-              else
-                ptx::mma_f16_pair(d_tmem, ad, bd, IDESC, (kb | k) != 0);
-            }
-            const uint32_t eb = ptx::smem_u32(&empty[stage]);
-            ptx::mma_commit_pair(eb);
-            ptx::mma_commit_pair(ptx::mapa_shared(eb, 1));
-          }
-          __syncwarp();
+          for (int h = 0; h < kNHalves; ++h)  // B^T rows of N half h: n0 + 256 h + 128 rank
+            ptx::tma_load_2d_pair(sB0 + stage * kPairStageB + h * 128 * 128, &tmB, full0_leader + stage * 8, kb * BK,
+                                  n_row + 256 * h);
+          ++issued;
           if (++stage == kPairStages) { stage = 0; phase ^= 1; }
         }
-        if (!ok) break;
-        if (lane == 0) {
-          const uint32_t tb = ptx::smem_u32(&tfull[acc]);
-          ptx::mma_commit_pair(tb);
-          ptx::mma_commit_pair(ptx::mapa_shared(tb, 1));
-        }
-        __syncwarp();
-        acc ^= 1;
-        if (acc == 0) acc_phase ^= 1;
       }
-      if (lane == 0) {
-        ptx::mma_commit_pair(ptx::smem_u32(drain));
+      // Drain (leader): the full barriers count both CTAs' bytes, so once they complete every load of the
+      // pair has landed. The peer's loads are covered by the cluster barrier that follows.
+      if (rank == 0) {
+        const uint32_t first = issued > kPairStages ? issued - kPairStages : 0;
         WaitCtl dctl = ctl;
         volatile int never = 0;
         dctl.abort = &never;
-        wait_bounded<true>(ptx::smem_u32(drain), 0, dctl, 5);
+        for (uint32_t i = first; i < issued; ++i)
+          wait_bounded<true>(full0 + (i % kPairStages) * 8, (i / kPairStages) & 1, dctl, 2);
       }
-      __syncwarp();
     }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (rank == 0 && lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer (leader, one thread)
+      uint32_t stage = 0, phase = 0, acc = 0, acc_phase = 0;
+      bool ok = true;
+      const uint32_t full0 = ptx::smem_u32(full), empty0 = ptx::smem_u32(empty);
+      const uint32_t empty0_peer = ptx::mapa_shared(empty0, 1);
+      const uint32_t tfull0 = ptx::smem_u32(tfull), tempty0 = ptx::smem_u32(tempty);
+      const uint32_t tfull0_peer = ptx::mapa_shared(tfull0, 1);
+      // Descriptors differ only in the start-address field: build them once and add the offset (>> 4).
+      const uint64_t adesc0 = ptx::smem_desc(ptx::smem_u32(sA), 16, 1024);
+      const uint64_t bdesc0 = ptx::smem_desc(ptx::smem_u32(sB), 16, 1024);
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        ok = wait_bounded<true, BSK_MMA_SLEEP_NS>(tempty0 + acc * 8, acc_phase ^ 1, ctl, 3);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * 256;
+        for (int kb = 0; kb < a.num_k_blocks; ++kb) {
+          ok = wait_bounded<true, BSK_MMA_SLEEP_NS>(full0 + stage * 8, phase, ctl, 4);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          const uint64_t ad = adesc0 + ((stage * kPairStageA) >> 4);
+          const uint64_t bd = bdesc0 + ((stage * kPairStageB) >> 4);
+#pragma unroll
+          for (int k = 0; k < K_STEPS; ++k) {
+#pragma unroll
+            for (int h = 0; h < kNHalves; ++h) {  // N half h accumulates in TMEM columns [256 h, 256 h + 256)
+              const uint64_t bdh = bd + ((h * 128 * 128) >> 4) + k * 2;
+              if constexpr (kElemBytes == 1)
+                ptx::mma_f8_pair(d_tmem + 256 * h, ad + k * 2, bdh, IDESC, (kb | k) != 0);
+              else
+                ptx::mma_f16_pair(d_tmem + 256 * h, ad + k * 2, bdh, IDESC, (kb | k) != 0);
+            }
+          }
+          ptx::mma_commit_pair(empty0 + stage * 8);
+          ptx::mma_commit_pair(empty0_peer + stage * 8);
+          if (++stage == kPairStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        ptx::mma_commit_pair(tfull0 + acc * 8);
+        ptx::mma_commit_pair(tfull0_peer + acc * 8);
+        if (++acc == T::kAccBufs) { acc = 0; acc_phase ^= 1; }
+      }
+      ptx::mma_commit_pair(ptx::smem_u32(drain));
+      WaitCtl dctl = ctl;
+      volatile int never = 0;
+      dctl.abort = &never;
+      wait_bounded<true>(ptx::smem_u32(drain), 0, dctl, 5);
+    }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------------ epilogue (warps 2..5, both CTAs)
     const int q = warp & 3;
@@ -179,14 +211,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     for (int tile = pair; tile < num_tiles; tile += npairs) {
       int mt, nt;
       gemm_tile_coords(tile, a, mt, nt);
-      const int n0 = nt * kPairBN;
-      if (!warp_wait_bounded<true>(ptx::smem_u32(&tfull[acc]), acc_phase, ctl, 6)) break;
+      const int n0 = nt * kTileN;
+      if (!warp_wait_bounded<true, BSK_EPI_SLEEP_NS>(ptx::smem_u32(&tfull[acc]), acc_phase, ctl, 6)) break;
       ptx::tc_fence_after();
       const int row = mt * kPairBM + static_cast<int>(rank) * 128 + 32 * q + lane;
       const bool row_ok = row < a.M;
-      const uint32_t t_row = tmem_base + acc * kPairBN + (static_cast<uint32_t>(32 * q) << 16);
+      const uint32_t t_row = tmem_base + acc * 256 + (static_cast<uint32_t>(32 * q) << 16);
 #pragma unroll 1
-      for (int c = 0; c < kPairBN; c += 32) {
+      for (int c = 0; c < kTileN; c += 32) {
         uint32_t r[32];
         __syncwarp();
         ptx::tmem_ld_32x32b_x32(t_row + c, r);
@@ -231,8 +263,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive_cluster(ptx::mapa_shared(ptx::smem_u32(&tempty[acc]), 0));
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1;
+      if (++acc == T::kAccBufs) { acc = 0; acc_phase ^= 1; }
     }
   }
 

@@ -206,55 +206,55 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    uint32_t stage = 0, phase = 0;
-    uint32_t acc = 0, acc_phase = 0;
-    bool ok = true;
-    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-      int mt, nt;
-      gemm_tile_coords(tile, a, mt, nt);
-      int nk;
-      if constexpr (kML == Mainloop::Dense) {
-        nk = a.num_k_blocks;
-      } else {
-        int j0, j1;
-        bsr_row_range(a, a.row_begin + mt, j0, j1);
-        nk = (j1 - j0) * BSR_STEPS;
-      }
-      ok = warp_wait_bounded(ptx::smem_u32(&tempty[acc]), acc_phase ^ 1, ctl, 3);
-      if (!ok) break;
-      ptx::tc_fence_after();
-      const uint32_t d_tmem = tmem_base + acc * kGemmBN;
-      for (int kb = 0; kb < nk; ++kb) {
-        ok = warp_wait_bounded(ptx::smem_u32(&full[stage]), phase, ctl, 4);
+    // ------------------------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      uint32_t stage = 0, phase = 0;
+      uint32_t acc = 0, acc_phase = 0;
+      bool ok = true;
+      const uint32_t full0 = ptx::smem_u32(full), empty0 = ptx::smem_u32(empty);
+      const uint32_t tfull0 = ptx::smem_u32(tfull), tempty0 = ptx::smem_u32(tempty);
+      // Descriptors differ only in the start-address field: build once, add the offset (>> 4).
+      const uint64_t adesc0 = ptx::smem_desc(ptx::smem_u32(sA), 16, 1024);
+      const uint64_t bdesc0 = kMNB ? ptx::smem_desc(ptx::smem_u32(sB), BK * 128, 1024)
+                                   : ptx::smem_desc(ptx::smem_u32(sB), 16, 1024);
+      constexpr uint32_t B_KSTEP = kMNB ? (MMA_K * 128) >> 4 : 2;  // +16 rows (MN-major) or +32 B (K-major)
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mt, nt;
+        gemm_tile_coords(tile, a, mt, nt);
+        int nk;
+        if constexpr (kML == Mainloop::Dense) {
+          nk = a.num_k_blocks;
+        } else {
+          int j0, j1;
+          bsr_row_range(a, a.row_begin + mt, j0, j1);
+          nk = (j1 - j0) * BSR_STEPS;
+        }
+        ok = wait_bounded(tempty0 + acc * 8, acc_phase ^ 1, ctl, 3);
         if (!ok) break;
         ptx::tc_fence_after();
-        if (lane == 0) {
-          const uint32_t a0 = ptx::smem_u32(sA + stage * kGemmAStage);
-          const uint32_t b0 = ptx::smem_u32(sB + stage * kGemmBStage);
+        const uint32_t d_tmem = tmem_base + acc * kGemmBN;
+        for (int kb = 0; kb < nk; ++kb) {
+          ok = wait_bounded(full0 + stage * 8, phase, ctl, 4);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          const uint64_t ad = adesc0 + ((stage * kGemmAStage) >> 4);
+          const uint64_t bd = bdesc0 + ((stage * kGemmBStage) >> 4);
 #pragma unroll
           for (int k = 0; k < K_STEPS; ++k) {
-            const uint64_t ad = ptx::smem_desc(a0 + k * 32, 16, 1024);
-            const uint64_t bd = kMNB ? ptx::smem_desc(b0 + k * (MMA_K * 128), BK * 128, 1024)
-                                     : ptx::smem_desc(b0 + k * 32, 16, 1024);
             if constexpr (kElemBytes == 1)
-              ptx::mma_f8_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+              ptx::mma_f8_ss(d_tmem, ad + k * 2, bd + k * B_KSTEP, IDESC, (kb | k) != 0);
             else
-              ptx::mma_f16_ss(d_tmem, ad, bd, IDESC, (kb | k) != 0);
+              ptx::mma_f16_ss(d_tmem, ad + k * 2, bd + k * B_KSTEP, IDESC, (kb | k) != 0);
           }
-          ptx::mma_commit(ptx::smem_u32(&empty[stage]));
+          ptx::mma_commit(empty0 + stage * 8);
+          if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
         }
-        __syncwarp();
-        if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
+        if (!ok) break;
+        ptx::mma_commit(tfull0 + acc * 8);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
       }
-      if (!ok) break;
-      if (lane == 0) ptx::mma_commit(ptx::smem_u32(&tfull[acc]));
-      __syncwarp();
-      acc ^= 1;
-      if (acc == 0) acc_phase ^= 1;
-    }
-    // Drain: all MMAs this thread issued complete before TMEM is released.
-    if (lane == 0) {
+      // Drain: all MMAs this thread issued complete before TMEM is released.
       ptx::mma_commit(ptx::smem_u32(drain));
       WaitCtl dctl = ctl;
       volatile int never = 0;

@@ -47,9 +47,22 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-// True once the phase with the given parity has completed.
+// True once the phase with the given parity has completed. With BSK_WAIT_SUSPEND_NS set, the waiting
+// thread may be suspended up to that long inside one try_wait instead of re-polling.
+#ifndef BSK_WAIT_SUSPEND_NS
+#define BSK_WAIT_SUSPEND_NS 0
+#endif
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
+#if BSK_WAIT_SUSPEND_NS > 0
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "n"(BSK_WAIT_SUSPEND_NS)
+      : "memory");
+#else
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n\t"
@@ -57,6 +70,7 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "=r"(ok)
       : "r"(bar), "r"(parity)
       : "memory");
+#endif
   return ok != 0;
 }
 
@@ -266,6 +280,15 @@ __device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_bar) {
 // Wait on this CTA's barrier whose arrivals may come from the peer CTA.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
   uint32_t ok;
+#if BSK_WAIT_SUSPEND_NS > 0
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "n"(BSK_WAIT_SUSPEND_NS)
+      : "memory");
+#else
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
@@ -273,6 +296,7 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
       : "=r"(ok)
       : "r"(bar), "r"(parity)
       : "memory");
+#endif
   return ok != 0;
 }
 
@@ -356,27 +380,35 @@ __device__ __forceinline__ bool try_wait_scoped(uint32_t bar, uint32_t parity) {
   return kCluster ? ptx::mbar_try_wait_cluster(bar, parity) : ptx::mbar_try_wait(bar, parity);
 }
 
-template <bool kCluster = false>
+// kMaxSleepNs > 0: between polls the thread backs off with __nanosleep (32 ns doubling up to kMaxSleepNs),
+// so roles that wait long (epilogue warps for a whole tile, the producer on a full ring) stop spinning and
+// the SM's issue slots and power go to the tensor pipe. kMaxSleepNs = 0 polls tightly (the MMA issuer).
+template <bool kCluster = false, uint32_t kMaxSleepNs = 0>
 __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, const WaitCtl& c, uint32_t site) {
   if (try_wait_scoped<kCluster>(bar, parity)) return true;
   const uint64_t t0 = ptx::globaltimer_ns();
+  uint32_t sleep_ns = 32;
   while (true) {
 #pragma unroll 1
-    for (int i = 0; i < 16; ++i)
+    for (int i = 0; i < (kMaxSleepNs ? 2 : 16); ++i)
       if (try_wait_scoped<kCluster>(bar, parity)) return true;
     if (*c.abort) return false;
     if (ptx::globaltimer_ns() - t0 > c.timeout_ns) {
       record_error(c, kErrWaitTimeout, site);
       return false;
     }
+    if constexpr (kMaxSleepNs > 0) {
+      __nanosleep(sleep_ns);
+      sleep_ns = sleep_ns * 2 > kMaxSleepNs ? kMaxSleepNs : sleep_ns * 2;
+    }
   }
 }
 
 // Warp-collective bounded wait: lane 0 waits, the result is broadcast to the warp.
-template <bool kCluster = false>
+template <bool kCluster = false, uint32_t kMaxSleepNs = 0>
 __device__ __forceinline__ bool warp_wait_bounded(uint32_t bar, uint32_t parity, const WaitCtl& c, uint32_t site) {
   int ok = 1;
-  if (ptx::lane_id() == 0) ok = wait_bounded<kCluster>(bar, parity, c, site) ? 1 : 0;
+  if (ptx::lane_id() == 0) ok = wait_bounded<kCluster, kMaxSleepNs>(bar, parity, c, site) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   return ok != 0;
 }

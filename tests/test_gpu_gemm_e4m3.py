@@ -41,7 +41,7 @@ def test_fp8_scales_applied(no_device_error):
     assert err <= TOL, err
 
 
-@pytest.mark.parametrize("tile", ["pair", "single"])
+@pytest.mark.parametrize("tile", ["pair", "wide", "single"])
 def test_fp8_tile_variants(no_device_error, monkeypatch, tile):
     monkeypatch.setenv("BSK_GEMM_TILE", tile)
     g = torch.Generator().manual_seed(17)

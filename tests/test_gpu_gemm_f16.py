@@ -72,10 +72,11 @@ def test_gemm_rejects_bad_args(cuda_dev):
     assert e.value.code == _capi.BSK_ERR_INVALID_ARG
 
 
-@pytest.mark.parametrize("tile", ["pair", "single"])
-@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 640), (300, 520, 200), (1024, 1024, 1024)])
+@pytest.mark.parametrize("tile", ["pair", "wide", "single"])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (512, 768, 640), (300, 520, 200), (1024, 1024, 1024),
+                                   (768, 1536, 4160)])
 def test_gemm_tile_variants(no_device_error, monkeypatch, tile, M, N, K):
-    """Both the CTA-pair (256x256) and the single-CTA (128x256) kernels against fp64."""
+    """The CTA-pair 256x256 and 256x512 kernels and the single-CTA 128x256 kernel against fp64."""
     monkeypatch.setenv("BSK_GEMM_TILE", tile)
     g = torch.Generator().manual_seed(M + 3 * N + 7 * K)
     A = torch.randn(M, K, generator=g).half()
@@ -90,8 +91,8 @@ def test_gemm_pair_and_single_agree_bitwise(no_device_error, monkeypatch):
     g = torch.Generator().manual_seed(77)
     A = torch.randn(512, 1024, generator=g).half()
     Bt = torch.randn(512, 1024, generator=g).half()
-    monkeypatch.setenv("BSK_GEMM_TILE", "pair")
-    c1 = _run(A, Bt)
-    monkeypatch.setenv("BSK_GEMM_TILE", "single")
-    c2 = _run(A, Bt)
-    assert torch.equal(c1, c2)
+    outs = []
+    for tile in ("pair", "wide", "single"):
+        monkeypatch.setenv("BSK_GEMM_TILE", tile)
+        outs.append(_run(A, Bt))
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], outs[2])
