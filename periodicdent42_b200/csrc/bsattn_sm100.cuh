@@ -40,12 +40,11 @@ struct AttnArgs {
   uint64_t timeout_ns;
 };
 
-// Work item -> (bh, qb): longest rows first (mask rows grow with the query block index under a causal
-// pattern), pairs interleaved so concurrent CTAs spread over heads.
+// Work item -> (bh, qb): head-major, so the CTAs running at the same time share one or two heads' K and V
+// blocks in L2; within a head the longest rows (highest query block under a causal pattern) come first.
 __device__ __forceinline__ void attn_item(const AttnArgs& a, int item, int& bh, int& qb) {
-  const int npairs = a.num_items / a.nqb;
-  qb = a.nqb - 1 - item / npairs;
-  bh = a.bh_begin + item % npairs;
+  qb = a.nqb - 1 - item % a.nqb;
+  bh = a.bh_begin + item / a.nqb;
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
