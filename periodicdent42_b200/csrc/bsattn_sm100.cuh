@@ -1,14 +1,24 @@
 // Block-sparse attention forward for sm_100a (bf16 in/out, fp32 online softmax), 128x128 blocks, D = 128.
 //
-// Work item = (b, h, query block-row i). For the nonzero key blocks j of that row (BSR index of the
-// per-(b,h) block mask) the CTA computes
-//     S_j = Q_i K_j^T          tcgen05.mma 128x128x16 x 8, K-major operands, fp32 into TMEM (2 S buffers)
-//     P_j = exp2(S_j*scale*log2e - m)  online softmax by 4 warps, one query row per thread, P -> smem bf16
-//     O  += P_j V_j            tcgen05.mma with V as an MN-major operand (row-major [kv, d] tile)
-// and writes O / l as bf16. Only nonzero blocks are ever loaded (TMA, 2-stage K and V rings).
-// Roles: warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 2-5 softmax + output.
-// The running max is only moved when a block raises it by more than 8 (log2 units); P then stays
-// below 2^8 and O is rescaled in TMEM (tcgen05.ld / st) only on those moves.
+// Work item = (b, h) pair and TWO query block-rows of it ("streams" A and B, rows 2t+1 and 2t counted from
+// the end, so the longest rows of a causal pattern come first). For every nonzero key block j of a stream's
+// mask row the CTA computes
+//     S_j = Q K_j^T                 tcgen05.mma 128x128x16 x 8 into the stream's TMEM S buffer
+//     P_j = exp2(S_j * c - m)       online softmax, one query row per thread; P (bf16) is written back into
+//                                   the first 64 columns of the stream's S buffer in TMEM (tcgen05.st)
+//     O  += P_j V_j                 tcgen05.mma with A = P from TMEM, V an MN-major shared-memory operand
+// and writes O / l as bf16. Only nonzero blocks are loaded (TMA through a 5-slot K/V ring).
+//
+// Roles (12 warps): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 4-7 softmax of stream A,
+// warps 8-11 softmax of stream B (warp w reads TMEM lanes 32*(w%4)..+31). Per block j the MMA warp issues
+// PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): tcgen05.mma ops of one thread execute in issue order, so S_A(j+1) may
+// overwrite the TMEM columns PV_A(j) reads, and the two streams interleave so that one stream's softmax
+// overlaps the other stream's tensor work. TMEM: S/P_A [0,128), S/P_B [128,256), O_A [256,384), O_B [384,512).
+//
+// Softmax: the reference max moves only when a block raises it by more than 8 (log2 units), so P <= 2^8 and
+// O is rescaled in TMEM only on those moves. exp2 runs on the MUFU for 3/4 of the elements and, for the
+// other 1/4, on the FMA pipe as a Cody-Waite split x = n + f with a cubic for 2^f on [0,1) (coefficients
+// fitted here by constrained minimax; max relative error 1.03e-4, p(0) = 1, p(1) = 2).
 #pragma once
 
 #include <cuda_bf16.h>
@@ -19,38 +29,76 @@ namespace bsk {
 
 constexpr int kAttnBlk = 128;
 constexpr int kAttnD = 128;
-constexpr int kAttnThreads = 192;
+constexpr int kAttnThreads = 384;
 constexpr int kAttnTile = kAttnBlk * kAttnD * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-col SW128 chunks)
 constexpr int kAttnChunk = kAttnTile / 2;          // 16 KB
-constexpr int kAttnKVStages = 2;
-constexpr int kAttnSmemBytes = 1024 + kAttnTile * (1 /*Q*/ + 2 * kAttnKVStages /*K,V*/ + 1 /*P*/) + 256;
-constexpr int kAttnTmemCols = 512;  // S0 [0,128), S1 [128,256), O [256,384)
+constexpr int kAttnKVSlots = 5;
+constexpr int kAttnSmemBytes = 1024 + kAttnTile * (2 /*Q*/ + kAttnKVSlots) + 256;
+constexpr int kAttnTmemCols = 512;
+constexpr uint32_t kAttnRegsLaunch = 168;  // 65536 / 384, rounded down to a multiple of 8
+constexpr uint32_t kAttnRegsLow = 112;
+constexpr uint32_t kAttnRegsHigh = 184;
+static_assert(128 * kAttnRegsLow + 256 * kAttnRegsHigh <= kAttnThreads * kAttnRegsLaunch,
+              "setmaxnreg split exceeds the launch allocation");
 
 struct AttnArgs {
   __nv_bfloat16* O;
   const int* row_ptr;
   const int* col_idx;
-  int S;          // sequence length
-  int nqb;        // S / 128
-  int bh_begin;   // first (b,h) pair of this launch
-  int num_items;  // (#pairs) * nqb
-  float scale_log2;
+  int S;              // sequence length
+  int nqb;            // S / 128
+  int items_per_pair; // ceil(nqb / 2)
+  int bh_begin;       // first (b,h) pair of this launch
+  int num_items;      // (#pairs) * items_per_pair
+  float scale_log2;   // softmax scale * log2(e)
   int causal_diag;
   uint32_t* err;
   uint64_t timeout_ns;
 };
 
-// Work item -> (bh, qb): head-major, so the CTAs running at the same time share one or two heads' K and V
-// blocks in L2; within a head the longest rows (highest query block under a causal pattern) come first.
-__device__ __forceinline__ void attn_item(const AttnArgs& a, int item, int& bh, int& qb) {
-  qb = a.nqb - 1 - item % a.nqb;
-  bh = a.bh_begin + item / a.nqb;
+struct AttnStream {
+  int qb;  // query block-row (-1: no row)
+  int j0;  // first nonzero of the row
+  int n;   // nonzero blocks of the row
+};
+
+// Work item -> (bh, two query block-rows). Head-major, so concurrent CTAs share a head's K/V in L2.
+__device__ __forceinline__ void attn_item(const AttnArgs& a, int item, int& bh, AttnStream& sa, AttnStream& sb) {
+  bh = a.bh_begin + item / a.items_per_pair;
+  const int t = item % a.items_per_pair;
+  sa.qb = a.nqb - 1 - 2 * t;
+  sb.qb = a.nqb - 2 - 2 * t;
+  const int pa = bh * a.nqb + sa.qb;
+  sa.j0 = __ldg(&a.row_ptr[pa]);
+  sa.n = __ldg(&a.row_ptr[pa + 1]) - sa.j0;
+  if (sb.qb >= 0) {
+    sb.j0 = __ldg(&a.row_ptr[pa - 1]);
+    sb.n = sa.j0 - sb.j0;
+  } else {
+    sb.j0 = 0;
+    sb.n = 0;
+  }
+  sa.n = max(sa.n, 0);
+  sb.n = max(sb.n, 0);
 }
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x on the FMA pipe: x = n + f, n = floor(x), 2^f by the cubic above, 2^n added to the exponent field.
+__device__ __forceinline__ float ex2_poly(float x) {
+  const float xc = fmaxf(x, -126.0f);
+  const float fl = floorf(xc);
+  const float f = xc - fl;
+  float p = fmaf(0.078267968f, f, 0.226307680f);
+  p = fmaf(p, f, 0.695424352f);
+  p = fmaf(p, f, 1.0f);
+  const int e = static_cast<int>(fl);
+  const float r = __int_as_float(__float_as_int(p) + (e << 23));
+  return x < -126.0f ? 0.0f : r;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -70,23 +118,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sK = sQ + kAttnTile;
-  uint8_t* sV = sK + kAttnKVStages * kAttnTile;
-  uint8_t* sP = sV + kAttnKVStages * kAttnTile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kAttnTile);
+  uint8_t* sQ = smem;                       // [2] Q_A, Q_B
+  uint8_t* sKV = sQ + 2 * kAttnTile;        // [kAttnKVSlots]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kAttnKVSlots * kAttnTile);
   uint64_t* q_full = bars + 0;
   uint64_t* q_empty = bars + 1;
-  uint64_t* k_full = bars + 2;   // [2]
-  uint64_t* k_empty = bars + 4;  // [2]
-  uint64_t* v_full = bars + 6;   // [2]
-  uint64_t* v_empty = bars + 8;  // [2]
-  uint64_t* s_full = bars + 10;  // [2]
-  uint64_t* s_empty = bars + 12; // [2]
-  uint64_t* p_full = bars + 14;
-  uint64_t* pv_done = bars + 15;
-  uint64_t* drain = bars + 16;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(bars + 17);
+  uint64_t* kv_full = bars + 2;                 // [3]
+  uint64_t* kv_empty = bars + 2 + kAttnKVSlots;  // [3]
+  uint64_t* s_full = bars + 2 + 2 * kAttnKVSlots;  // [2] per stream: S_j in TMEM
+  uint64_t* p_full = s_full + 2;                   // [2] P_j written to TMEM (4 warp arrivals)
+  uint64_t* o_done = p_full + 2;                   // [2] last PV of the stream's row completed
+  uint64_t* drain = o_done + 2;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -95,16 +138,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   if (threadIdx.x == 0) {
     ptx::mbar_init(ptx::smem_u32(q_full), 1);
     ptx::mbar_init(ptx::smem_u32(q_empty), 1);
-    for (int s = 0; s < 2; ++s) {
-      ptx::mbar_init(ptx::smem_u32(&k_full[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&k_empty[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&v_full[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&v_empty[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&s_full[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&s_empty[s]), 4);
+    for (int s = 0; s < kAttnKVSlots; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&kv_full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&kv_empty[s]), 1);
     }
-    ptx::mbar_init(ptx::smem_u32(p_full), 4);
-    ptx::mbar_init(ptx::smem_u32(pv_done), 1);
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&s_full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&p_full[s]), 4);
+      ptx::mbar_init(ptx::smem_u32(&o_done[s]), 1);
+    }
     ptx::mbar_init(ptx::smem_u32(drain), 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -124,149 +166,142 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
   WaitCtl ctl{abort_flag, a.err, a.timeout_ns, kKidBsAttn};
 
+  // Launch allocation 384 x 168 = 64512 registers; warpgroup 0 (producer, MMA, 2 idle warps) drops to
+  // kAttnRegsLow per thread, the two softmax warpgroups rise to kAttnRegsHigh (sum checked at compile time).
+  static_assert(kAttnThreads == 384, "register split assumes 12 warps");
+  if (warp < 4) ptx::setmaxnreg_dec<kAttnRegsLow>();
+
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
-    uint32_t q_phase = 0, kv_stage = 0, kv_phase = 0;
-    uint32_t q_issued = 0, kv_issued = 0;
-    bool ok = true;
-    for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
-      int bh, qb;
-      attn_item(a, item, bh, qb);
-      const int p = bh * a.nqb + qb;
-      const int j0 = __ldg(&a.row_ptr[p]);
-      const int j1 = __ldg(&a.row_ptr[p + 1]);
-      if (j1 <= j0) continue;
-      ok = warp_wait_bounded(ptx::smem_u32(q_empty), q_phase ^ 1, ctl, 1);
-      if (!ok) break;
-      const int row0 = bh * a.S;
-      if (lane == 0) {
-        const uint32_t fb = ptx::smem_u32(q_full);
+    // ------------------------------------------------------------------ TMA producer (one thread)
+    if (lane == 0) {
+      uint32_t q_phase = 0, slot = 0, slot_phase = 0, q_issued = 0, kv_issued = 0;
+      bool ok = true;
+      const uint32_t kv0 = ptx::smem_u32(sKV);
+      auto push = [&](const CUtensorMap* m, int row) -> bool {
+        if (!wait_bounded<false, 512>(ptx::smem_u32(&kv_empty[slot]), slot_phase ^ 1, ctl, 2)) return false;
+        const uint32_t fb = ptx::smem_u32(&kv_full[slot]);
+        const uint32_t dst = kv0 + slot * kAttnTile;
         ptx::mbar_arrive_expect_tx(fb, kAttnTile);
-        ptx::tma_load_2d(ptx::smem_u32(sQ), &tmQ, fb, 0, row0 + qb * kAttnBlk);
-        ptx::tma_load_2d(ptx::smem_u32(sQ + kAttnChunk), &tmQ, fb, 64, row0 + qb * kAttnBlk);
-      }
-      ++q_issued;
-      q_phase ^= 1;
-      for (int jb = j0; jb < j1 && ok; jb += 32) {
-        const int cidx = (jb + lane < j1) ? __ldg(&a.col_idx[jb + lane]) : 0;
-        const int cnt = min(32, j1 - jb);
-        for (int jj = 0; jj < cnt; ++jj) {
-          int kb = __shfl_sync(0xffffffffu, cidx, jj);
-          if (kb < 0 || kb >= a.nqb) {  // out-of-range index: flag it, load nothing real (zero fill)
-            if (lane == 0) atomicCAS(a.err, 0u, kErrBounds | (kKidBsAttn << 8) | (7u << 16));
-            kb = a.nqb;
-          }
-          const int kvrow = row0 + kb * kAttnBlk;
-          ok = warp_wait_bounded(ptx::smem_u32(&k_empty[kv_stage]), kv_phase ^ 1, ctl, 2);
-          if (!ok) break;
-          if (lane == 0) {
-            const uint32_t fb = ptx::smem_u32(&k_full[kv_stage]);
-            const uint32_t dst = ptx::smem_u32(sK + kv_stage * kAttnTile);
-            ptx::mbar_arrive_expect_tx(fb, kAttnTile);
-            ptx::tma_load_2d(dst, &tmK, fb, 0, kvrow);
-            ptx::tma_load_2d(dst + kAttnChunk, &tmK, fb, 64, kvrow);
-          }
-          ok = warp_wait_bounded(ptx::smem_u32(&v_empty[kv_stage]), kv_phase ^ 1, ctl, 3);
-          if (!ok) break;
-          if (lane == 0) {
-            const uint32_t fb = ptx::smem_u32(&v_full[kv_stage]);
-            const uint32_t dst = ptx::smem_u32(sV + kv_stage * kAttnTile);
-            ptx::mbar_arrive_expect_tx(fb, kAttnTile);
-            ptx::tma_load_2d(dst, &tmV, fb, 0, kvrow);
-            ptx::tma_load_2d(dst + kAttnChunk, &tmV, fb, 64, kvrow);
-          }
-          ++kv_issued;
-          if (++kv_stage == kAttnKVStages) { kv_stage = 0; kv_phase ^= 1; }
+        ptx::tma_load_2d(dst, m, fb, 0, row);
+        ptx::tma_load_2d(dst + kAttnChunk, m, fb, 64, row);
+        ++kv_issued;
+        if (++slot == kAttnKVSlots) { slot = 0; slot_phase ^= 1; }
+        return true;
+      };
+      // key block j of a stream -> first row of its K/V tile in the [B*H*S, D] view
+      auto kvrow = [&](int bh, const AttnStream& st, int j) -> int {
+        int kb = __ldg(&a.col_idx[st.j0 + j]);
+        if (kb < 0 || kb >= a.nqb) {  // out-of-range index: flag it; the load reads zero fill
+          atomicCAS(a.err, 0u, kErrBounds | (kKidBsAttn << 8) | (7u << 16));
+          kb = a.nqb;
+        }
+        return bh * a.S + kb * kAttnBlk;
+      };
+      for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
+        int bh;
+        AttnStream A, B;
+        attn_item(a, item, bh, A, B);
+        if (A.n + B.n == 0) continue;
+        ok = wait_bounded<false, 512>(ptx::smem_u32(q_empty), q_phase ^ 1, ctl, 1);
+        if (!ok) break;
+        const uint32_t qf = ptx::smem_u32(q_full);
+        ptx::mbar_arrive_expect_tx(qf, (A.n > 0 ? kAttnTile : 0) + (B.n > 0 ? kAttnTile : 0));
+        const int row0 = bh * a.S;
+        if (A.n > 0) {
+          ptx::tma_load_2d(ptx::smem_u32(sQ), &tmQ, qf, 0, row0 + A.qb * kAttnBlk);
+          ptx::tma_load_2d(ptx::smem_u32(sQ) + kAttnChunk, &tmQ, qf, 64, row0 + A.qb * kAttnBlk);
+        }
+        if (B.n > 0) {
+          ptx::tma_load_2d(ptx::smem_u32(sQ) + kAttnTile, &tmQ, qf, 0, row0 + B.qb * kAttnBlk);
+          ptx::tma_load_2d(ptx::smem_u32(sQ) + kAttnTile + kAttnChunk, &tmQ, qf, 64, row0 + B.qb * kAttnBlk);
+        }
+        ++q_issued;
+        q_phase ^= 1;
+        // Same order as the MMA warp consumes: K_A0, K_B0, then per j: V_A(j), K_A(j+1), V_B(j), K_B(j+1).
+        if (A.n > 0) ok = ok && push(&tmK, kvrow(bh, A, 0));
+        if (B.n > 0) ok = ok && push(&tmK, kvrow(bh, B, 0));
+        const int n = max(A.n, B.n);
+        for (int j = 0; j < n && ok; ++j) {
+          if (j < A.n) ok = ok && push(&tmV, kvrow(bh, A, j));
+          if (j + 1 < A.n) ok = ok && push(&tmK, kvrow(bh, A, j + 1));
+          if (j < B.n) ok = ok && push(&tmV, kvrow(bh, B, j));
+          if (j + 1 < B.n) ok = ok && push(&tmK, kvrow(bh, B, j + 1));
         }
       }
-    }
-    // Drain loads still in flight.
-    if (lane == 0) {
+      // Drain loads still in flight.
       WaitCtl dctl = ctl;
       volatile int never = 0;
       dctl.abort = &never;
       if (q_issued) wait_bounded(ptx::smem_u32(q_full), (q_issued - 1) & 1, dctl, 8);
-      const uint32_t first = kv_issued > kAttnKVStages ? kv_issued - kAttnKVStages : 0;
-      for (uint32_t i = first; i < kv_issued; ++i) {
-        wait_bounded(ptx::smem_u32(&k_full[i % kAttnKVStages]), (i / kAttnKVStages) & 1, dctl, 8);
-        wait_bounded(ptx::smem_u32(&v_full[i % kAttnKVStages]), (i / kAttnKVStages) & 1, dctl, 8);
-      }
+      const uint32_t first = kv_issued > kAttnKVSlots ? kv_issued - kAttnKVSlots : 0;
+      for (uint32_t i = first; i < kv_issued; ++i)
+        wait_bounded(ptx::smem_u32(&kv_full[i % kAttnKVSlots]), (i / kAttnKVSlots) & 1, dctl, 8);
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer
-    uint32_t q_phase = 0;
-    uint32_t k_stage = 0, k_phase = 0, v_stage = 0, v_phase = 0;
-    uint32_t s_cnt = 0;   // S computations issued (buffer = s_cnt & 1)
-    uint32_t p_cnt = 0;   // P tiles consumed
-    bool ok = true;
-    const uint32_t sQa = ptx::smem_u32(sQ);
-    const uint32_t sPa = ptx::smem_u32(sP);
-    const uint32_t tO = tmem_base + 256;
-
-    auto issue_s = [&](bool last_of_item) -> bool {
-      const uint32_t sb = s_cnt & 1;
-      // S buffer sb is free once the softmax warps have read its previous use.
-      if (!warp_wait_bounded(ptx::smem_u32(&s_empty[sb]), ((s_cnt >> 1) & 1) ^ 1, ctl, 10)) return false;
-      if (!warp_wait_bounded(ptx::smem_u32(&k_full[k_stage]), k_phase, ctl, 11)) return false;
-      ptx::tc_fence_after();
-      if (lane == 0) {
-        const uint32_t kA = ptx::smem_u32(sK + k_stage * kAttnTile);
+    // ------------------------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      uint32_t q_phase = 0, slot = 0, slot_phase = 0;
+      uint32_t p_uses[2] = {0, 0};
+      bool ok = true;
+      const uint32_t sQa = ptx::smem_u32(sQ), kv0 = ptx::smem_u32(sKV);
+      auto take_slot = [&](uint32_t site) -> uint32_t {
+        if (!wait_bounded(ptx::smem_u32(&kv_full[slot]), slot_phase, ctl, site)) return 0xFFFFFFFFu;
+        return slot;
+      };
+      auto release_slot = [&](uint32_t sl) {
+        ptx::mma_commit(ptx::smem_u32(&kv_empty[sl]));
+        if (++slot == kAttnKVSlots) { slot = 0; slot_phase ^= 1; }
+      };
+      auto issue_s = [&](int x) -> bool {  // S_x = Q_x K^T (after PV_x of the previous block, in issue order)
+        const uint32_t sl = take_slot(11);
+        if (sl == 0xFFFFFFFFu) return false;
+        ptx::tc_fence_after();
+        const uint32_t kA = kv0 + sl * kAttnTile, qA = sQa + x * kAttnTile;
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t off = (k >> 2) * kAttnChunk + (k & 3) * 32;
-          ptx::mma_f16_ss(tmem_base + sb * 128, ptx::smem_desc(sQa + off, 16, 1024), ptx::smem_desc(kA + off, 16, 1024),
+          ptx::mma_f16_ss(tmem_base + x * 128, ptx::smem_desc(qA + off, 16, 1024), ptx::smem_desc(kA + off, 16, 1024),
                           IDESC_S, k != 0);
         }
-        ptx::mma_commit(ptx::smem_u32(&k_empty[k_stage]));
-        ptx::mma_commit(ptx::smem_u32(&s_full[sb]));
-        if (last_of_item) ptx::mma_commit(ptx::smem_u32(q_empty));
-      }
-      __syncwarp();
-      ++s_cnt;
-      if (++k_stage == kAttnKVStages) { k_stage = 0; k_phase ^= 1; }
-      return true;
-    };
-    auto issue_pv = [&](bool first_of_item) -> bool {
-      if (!warp_wait_bounded(ptx::smem_u32(p_full), p_cnt & 1, ctl, 12)) return false;
-      if (!warp_wait_bounded(ptx::smem_u32(&v_full[v_stage]), v_phase, ctl, 13)) return false;
-      ptx::tc_fence_after();
-      if (lane == 0) {
-        const uint32_t vA = ptx::smem_u32(sV + v_stage * kAttnTile);
+        release_slot(sl);
+        ptx::mma_commit(ptx::smem_u32(&s_full[x]));
+        return true;
+      };
+      auto issue_pv = [&](int x, bool first, bool last) -> bool {  // O_x += P_x (TMEM) V
+        if (!wait_bounded(ptx::smem_u32(&p_full[x]), p_uses[x] & 1, ctl, 12)) return false;
+        ++p_uses[x];
+        const uint32_t sl = take_slot(13);
+        if (sl == 0xFFFFFFFFu) return false;
+        ptx::tc_fence_after();
+        const uint32_t vA = kv0 + sl * kAttnTile;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
-          const uint32_t aoff = (k >> 2) * kAttnChunk + (k & 3) * 32;
-          ptx::mma_f16_ss(tO, ptx::smem_desc(sPa + aoff, 16, 1024), ptx::smem_desc(vA + k * 2048, kAttnChunk, 1024),
-                          IDESC_PV, (first_of_item && k == 0) ? 0u : 1u);
+        for (int k = 0; k < 8; ++k)  // K step k: P columns [8k, 8k+8) hold kv positions [16k, 16k+16)
+          ptx::mma_f16_ts(tmem_base + 256 + x * 128, tmem_base + x * 128 + 8 * k,
+                          ptx::smem_desc(vA + k * 2048, kAttnChunk, 1024), IDESC_PV, (first && k == 0) ? 0u : 1u);
+        release_slot(sl);
+        if (last) ptx::mma_commit(ptx::smem_u32(&o_done[x]));
+        return true;
+      };
+      for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
+        int bh;
+        AttnStream A, B;
+        attn_item(a, item, bh, A, B);
+        if (A.n + B.n == 0) continue;
+        ok = wait_bounded(ptx::smem_u32(q_full), q_phase, ctl, 14);
+        if (!ok) break;
+        q_phase ^= 1;
+        if (A.n > 0) ok = ok && issue_s(0);
+        if (B.n > 0) ok = ok && issue_s(1);
+        const int n = max(A.n, B.n);
+        for (int j = 0; j < n && ok; ++j) {
+          if (j < A.n) ok = ok && issue_pv(0, j == 0, j + 1 == A.n);
+          if (j + 1 < A.n) ok = ok && issue_s(0);
+          if (j < B.n) ok = ok && issue_pv(1, j == 0, j + 1 == B.n);
+          if (j + 1 < B.n) ok = ok && issue_s(1);
         }
-        ptx::mma_commit(ptx::smem_u32(&v_empty[v_stage]));
-        ptx::mma_commit(ptx::smem_u32(pv_done));
+        if (ok) ptx::mma_commit(ptx::smem_u32(q_empty));
       }
-      __syncwarp();
-      ++p_cnt;
-      if (++v_stage == kAttnKVStages) { v_stage = 0; v_phase ^= 1; }
-      return true;
-    };
-
-    for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
-      int bh, qb;
-      attn_item(a, item, bh, qb);
-      const int p = bh * a.nqb + qb;
-      const int n = __ldg(&a.row_ptr[p + 1]) - __ldg(&a.row_ptr[p]);
-      if (n <= 0) continue;
-      ok = warp_wait_bounded(ptx::smem_u32(q_full), q_phase, ctl, 14);
-      if (!ok) break;
-      q_phase ^= 1;
-      ok = issue_s(n == 1);
-      for (int jj = 0; jj < n && ok; ++jj) {
-        if (jj + 1 < n) {
-          ok = issue_s(jj + 2 == n);
-          if (!ok) break;
-        }
-        ok = issue_pv(jj == 0);
-      }
-    }
-    if (lane == 0) {
       ptx::mma_commit(ptx::smem_u32(drain));
       WaitCtl dctl = ctl;
       volatile int never = 0;
@@ -274,125 +309,118 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       wait_bounded(ptx::smem_u32(drain), 0, dctl, 15);
     }
     __syncwarp();
-  } else {
-    // ------------------------------------------------------------------ softmax + output (warps 2..5)
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ softmax + output (warps 4..11)
+    ptx::setmaxnreg_inc<kAttnRegsHigh>();
+    const int x = (warp - 4) >> 2;  // stream of this warp group
     const int q = warp & 3;
     const int r = 32 * q + lane;  // query row within the block == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
-    const uint32_t tO = tmem_base + 256 + lane_off;
-    uint32_t s_cnt = 0, pv_cnt = 0;
-    const uint32_t sPa = ptx::smem_u32(sP);
+    const uint32_t tS = tmem_base + x * 128 + lane_off;
+    const uint32_t tO = tmem_base + 256 + x * 128 + lane_off;
+    const float c = a.scale_log2;
+    uint32_t s_cnt = 0, o_cnt = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
-      int bh, qb;
-      attn_item(a, item, bh, qb);
-      const int p = bh * a.nqb + qb;
-      const int j0 = __ldg(&a.row_ptr[p]);
-      const int n = __ldg(&a.row_ptr[p + 1]) - j0;
-      __nv_bfloat16* orow = a.O + (static_cast<int64_t>(bh) * a.S + qb * kAttnBlk + r) * kAttnD;
-      if (n <= 0) {
+      int bh;
+      AttnStream A, B;
+      attn_item(a, item, bh, A, B);
+      const AttnStream st = x == 0 ? A : B;
+      if (st.qb < 0) continue;
+      __nv_bfloat16* orow = a.O + (static_cast<int64_t>(bh) * a.S + st.qb * kAttnBlk + r) * kAttnD;
+      if (st.n <= 0) {
         const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int c = 0; c < 16; ++c) reinterpret_cast<uint4*>(orow)[c] = z;
+        for (int cc = 0; cc < 16; ++cc) reinterpret_cast<uint4*>(orow)[cc] = z;
         continue;
       }
-      float m_run = -INFINITY, l_run = 0.0f;
-      for (int jj = 0; jj < n; ++jj) {
-        const int kb = __ldg(&a.col_idx[j0 + jj]);
-        const bool diag = a.causal_diag && kb == qb;
-        const uint32_t sb = s_cnt & 1;
-        ok = warp_wait_bounded(ptx::smem_u32(&s_full[sb]), (s_cnt >> 1) & 1, ctl, 20);
+      float m_run = -INFINITY, l_run = 0.0f;  // m_run in scaled log2 units
+      for (int j = 0; j < st.n; ++j) {
+        const int kb = __ldg(&a.col_idx[st.j0 + j]);
+        const bool diag = a.causal_diag && kb == st.qb;
+        // S_j complete; it was issued after PV_{j-1}, so O already holds block j-1's contribution.
+        ok = warp_wait_bounded(ptx::smem_u32(&s_full[x]), s_cnt & 1, ctl, 20);
         if (!ok) break;
-        ptx::tc_fence_after();
-        float x[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          uint32_t v[32];
-          ptx::tmem_ld_32x32b_x32(tmem_base + sb * 128 + lane_off + c * 32, v);
-          ptx::tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) x[c * 32 + i] = __uint_as_float(v[i]) * a.scale_log2;
-        }
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&s_empty[sb]));
         ++s_cnt;
-        float mb = -INFINITY;
+        ptx::tc_fence_after();
+        uint32_t sv[128];  // S row, loaded straight into the registers the softmax works in
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          if (diag && i > r) x[i] = -INFINITY;
-          mb = fmaxf(mb, x[i]);
+        for (int cc = 0; cc < 4; ++cc)
+          ptx::tmem_ld_32x32b_x32(tS + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[cc * 32]));
+        ptx::tmem_wait_ld();
+        float* v = reinterpret_cast<float*>(sv);
+        if (diag) {
+#pragma unroll
+          for (int i = 0; i < 128; ++i)
+            if (i > r) v[i] = -INFINITY;
         }
-        // Move the reference max only when this block raises it by more than 8.
-        const bool move = mb > m_run + 8.0f;
-        const float m_new = move ? mb : m_run;
+        // Row max and row sum as 8 independent partial chains (a single chain is 127 dependent ops deep).
+        float pm[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) pm[k] = v[k];
+#pragma unroll
+        for (int i = 8; i < 128; ++i) pm[i & 7] = fmaxf(pm[i & 7], v[i]);
+        const float mb = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+        const float mbs = mb * c;
+        const bool move = mbs > m_run + 8.0f;
         float alpha = 1.0f;
-        if (move) alpha = (m_run == -INFINITY) ? 0.0f : ex2_approx(m_run - m_new);
-        const bool need_rescale = __any_sync(0xffffffffu, move && jj > 0);
-        const float m_sub = (m_new == -INFINITY) ? 0.0f : m_new;  // fully masked so far: P = 0, no NaN
-        float rs = 0.0f;
+        if (move) alpha = (m_run == -INFINITY) ? 0.0f : ex2_approx(m_run - mbs);
+        if (move) m_run = mbs;
+        const bool need_rescale = __any_sync(0xffffffffu, move && j > 0);
+        const float m_sub = (m_run == -INFINITY) ? 0.0f : m_run;  // fully masked so far: P = 0, no NaN
+        float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+        // P packed to bf16 pairs in place: pair k lands in sv[k], whose S value (element k <= i) is already used.
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-          x[i] = ex2_approx(x[i] - m_sub);
-          rs += x[i];
+        for (int i = 0; i < 128; i += 2) {
+          const float t0 = fmaf(v[i], c, -m_sub), t1 = fmaf(v[i + 1], c, -m_sub);
+          const float e0 = ex2_approx(t0);
+          const float e1 = (i & 3) == 2 ? ex2_poly(t1) : ex2_approx(t1);
+          ps[i & 7] += e0;
+          ps[(i + 1) & 7] += e1;
+          sv[i >> 1] = pack_bf16(e0, e1);
         }
+        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
         l_run = l_run * alpha + rs;
-        m_run = m_new;
-        // P shared memory and O are free once the previous PV has completed.
-        if (jj > 0) {
-          ok = warp_wait_bounded(ptx::smem_u32(pv_done), pv_cnt & 1, ctl, 21);
-          if (!ok) break;
-          ++pv_cnt;
-          ptx::tc_fence_after();
-          if (need_rescale) {
-            const float al = move ? alpha : 1.0f;
+        if (need_rescale) {  // O (complete through block j-1) *= alpha, in TMEM
+          const float al = move ? alpha : 1.0f;
 #pragma unroll 1
-            for (int c = 0; c < 4; ++c) {
-              uint32_t v[32];
-              ptx::tmem_ld_32x32b_x32(tO + c * 32, v);
-              ptx::tmem_wait_ld();
+          for (int cc = 0; cc < 4; ++cc) {
+            uint32_t u[32];
+            ptx::tmem_ld_32x32b_x32(tO + cc * 32, u);
+            ptx::tmem_wait_ld();
 #pragma unroll
-              for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * al);
-              ptx::tmem_st_32x32b_x32(tO + c * 32, v);
-            }
-            ptx::tmem_wait_st();
+            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * al);
+            ptx::tmem_st_32x32b_x32(tO + cc * 32, u);
           }
         }
-        // P row r -> shared memory, K-major, 128-B swizzle: 16-B chunk ch of a 128-B row lands at ch ^ (r & 7).
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const uint32_t rowbase = sPa + half * kAttnChunk + r * 128;
-#pragma unroll
-          for (int ch = 0; ch < 8; ++ch) {
-            const float* xs = &x[half * 64 + ch * 8];
-            st_shared_v4(rowbase + ((ch ^ (r & 7)) << 4), pack_bf16(xs[0], xs[1]), pack_bf16(xs[2], xs[3]),
-                         pack_bf16(xs[4], xs[5]), pack_bf16(xs[6], xs[7]));
-          }
-        }
-        ptx::fence_proxy_async_smem();
+        // P row r (bf16 pairs) -> TMEM columns [0, 64) of this stream's S buffer.
+        ptx::tmem_st_32x32b_x32(tS, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        ptx::tmem_st_32x32b_x32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(p_full));
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&p_full[x]));
       }
       if (!ok) break;
       // Output: wait for the last PV of this row, then O / l -> bf16.
-      ok = warp_wait_bounded(ptx::smem_u32(pv_done), pv_cnt & 1, ctl, 22);
+      ok = warp_wait_bounded<false, 256>(ptx::smem_u32(&o_done[x]), o_cnt & 1, ctl, 22);
       if (!ok) break;
-      ++pv_cnt;
+      ++o_cnt;
       ptx::tc_fence_after();
       const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
 #pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        uint32_t v[32];
-        ptx::tmem_ld_32x32b_x32(tO + c * 32, v);
+      for (int cc = 0; cc < 4; ++cc) {
+        uint32_t u[32];
+        ptx::tmem_ld_32x32b_x32(tO + cc * 32, u);
         ptx::tmem_wait_ld();
-        uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+        uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          dst[g] = make_uint4(pack_bf16(__uint_as_float(v[8 * g + 0]) * inv_l, __uint_as_float(v[8 * g + 1]) * inv_l),
-                              pack_bf16(__uint_as_float(v[8 * g + 2]) * inv_l, __uint_as_float(v[8 * g + 3]) * inv_l),
-                              pack_bf16(__uint_as_float(v[8 * g + 4]) * inv_l, __uint_as_float(v[8 * g + 5]) * inv_l),
-                              pack_bf16(__uint_as_float(v[8 * g + 6]) * inv_l, __uint_as_float(v[8 * g + 7]) * inv_l));
+          dst[g] = make_uint4(pack_bf16(__uint_as_float(u[8 * g + 0]) * inv_l, __uint_as_float(u[8 * g + 1]) * inv_l),
+                              pack_bf16(__uint_as_float(u[8 * g + 2]) * inv_l, __uint_as_float(u[8 * g + 3]) * inv_l),
+                              pack_bf16(__uint_as_float(u[8 * g + 4]) * inv_l, __uint_as_float(u[8 * g + 5]) * inv_l),
+                              pack_bf16(__uint_as_float(u[8 * g + 6]) * inv_l, __uint_as_float(u[8 * g + 7]) * inv_l));
         }
       }
       ptx::tc_fence_before();

@@ -464,8 +464,9 @@ int bsk_bsattn_fwd_bf16(const void* Q, const void* K, const void* V, void* O, co
   a.col_idx = col_idx;
   a.S = S;
   a.nqb = S / blk;
+  a.items_per_pair = (a.nqb + 1) / 2;
   a.bh_begin = bh_begin;
-  a.num_items = (bh_end - bh_begin) * a.nqb;
+  a.num_items = (bh_end - bh_begin) * a.items_per_pair;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.causal_diag = causal_diag;
   a.err = st->err_word;
