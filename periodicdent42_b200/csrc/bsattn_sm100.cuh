@@ -16,9 +16,9 @@
 // overlaps the other stream's tensor work. TMEM: S/P_A [0,128), S/P_B [128,256), O_A [256,384), O_B [384,512).
 //
 // Softmax: the reference max moves only when a block raises it by more than 8 (log2 units), so P <= 2^8 and
-// O is rescaled in TMEM only on those moves. exp2 runs on the MUFU for 3/4 of the elements and, for the
-// other 1/4, on the FMA pipe as a Cody-Waite split x = n + f with a cubic for 2^f on [0,1) (coefficients
-// fitted here by constrained minimax; max relative error 1.03e-4, p(0) = 1, p(1) = 2).
+// O is rescaled in TMEM only on those moves. Scale, sums and the polynomial use packed fp32x2 FMA/ADD; row
+// max uses three-input max. exp2 runs on the MUFU for 3/4 of the elements and on the FMA pipe for 1/4
+// (ex2_poly2 below), balancing the MUFU against instruction issue.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -88,17 +88,50 @@ __device__ __forceinline__ float ex2_approx(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe: x = n + f, n = floor(x), 2^f by the cubic above, 2^n added to the exponent field.
-__device__ __forceinline__ float ex2_poly(float x) {
-  const float xc = fmaxf(x, -126.0f);
-  const float fl = floorf(xc);
-  const float f = xc - fl;
-  float p = fmaf(0.078267968f, f, 0.226307680f);
-  p = fmaf(p, f, 0.695424352f);
-  p = fmaf(p, f, 1.0f);
-  const int e = static_cast<int>(fl);
-  const float r = __int_as_float(__float_as_int(p) + (e << 23));
-  return x < -126.0f ? 0.0f : r;
+// Packed fp32x2 helpers (sm_100 FMA pipe processes both halves in one instruction).
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair on the FMA pipe (Cody-Waite split, published FlashAttention-4 approach): x = n + f with
+// n = round(x) from the 1.5*2^23 magic addition, f in [-1/2, 1/2], 2^f by a cubic fitted here (constrained
+// minimax: 1 + 0.693282906 f + 0.242210542 f^2 + 0.055008705 f^3, max relative error 1.01e-4), and 2^n added
+// to the exponent field. Inputs below -125 are clamped (result ~2^-125; only masked elements get there).
+__device__ __forceinline__ void ex2_poly2(float x0, float x1, float& y0, float& y1) {
+  const uint64_t kMagic = f2_pack(12582912.0f, 12582912.0f);
+  const uint64_t kNegMagic = f2_pack(-12582912.0f, -12582912.0f);
+  const uint64_t xc = f2_pack(fmaxf(x0, -125.0f), fmaxf(x1, -125.0f));
+  const uint64_t xr = f2_add(xc, kMagic);        // n in the low mantissa bits
+  const uint64_t fl = f2_add(xr, kNegMagic);     // n as a float
+  const uint64_t f = f2_fma(fl, f2_pack(-1.0f, -1.0f), xc);
+  uint64_t p = f2_fma(f2_pack(0.055008705f, 0.055008705f), f, f2_pack(0.242210542f, 0.242210542f));
+  p = f2_fma(p, f, f2_pack(0.693282906f, 0.693282906f));
+  p = f2_fma(p, f, f2_pack(1.0f, 1.0f));
+  float p0, p1, r0, r1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(xr, r0, r1);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(r0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(r1) << 23));
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
@@ -359,9 +392,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int k = 0; k < 8; ++k) pm[k] = v[k];
 #pragma unroll
-        for (int i = 8; i < 128; ++i) pm[i & 7] = fmaxf(pm[i & 7], v[i]);
-        const float mb = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
-                               fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7])));
+        for (int i = 8; i < 128; i += 16)
+#pragma unroll
+          for (int k = 0; k < 8; ++k) pm[k] = max3f(pm[k], v[i + k], v[i + 8 + k]);
+        const float mb = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
         const float mbs = mb * c;
         const bool move = mbs > m_run + 8.0f;
         float alpha = 1.0f;
@@ -369,18 +403,30 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (move) m_run = mbs;
         const bool need_rescale = __any_sync(0xffffffffu, move && j > 0);
         const float m_sub = (m_run == -INFINITY) ? 0.0f : m_run;  // fully masked so far: P = 0, no NaN
-        float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        // P packed to bf16 pairs in place: pair k lands in sv[k], whose S value (element k <= i) is already used.
+        // exp2 on pairs: t = s * c - m by fma.f32x2; 3 of every 4 pairs on the MUFU, 1 on the FMA pipe.
+        // P is packed to bf16 pairs in place: pair k lands in sv[k], whose S value (element k <= i) is used.
+        const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(-m_sub, -m_sub);
+        uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
         for (int i = 0; i < 128; i += 2) {
-          const float t0 = fmaf(v[i], c, -m_sub), t1 = fmaf(v[i + 1], c, -m_sub);
-          const float e0 = ex2_approx(t0);
-          const float e1 = (i & 3) == 2 ? ex2_poly(t1) : ex2_approx(t1);
-          ps[i & 7] += e0;
-          ps[(i + 1) & 7] += e1;
+          float t0, t1, e0, e1;
+          f2_unpack(f2_fma(f2_pack(v[i], v[i + 1]), c2, nm2), t0, t1);
+          if ((i & 7) == 6) {
+            ex2_poly2(t0, t1, e0, e1);
+          } else {
+            e0 = ex2_approx(t0);
+            e1 = ex2_approx(t1);
+          }
+          acc[(i >> 1) & 3] = f2_add(acc[(i >> 1) & 3], f2_pack(e0, e1));
           sv[i >> 1] = pack_bf16(e0, e1);
         }
-        const float rs = ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+        float rs;
+        {
+          const uint64_t a01 = f2_add(acc[0], acc[1]), a23 = f2_add(acc[2], acc[3]);
+          float lo, hi;
+          f2_unpack(f2_add(a01, a23), lo, hi);
+          rs = lo + hi;
+        }
         l_run = l_run * alpha + rs;
         if (need_rescale) {  // O (complete through block j-1) *= alpha, in TMEM
           const float al = move ? alpha : 1.0f;
