@@ -68,6 +68,8 @@ class Ctx:
         self.stream = None
 
     def init_gpu(self):
+        # NCCL prints a version banner on stdout at INFO/VERSION level; the bench's stdout is one JSON line.
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
         torch.cuda.set_device(self.local_rank)
         self.dev = torch.device("cuda", self.local_rank)
         if self.world > 1:
