@@ -8,8 +8,9 @@
  *    thread-local message for the last failure on the calling thread.
  *  - Device pointers are borrowed; outputs are preallocated by the caller. Nothing is synchronised:
  *    work is enqueued on `stream` (a cudaStream_t, NULL = legacy default stream) of the current device.
- *  - Arguments are validated on the host before any launch (shapes, strides, 16-byte alignment needed
- *    by TMA, BSR index ranges when `check_indices` is requested through bsk_spmm_bsr_validate).
+ *  - Arguments are validated on the host before any launch (shapes, strides, the 16-byte alignment TMA
+ *    needs); BSR index structures in host memory can be checked with bsk_bsr_validate_host, and the kernels
+ *    clamp and flag out-of-range indices on the device.
  *  - Every device-side wait is bounded. A wait that runs out records a code in a per-device error word
  *    (read and cleared by bsk_device_error) and the kernel returns early with its output incomplete.
  *  - There is no CPU fallback: without a usable sm_100 device every compute entry point fails with
@@ -52,6 +53,22 @@ int bsk_device_sm_count(void);
  */
 int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc, int M, int N,
                     int K, int k_begin, int k_end, void* stream);
+
+/*
+ * Dense GEMM as bsk_gemm_f16f32 (k range = all of K) with the K dimension split across CTA pairs, for shapes
+ * whose output has too few 256 x 256 tiles to occupy the GPU (e.g. 1024 x 1024 with long K). Each split writes
+ * an fp32 partial slab into `workspace`; a second kernel sums the slabs in split order (deterministic) into C.
+ *   splits <= 0 : automatic (enough (tile, split) units for every CTA pair, >= 4 K stages per split, <= 32)
+ *   workspace   : device memory of at least bsk_gemm_splitk_workspace_bytes(M, N, K, splits) bytes, 16-byte
+ *                 aligned; may be NULL when that size is 0 (no split chosen). Used as scratch by this call only.
+ * No reference counterpart (the reference's GEMM programs, BlackwellSparseK/src/gemm_h100_*.cu, had no split-K).
+ */
+int bsk_gemm_f16f32_splitk(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc, int M,
+                           int N, int K, int splits, void* workspace, int64_t workspace_bytes, void* stream);
+
+/* Workspace bytes bsk_gemm_f16f32_splitk needs on the current device (0 if it would not split K), or a negative
+ * error code. */
+int64_t bsk_gemm_splitk_workspace_bytes(int M, int N, int K, int splits);
 
 /*
  * FP8 GEMM, e4m3 x e4m3 -> bf16:  D[M,N] = bf16( (A_q[M,K] * B_q[K,N]) * scale_a * scale_b ).

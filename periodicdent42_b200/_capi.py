@@ -32,6 +32,8 @@ SIGNATURES = {
     "bsk_last_error": (ctypes.c_char_p, []),
     "bsk_device_sm_count": (_i32, []),
     "bsk_gemm_f16f32": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "bsk_gemm_f16f32_splitk": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp]),
+    "bsk_gemm_splitk_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32]),
     "bsk_gemm_e4m3_bf16": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp]),
     "bsk_spmm_bsr_f16f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _i32, _i32, _i32,
                                    _i32, _i32, _vp]),
@@ -101,6 +103,28 @@ def gemm_f16f32(A, Bt, C, k_begin: int = 0, k_end: int | None = None, stream=Non
     k_end = K if k_end is None else k_end
     check(lib().bsk_gemm_f16f32(_ptr(A), A.stride(0), _ptr(Bt), Bt.stride(0), _ptr(C), C.stride(0), M, N, K,
                                 k_begin, k_end, _stream(stream)), "bsk_gemm_f16f32")
+
+
+def gemm_splitk_workspace_bytes(M: int, N: int, K: int, splits: int = 0) -> int:
+    n = lib().bsk_gemm_splitk_workspace_bytes(M, N, K, splits)
+    if n < 0:
+        raise BskError(n, "bsk_gemm_splitk_workspace_bytes", last_error())
+    return n
+
+
+def gemm_f16f32_splitk(A, Bt, C, splits: int = 0, workspace=None, stream=None) -> None:
+    """C = A @ B with K split across CTA pairs; `workspace` (a CUDA tensor) defaults to a fresh uint8 buffer of
+    the queried size."""
+    import torch
+
+    M, K = A.shape
+    N = Bt.shape[0]
+    need = gemm_splitk_workspace_bytes(M, N, K, splits)
+    if workspace is None and need > 0:
+        workspace = torch.empty(need, dtype=torch.uint8, device=A.device)
+    nbytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
+    check(lib().bsk_gemm_f16f32_splitk(_ptr(A), A.stride(0), _ptr(Bt), Bt.stride(0), _ptr(C), C.stride(0), M, N, K,
+                                       splits, _ptr(workspace), nbytes, _stream(stream)), "bsk_gemm_f16f32_splitk")
 
 
 def gemm_e4m3_bf16(Aq, Bqt, scale_a, scale_b, D, stream=None) -> None:

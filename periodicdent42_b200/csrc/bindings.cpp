@@ -74,6 +74,26 @@ torch::Tensor gemm_f16f32(torch::Tensor A, torch::Tensor Bt, int64_t k_begin, in
   return C;
 }
 
+// C = A @ B with K split across CTA pairs (workspace from torch's caching allocator); splits <= 0: automatic.
+torch::Tensor gemm_f16f32_splitk(torch::Tensor A, torch::Tensor Bt, int64_t splits) {
+  TORCH_CHECK(A.is_cuda() && Bt.is_cuda(), "gemm_f16f32_splitk: CUDA tensors required");
+  TORCH_CHECK(A.scalar_type() == torch::kFloat16 && Bt.scalar_type() == torch::kFloat16, "gemm_f16f32_splitk: float16 inputs");
+  TORCH_CHECK(A.dim() == 2 && Bt.dim() == 2 && A.size(1) == Bt.size(1), "gemm_f16f32_splitk: A [M,K] and Bt [N,K] expected");
+  TORCH_CHECK(A.stride(1) == 1 && Bt.stride(1) == 1, "gemm_f16f32_splitk: inner dimension must be contiguous");
+  const at::cuda::CUDAGuard guard(A.device());
+  const int64_t M = A.size(0), K = A.size(1), N = Bt.size(0);
+  const int64_t need = bsk_gemm_splitk_workspace_bytes(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K),
+                                                       static_cast<int>(splits));
+  TORCH_CHECK(need >= 0, "bsk_gemm_splitk_workspace_bytes failed: ", bsk_last_error());
+  auto ws = torch::empty({need > 0 ? need : 1}, A.options().dtype(torch::kUInt8));
+  auto C = torch::empty({M, N}, A.options().dtype(torch::kFloat32));
+  check_rc(bsk_gemm_f16f32_splitk(A.data_ptr(), A.stride(0), Bt.data_ptr(), Bt.stride(0), C.data_ptr<float>(), N,
+                                  static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), static_cast<int>(splits),
+                                  ws.data_ptr(), need, stream_of(C)),
+           "bsk_gemm_f16f32_splitk");
+  return C;
+}
+
 // D (bf16) = (Aq @ Bq) * scale_a * scale_b, Aq e4m3 [M, K], Bq given as Bqt e4m3 [N, K].
 torch::Tensor gemm_e4m3(torch::Tensor Aq, torch::Tensor Bqt, torch::Tensor scale_a, torch::Tensor scale_b) {
   TORCH_CHECK(Aq.is_cuda() && Bqt.is_cuda() && scale_a.is_cuda() && scale_b.is_cuda(), "gemm_e4m3: CUDA tensors required");
@@ -133,6 +153,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("K"), py::arg("BM") = 256, py::arg("BN") = 128, py::arg("BK") = 32);
   m.def("gemm_f16f32", &gemm_f16f32, "fp16 x fp16 -> fp32 GEMM (sm_100a)", py::arg("A"), py::arg("Bt"),
         py::arg("k_begin") = 0, py::arg("k_end") = -1);
+  m.def("gemm_f16f32_splitk", &gemm_f16f32_splitk, "fp16 x fp16 -> fp32 GEMM with split K (sm_100a)", py::arg("A"),
+        py::arg("Bt"), py::arg("splits") = 0);
   m.def("gemm_e4m3", &gemm_e4m3, "e4m3 x e4m3 -> bf16 GEMM with per-tensor scales (sm_100a)", py::arg("Aq"),
         py::arg("Bqt"), py::arg("scale_a"), py::arg("scale_b"));
   m.def("bsattn_fwd", &bsattn_fwd, "block-sparse attention forward (sm_100a)", py::arg("Q"), py::arg("K"),

@@ -277,6 +277,8 @@ int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, floa
   a.num_n_tiles = (N + tn - 1) / tn;
   a.num_k_blocks = (kr + 63) / 64;
   a.group_m = pick_group_m(a.num_m_tiles, kind);
+  a.k_splits = 1;
+  a.kb_per_split = a.num_k_blocks;
   a.out = C;
   a.ldo = ldc;
   a.vec_ok = aligned16(C) && (ldc % 4 == 0);
@@ -323,6 +325,8 @@ int bsk_gemm_e4m3_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, c
   a.num_n_tiles = (N + tn - 1) / tn;
   a.num_k_blocks = (K + 127) / 128;
   a.group_m = pick_group_m(a.num_m_tiles, kind);
+  a.k_splits = 1;
+  a.kb_per_split = a.num_k_blocks;
   a.out = D;
   a.ldo = ldd;
   a.vec_ok = aligned16(D) && (ldd % 8 == 0);
@@ -341,6 +345,125 @@ int bsk_gemm_e4m3_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, c
     gemm_sm100_kernel<1, Mainloop::Dense, Epi::BF16Scaled><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
   }
   return launch_status("gemm_e4m3 launch");
+}
+
+}  // extern "C"
+
+namespace {
+
+struct SplitPlan {
+  int kind;          // 1: pair 256x256, 2: pair 256x512
+  int splits;        // K splits per tile (1 = no split)
+  int kb_per_split;  // 64-element K stages per split
+  int64_t ld_ws;     // row stride of a partial slab (elements)
+};
+
+// K splits for an fp16 GEMM of the given shape: enough (tile, split) units to occupy every co-resident CTA
+// pair, each split at least 4 K stages, at most 32 splits.
+SplitPlan plan_splitk(const DeviceState& st, int M, int N, int kr, int splits_req) {
+  SplitPlan p{};
+  const int nkb = (kr + 63) / 64;
+  const int tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  int s = splits_req;
+  if (s <= 0) {
+    s = tiles >= st.pair_clusters ? 1 : st.pair_clusters / tiles;
+    const int cap = nkb / 4 > 1 ? nkb / 4 : 1;
+    s = s < cap ? s : cap;
+    s = s < 32 ? s : 32;
+  }
+  s = s < 1 ? 1 : (s > nkb ? nkb : s);
+  p.kb_per_split = (nkb + s - 1) / s;
+  p.splits = (nkb + p.kb_per_split - 1) / p.kb_per_split;  // every split non-empty
+  p.kind = (N >= 512 && p.kb_per_split * 64 >= 8192) ? 2 : 1;
+  p.ld_ws = (static_cast<int64_t>(N) + 3) / 4 * 4;
+  return p;
+}
+
+// One CTA-pair launch over (tile, split) units writing fp32 partial slabs (or C when splits == 1).
+int launch_pair_f16(const DeviceState& st, const SplitPlan& p, const __half* Ah, int64_t lda, const __half* Bh,
+                    int64_t ldb, int M, int N, int kr, float* out, int64_t ldo, int64_t split_stride,
+                    cudaStream_t s) {
+  using namespace bsk;
+  CUtensorMap ta, tb;
+  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Ah, kr, M, lda * 2, 64, 128, "A")) return rc;
+  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Bh, kr, N, ldb * 2, 64, 128, "B")) return rc;
+  GemmArgs a{};
+  const int tn = p.kind == 2 ? 512 : 256;
+  a.M = M;
+  a.N = N;
+  a.num_m_tiles = (M + kPairBM - 1) / kPairBM;
+  a.num_n_tiles = (N + tn - 1) / tn;
+  a.num_k_blocks = (kr + 63) / 64;
+  a.group_m = pick_group_m(a.num_m_tiles, p.kind);
+  a.k_splits = p.splits;
+  a.kb_per_split = p.kb_per_split;
+  a.split_stride = split_stride;
+  a.out = out;
+  a.ldo = ldo;
+  a.vec_ok = aligned16(out) && (ldo % 4 == 0);
+  a.err = st.err_word;
+  a.timeout_ns = t_timeout_ns;
+  const int units = a.num_m_tiles * a.num_n_tiles * a.k_splits;
+  const int clusters = units < st.pair_clusters ? units : st.pair_clusters;
+  if (p.kind == 2)
+    gemm_pair_sm100_kernel<2, Epi::F32, 2><<<2 * clusters, kPairThreads, kPairWideSmemBytes, s>>>(ta, tb, a);
+  else
+    gemm_pair_sm100_kernel<2, Epi::F32, 1><<<2 * clusters, kPairThreads, kPairSmemBytes, s>>>(ta, tb, a);
+  return launch_status("gemm split-K launch");
+}
+
+int splitk_reduce(const DeviceState& st, const float* ws, const SplitPlan& p, float* C, int64_t ldc, int M, int N,
+                  cudaStream_t s) {
+  const int64_t groups = static_cast<int64_t>(M) * ((N + 3) / 4);
+  int64_t blocks = (groups + 255) / 256;
+  const int64_t cap = static_cast<int64_t>(st.sm_count) * 8;
+  blocks = blocks < cap ? blocks : cap;
+  bsk::splitk_reduce_kernel<<<static_cast<int>(blocks), 256, 0, s>>>(
+      ws, p.splits, static_cast<int64_t>(M) * p.ld_ws, p.ld_ws, C, ldc, M, N, aligned16(C) && (ldc % 4 == 0));
+  return launch_status("split-K reduce launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int64_t bsk_gemm_splitk_workspace_bytes(int M, int N, int K, int splits) {
+  if (M < 0 || N < 0 || K < 0) return set_error(BSK_ERR_INVALID_ARG, "splitk workspace: negative extent");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  if (M == 0 || N == 0 || K == 0) return 0;
+  const SplitPlan p = plan_splitk(*st, M, N, K, splits);
+  return p.splits <= 1 ? 0 : static_cast<int64_t>(p.splits) * M * p.ld_ws * static_cast<int64_t>(sizeof(float));
+}
+
+int bsk_gemm_f16f32_splitk(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc, int M,
+                           int N, int K, int splits, void* workspace, int64_t workspace_bytes, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return set_error(BSK_ERR_INVALID_ARG, "gemm_splitk: negative extent");
+  if (lda < K || ldb < K || ldc < N)
+    return set_error(BSK_ERR_INVALID_ARG, "gemm_splitk: leading dimensions smaller than the extents");
+  if (lda % 8 || ldb % 8) return set_error(BSK_ERR_INVALID_ARG, "gemm_splitk: lda and ldb must be multiples of 8");
+  if (!A || !B || !C) return set_error(BSK_ERR_INVALID_ARG, "gemm_splitk: null pointer");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  if (M == 0 || N == 0) return BSK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0) {
+    cudaError_t e = cudaMemset2DAsync(C, ldc * sizeof(float), 0, (size_t)N * sizeof(float), M, s);
+    return e == cudaSuccess ? BSK_OK : cuda_fail(e, "gemm_splitk: zero fill");
+  }
+  const SplitPlan p = plan_splitk(*st, M, N, K, splits);
+  const __half* Ah = static_cast<const __half*>(A);
+  const __half* Bh = static_cast<const __half*>(B);
+  if (p.splits <= 1) return launch_pair_f16(*st, p, Ah, lda, Bh, ldb, M, N, K, C, ldc, 0, s);
+  const int64_t need = static_cast<int64_t>(p.splits) * M * p.ld_ws * static_cast<int64_t>(sizeof(float));
+  if (!workspace || workspace_bytes < need)
+    return set_error(BSK_ERR_INVALID_ARG, "gemm_splitk: workspace of %lld bytes needed (%d splits), %lld given",
+                     (long long)need, p.splits, (long long)workspace_bytes);
+  if (!aligned16(workspace)) return set_error(BSK_ERR_INVALID_ARG, "gemm_splitk: workspace must be 16-byte aligned");
+  float* ws = static_cast<float*>(workspace);
+  if (int rc = launch_pair_f16(*st, p, Ah, lda, Bh, ldb, M, N, K, ws, p.ld_ws, static_cast<int64_t>(M) * p.ld_ws, s))
+    return rc;
+  return splitk_reduce(*st, ws, p, C, ldc, M, N, s);
 }
 
 int bsk_bsr_validate_host(const int32_t* row_ptr, const int32_t* col_idx, int Mb, int Kb, int nnzb) {
@@ -397,6 +520,8 @@ int bsk_spmm_bsr_f16f32(const int32_t* row_ptr, const int32_t* col_idx, const vo
   a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
   a.num_k_blocks = 0;
   a.group_m = pick_group_m(a.num_m_tiles);
+  a.k_splits = 1;
+  a.kb_per_split = a.num_k_blocks;
   a.out = C;
   a.ldo = ldc;
   a.vec_ok = aligned16(C) && (ldc % 4 == 0);

@@ -112,7 +112,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
 
   WaitCtl ctl{abort_flag, a.err, a.timeout_ns, KID};
-  const int num_tiles = a.num_m_tiles * a.num_n_tiles;
+  // Work unit = (output tile, K split); the splits of one tile are adjacent units.
+  const int num_units = a.num_m_tiles * a.num_n_tiles * a.k_splits;
+  auto unit_coords = [&](int unit, int& mt, int& nt, int& kb0, int& kb1) {
+    gemm_tile_coords(unit / a.k_splits, a, mt, nt);
+    kb0 = (unit % a.k_splits) * a.kb_per_split;
+    kb1 = min(a.num_k_blocks, kb0 + a.kb_per_split);
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (both CTAs, one thread)
@@ -122,12 +128,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       const uint32_t sA0 = ptx::smem_u32(sA), sB0 = ptx::smem_u32(sB);
       const uint32_t full0 = ptx::smem_u32(full), empty0 = ptx::smem_u32(empty);
       const uint32_t full0_leader = ptx::mapa_shared(full0, 0);
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
-        int mt, nt;
-        gemm_tile_coords(tile, a, mt, nt);
+      for (int unit = pair; unit < num_units && ok; unit += npairs) {
+        int mt, nt, kb0, kb1;
+        unit_coords(unit, mt, nt, kb0, kb1);
         const int m_row = mt * kPairBM + static_cast<int>(rank) * 128;
         const int n_row = nt * kTileN + static_cast<int>(rank) * 128;
-        for (int kb = 0; kb < a.num_k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           ok = wait_bounded<true, BSK_PROD_SLEEP_NS>(empty0 + stage * 8, phase ^ 1, ctl, 1);
           if (!ok) break;
           if (rank == 0) ptx::mbar_arrive_expect_tx(full0 + stage * 8, PAIR_TX);
@@ -164,12 +170,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       // Descriptors differ only in the start-address field: build them once and add the offset (>> 4).
       const uint64_t adesc0 = ptx::smem_desc(ptx::smem_u32(sA), 16, 1024);
       const uint64_t bdesc0 = ptx::smem_desc(ptx::smem_u32(sB), 16, 1024);
-      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+      for (int unit = pair; unit < num_units && ok; unit += npairs) {
+        int mt, nt, kb0, kb1;
+        unit_coords(unit, mt, nt, kb0, kb1);
         ok = wait_bounded<true, BSK_MMA_SLEEP_NS>(tempty0 + acc * 8, acc_phase ^ 1, ctl, 3);
         if (!ok) break;
         ptx::tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * 256;
-        for (int kb = 0; kb < a.num_k_blocks; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           ok = wait_bounded<true, BSK_MMA_SLEEP_NS>(full0 + stage * 8, phase, ctl, 4);
           if (!ok) break;
           ptx::tc_fence_after();
@@ -180,10 +188,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
 #pragma unroll
             for (int h = 0; h < kNHalves; ++h) {  // N half h accumulates in TMEM columns [256 h, 256 h + 256)
               const uint64_t bdh = bd + ((h * 128 * 128) >> 4) + k * 2;
+              const uint32_t accum = (kb != kb0 || k != 0) ? 1u : 0u;
               if constexpr (kElemBytes == 1)
-                ptx::mma_f8_pair(d_tmem + 256 * h, ad + k * 2, bdh, IDESC, (kb | k) != 0);
+                ptx::mma_f8_pair(d_tmem + 256 * h, ad + k * 2, bdh, IDESC, accum);
               else
-                ptx::mma_f16_pair(d_tmem + 256 * h, ad + k * 2, bdh, IDESC, (kb | k) != 0);
+                ptx::mma_f16_pair(d_tmem + 256 * h, ad + k * 2, bdh, IDESC, accum);
             }
           }
           ptx::mma_commit_pair(empty0 + stage * 8);
@@ -208,9 +217,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     uint32_t acc = 0, acc_phase = 0;
     float scale = 1.0f;
     if constexpr (kEpi == Epi::BF16Scaled) scale = __ldg(a.scale_a) * __ldg(a.scale_b);
-    for (int tile = pair; tile < num_tiles; tile += npairs) {
-      int mt, nt;
-      gemm_tile_coords(tile, a, mt, nt);
+    for (int unit = pair; unit < num_units; unit += npairs) {
+      int mt, nt, kb0, kb1;
+      unit_coords(unit, mt, nt, kb0, kb1);
+      const int split = unit % a.k_splits;
       const int n0 = nt * kTileN;
       if (!warp_wait_bounded<true, BSK_EPI_SLEEP_NS>(ptx::smem_u32(&tfull[acc]), acc_phase, ctl, 6)) break;
       ptx::tc_fence_after();
@@ -226,7 +236,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         const int col0 = n0 + c;
         if (row_ok) {
           if constexpr (kEpi == Epi::F32) {
-            float* dst = reinterpret_cast<float*>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
+            float* dst = reinterpret_cast<float*>(a.out) + split * a.split_stride + static_cast<int64_t>(row) * a.ldo +
+                         col0;
             if (a.vec_ok && col0 + 32 <= a.N) {
 #pragma unroll
               for (int v = 0; v < 8; ++v)
@@ -271,6 +282,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   ptx::cluster_sync();  // no CTA leaves while its peer may still read its shared memory or signal its barriers
   ptx::tc_fence_after();
   if (warp == 1) ptx::tmem_dealloc_pair(tmem_base, kPairTmemCols);
+}
+
+// Split-K reduction: C[row, col] = sum over s of ws[s][row][col], added in split order (deterministic).
+// ws slabs are [M, ld_ws] fp32 with ld_ws a multiple of 4 and 16-byte aligned rows.
+__global__ void __launch_bounds__(256) splitk_reduce_kernel(const float* __restrict__ ws, int splits,
+                                                            int64_t split_stride, int64_t ld_ws,
+                                                            float* __restrict__ C, int64_t ldc, int M, int N,
+                                                            int vec_ok) {
+  const int groups = (N + 3) / 4;
+  const int64_t total = static_cast<int64_t>(M) * groups;
+  for (int64_t g = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; g < total;
+       g += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int row = static_cast<int>(g / groups);
+    const int c4 = static_cast<int>(g % groups) * 4;
+    const float* src = ws + static_cast<int64_t>(row) * ld_ws + c4;
+    float4 acc = *reinterpret_cast<const float4*>(src);
+    for (int sidx = 1; sidx < splits; ++sidx) {
+      const float4 v = *reinterpret_cast<const float4*>(src + sidx * split_stride);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    float* dst = C + static_cast<int64_t>(row) * ldc + c4;
+    if (vec_ok && c4 + 4 <= N) {
+      *reinterpret_cast<float4*>(dst) = acc;
+    } else {
+      const float vals[4] = {acc.x, acc.y, acc.z, acc.w};
+      for (int i = 0; i < 4 && c4 + i < N; ++i) dst[i] = vals[i];
+    }
+  }
 }
 
 }  // namespace bsk

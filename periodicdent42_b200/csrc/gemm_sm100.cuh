@@ -50,6 +50,9 @@ struct GemmArgs {
   int row_begin;             // BSR only: first block-row of this launch
   int nnzb;                  // BSR only: number of nonzero blocks (clamp for row_ptr)
   int kb_count;              // BSR only: number of block-columns (K / 128)
+  int k_splits;              // CTA-pair kernels: K splits per output tile (1 = none)
+  int kb_per_split;          // K stages per split (every split non-empty)
+  int64_t split_stride;      // elements between the partial-output slabs of consecutive splits
   uint32_t* err;
   uint64_t timeout_ns;
 };

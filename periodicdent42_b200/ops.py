@@ -146,10 +146,13 @@ def sparse_mm_benchmark(A: torch.Tensor, B: torch.Tensor,
 
 
 # ----------------------------------------------------------------------------------------- dense GEMM
-def gemm(A: torch.Tensor, B: torch.Tensor, out_dtype: torch.dtype = torch.float32, k_range=None) -> torch.Tensor:
+def gemm(A: torch.Tensor, B: torch.Tensor, out_dtype: torch.dtype = torch.float32, k_range=None,
+         split_k: Optional[int] = None) -> torch.Tensor:
     """C = A @ B, fp16 inputs, fp32 output. A [M, K] row-major; B [K, N], column-major preferred
     (``B = Bt.t()`` with Bt contiguous costs nothing; a row-major B is transposed once). ``k_range``
-    = (k_begin, k_end) restricts the contraction (split-K shards)."""
+    = (k_begin, k_end) restricts the contraction (split-K shards across ranks). ``split_k``: None = one pass;
+    0 = split K across CTA pairs automatically when the output has too few tiles to fill the GPU; n > 0 =
+    n splits (partials in a torch-allocated workspace, summed deterministically)."""
     _check_cuda_f16(A, B)
     if out_dtype != torch.float32:
         raise ValueError("gemm computes fp16 x fp16 -> fp32; out_dtype must be torch.float32")
@@ -158,6 +161,10 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out_dtype: torch.dtype = torch.float3
     A = A if A.stride(1) == 1 else A.contiguous()
     Bt = B.t()
     Bt = Bt if Bt.stride(1) == 1 else Bt.contiguous()
+    if split_k is not None:
+        if k_range is not None:
+            raise ValueError("gemm: k_range and split_k are exclusive")
+        return _C().gemm_f16f32_splitk(A, Bt, int(split_k))
     kb, ke = (0, -1) if k_range is None else k_range
     return _C().gemm_f16f32(A, Bt, kb, ke)
 
