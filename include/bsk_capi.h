@@ -71,6 +71,21 @@ int bsk_gemm_f16f32_splitk(const void* A, int64_t lda, const void* B, int64_t ld
 int64_t bsk_gemm_splitk_workspace_bytes(int M, int N, int K, int splits);
 
 /*
+ * bsk_gemm_f16f32_splitk for callers that cannot allocate device memory -- code bound to a fixed C signature
+ * with no workspace argument (an FFI stub or plugin interface), or running where device allocation is not
+ * permitted or is owned by another allocator. It allocates nothing: the split partials go to a static device
+ * array of 32 MiB built into this library (every GPU that loads the library holds it until exit).
+ *   - splits * M * round_up(N, 4) * 4 bytes must fit in 32 MiB, else BSK_ERR_INVALID_ARG with a message
+ *     (e.g. 1024 x 1024 with up to 8 splits).
+ *   - The first call on each device looks up the array's device address (cudaGetSymbolAddress); make that
+ *     first call on a device before any stream capture.
+ *   - All calls share the array: calls that overlap on the GPU (other streams, other threads) race on it.
+ * No counterpart in the reference.
+ */
+int bsk_gemm_f16f32_splitk_static(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc,
+                                  int M, int N, int K, int splits, void* stream);
+
+/*
  * FP8 GEMM, e4m3 x e4m3 -> bf16:  D[M,N] = bf16( (A_q[M,K] * B_q[K,N]) * scale_a * scale_b ).
  *   A   : e4m3 bytes, row-major [M, K] (lda multiple of 16)
  *   B   : e4m3 bytes, column-major [K, N] (B^T row-major [N, K], ldb multiple of 16)

@@ -34,6 +34,7 @@ SIGNATURES = {
     "bsk_gemm_f16f32": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp]),
     "bsk_gemm_f16f32_splitk": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp]),
     "bsk_gemm_splitk_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32]),
+    "bsk_gemm_f16f32_splitk_static": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp]),
     "bsk_gemm_e4m3_bf16": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp]),
     "bsk_spmm_bsr_f16f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _i32, _i32, _i32,
                                    _i32, _i32, _vp]),
@@ -125,6 +126,15 @@ def gemm_f16f32_splitk(A, Bt, C, splits: int = 0, workspace=None, stream=None) -
     nbytes = 0 if workspace is None else workspace.numel() * workspace.element_size()
     check(lib().bsk_gemm_f16f32_splitk(_ptr(A), A.stride(0), _ptr(Bt), Bt.stride(0), _ptr(C), C.stride(0), M, N, K,
                                        splits, _ptr(workspace), nbytes, _stream(stream)), "bsk_gemm_f16f32_splitk")
+
+
+def gemm_f16f32_splitk_static(A, Bt, C, splits: int = 0, stream=None) -> None:
+    """Split-K GEMM that allocates nothing: the partials live in the library's static 32 MiB device array
+    (for callers that cannot allocate device memory). Concurrent calls on the GPU race on that array."""
+    M, K = A.shape
+    N = Bt.shape[0]
+    check(lib().bsk_gemm_f16f32_splitk_static(_ptr(A), A.stride(0), _ptr(Bt), Bt.stride(0), _ptr(C), C.stride(0), M,
+                                              N, K, splits, _stream(stream)), "bsk_gemm_f16f32_splitk_static")
 
 
 def gemm_e4m3_bf16(Aq, Bqt, scale_a, scale_b, D, stream=None) -> None:

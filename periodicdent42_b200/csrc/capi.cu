@@ -466,6 +466,68 @@ int bsk_gemm_f16f32_splitk(const void* A, int64_t lda, const void* B, int64_t ld
   return splitk_reduce(*st, ws, p, C, ldc, M, N, s);
 }
 
+}  // extern "C"
+
+namespace {
+
+// Scratch of bsk_gemm_f16f32_splitk_static: the split-K partial slabs, for callers that cannot allocate device
+// memory. A fixed 32 MiB that every GPU which loads this library holds until the process exits. All calls
+// share it and it keeps the last call's contents; nothing in it has to start at zero (each call overwrites
+// every partial element it later reads).
+constexpr int64_t kStaticScratchBytes = 32ll << 20;
+static __device__ __align__(256) unsigned char g_bsk_static_scratch[kStaticScratchBytes];
+
+// Device address of g_bsk_static_scratch, looked up once per device (with that device current) on the first
+// call of bsk_gemm_f16f32_splitk_static there: in host code the array's name is only a host-side stand-in.
+struct StaticScratch {
+  std::once_flag once;
+  cudaError_t status = cudaSuccess;
+  void* ptr = nullptr;
+};
+StaticScratch g_static_scratch[kMaxDevices];
+
+}  // namespace
+
+extern "C" {
+
+int bsk_gemm_f16f32_splitk_static(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc,
+                                  int M, int N, int K, int splits, void* stream) {
+  if (M < 0 || N < 0 || K < 0) return set_error(BSK_ERR_INVALID_ARG, "gemm_splitk_static: negative extent");
+  if (lda < K || ldb < K || ldc < N)
+    return set_error(BSK_ERR_INVALID_ARG, "gemm_splitk_static: leading dimensions smaller than the extents");
+  if (lda % 8 || ldb % 8)
+    return set_error(BSK_ERR_INVALID_ARG, "gemm_splitk_static: lda and ldb must be multiples of 8");
+  if (!A || !B || !C) return set_error(BSK_ERR_INVALID_ARG, "gemm_splitk_static: null pointer");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "gemm_splitk_static: current device");
+  StaticScratch& sc = g_static_scratch[dev];
+  std::call_once(sc.once, [&] { sc.status = cudaGetSymbolAddress(&sc.ptr, g_bsk_static_scratch); });
+  if (sc.status != cudaSuccess) return cuda_fail(sc.status, "gemm_splitk_static: cudaGetSymbolAddress(scratch)");
+  if (M == 0 || N == 0) return BSK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0) {
+    e = cudaMemset2DAsync(C, ldc * sizeof(float), 0, (size_t)N * sizeof(float), M, s);
+    return e == cudaSuccess ? BSK_OK : cuda_fail(e, "gemm_splitk_static: zero fill");
+  }
+  const SplitPlan p = plan_splitk(*st, M, N, K, splits);
+  const __half* Ah = static_cast<const __half*>(A);
+  const __half* Bh = static_cast<const __half*>(B);
+  if (p.splits <= 1) return launch_pair_f16(*st, p, Ah, lda, Bh, ldb, M, N, K, C, ldc, 0, s);
+  const int64_t need = static_cast<int64_t>(p.splits) * M * p.ld_ws * static_cast<int64_t>(sizeof(float));
+  if (need > kStaticScratchBytes)
+    return set_error(BSK_ERR_INVALID_ARG,
+                     "gemm_splitk_static: %d splits of a %dx%d fp32 output need %lld bytes of scratch; the static "
+                     "scratch holds %lld (use fewer splits, or bsk_gemm_f16f32_splitk with a workspace)",
+                     p.splits, M, N, (long long)need, (long long)kStaticScratchBytes);
+  float* ws = static_cast<float*>(sc.ptr);
+  if (int rc = launch_pair_f16(*st, p, Ah, lda, Bh, ldb, M, N, K, ws, p.ld_ws, static_cast<int64_t>(M) * p.ld_ws, s))
+    return rc;
+  return splitk_reduce(*st, ws, p, C, ldc, M, N, s);
+}
+
 int bsk_bsr_validate_host(const int32_t* row_ptr, const int32_t* col_idx, int Mb, int Kb, int nnzb) {
   if (Mb < 0 || Kb < 0 || nnzb < 0) return set_error(BSK_ERR_INVALID_ARG, "bsr: negative extent");
   if (!row_ptr) return set_error(BSK_ERR_INVALID_ARG, "bsr: null row_ptr");
