@@ -49,7 +49,9 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--ops", default="dense,fp8,bsr,attn", help="comma list; dense is the headline")
-    p.add_argument("--dense-mode", choices=["nshard", "splitk"], default="nshard")
+    p.add_argument("--dense-mode", choices=["nshard", "splitk", "splitk_nccl"], default="nshard",
+                   help="nshard: N-sharded, no communication; splitk: K split across ranks, reduce-scatter fused "
+                        "into the GEMM (peer-memory epilogue); splitk_nccl: K split + NCCL reduce_scatter")
     p.add_argument("--shape", default=None, help="M,N,K override of the dense GEMM (profiling a small case)")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
@@ -243,7 +245,7 @@ def bench_dense(ctx: Ctx, args, res: dict):
             _capi.gemm_f16f32(A, Bt_r, C_r, stream=ctx.stream)
         launches = 1
         comm = None
-    else:
+    elif args.dense_mode == "splitk_nccl":
         k0, k1 = sharding.dense_ksplit(cfg.K, ctx.world, ctx.rank)
         Cp = torch.empty(cfg.M, cfg.N, device=ctx.dev)
         out = torch.empty(cfg.M // ctx.world, cfg.N, device=ctx.dev)
@@ -254,7 +256,22 @@ def bench_dense(ctx: Ctx, args, res: dict):
                 dist.reduce_scatter_tensor(out, Cp)
         launches = 1
         comm = "reduce_scatter (NCCL)"
+    else:
+        from periodicdent42_b200.dist import SplitKReduceScatterGemm
+
+        op = SplitKReduceScatterGemm(cfg.M, cfg.N) if ctx.world > 1 else None
+        out = torch.empty(cfg.M // ctx.world, cfg.N, device=ctx.dev)
+
+        def step():
+            if op is None:
+                _capi.gemm_f16f32(A, Bt, out, stream=ctx.stream)
+            else:
+                op(A, Bt, out, stream=ctx.stream)
+        launches = 2 if ctx.world > 1 else 1  # scatter GEMM + slot reduction
+        comm = "fused into the GEMM epilogue (NVLink peer stores) + 1-element all-reduce barrier"
     ms = time_region(ctx, step, args.steps, args.warmup, "dense")
+    if args.dense_mode == "splitk" and ctx.world > 1:
+        op.close()
     total_flops = cfg.flops
     tflops = total_flops / (ms * 1e-3) / 1e12
     res["dense"] = {"ms": ms, "tflops": tflops, "flops": total_flops, "launches_per_step": launches,

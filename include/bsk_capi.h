@@ -86,6 +86,32 @@ int bsk_gemm_f16f32_splitk_static(const void* A, int64_t lda, const void* B, int
                                   int M, int N, int K, int splits, void* stream);
 
 /*
+ * Split-K across ranks with the reduce-scatter fused into the GEMM (one process per GPU, NVLink peers).
+ * Each rank r computes C_r = A[:, k_begin:k_end] * B[k_begin:k_end, :] for its K range and its epilogue stores
+ * every output row i straight into the receive buffer of the row's owner (i / (M/world)), slot r:
+ *   slot_bufs[o] -> owner o's buffer [world][M/world][ld_slot] fp32 (its own buffer for o == rank, the others
+ *                   opened with bsk_peer_buffer_open); the stores cross NVLink while later tiles compute.
+ * After every rank's call has completed (a stream-ordered barrier such as a one-element all-reduce),
+ * bsk_splitk_slots_reduce on each rank sums its world slots in rank order (deterministic) into its M/world rows.
+ * Replaces the split-K + NCCL reduce-scatter plan of the operator family's multi-GPU dense GEMM; no reference
+ * counterpart (the reference has no multi-GPU code).
+ */
+int bsk_gemm_f16f32_splitk_scatter(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K,
+                                   int k_begin, int k_end, int world, int rank, void* const* slot_bufs,
+                                   int64_t ld_slot, void* stream);
+
+/* C[rows, N] = sum over s < world of slots[s][rows][ld_slot], in slot order. */
+int bsk_splitk_slots_reduce(const float* slots, int world, int rows, int N, int64_t ld_slot, float* C, int64_t ldc,
+                            void* stream);
+
+/* Receive buffers shared between processes: cudaMalloc + a 64-byte CUDA IPC handle; open a peer's handle
+ * (peer access enabled lazily), close it, free an own buffer. */
+int bsk_peer_buffer_alloc(int64_t bytes, void** dev_ptr, void* ipc_handle);
+int bsk_peer_buffer_open(const void* ipc_handle, void** dev_ptr);
+int bsk_peer_buffer_close(void* dev_ptr);
+int bsk_peer_buffer_free(void* dev_ptr);
+
+/*
  * FP8 GEMM, e4m3 x e4m3 -> bf16:  D[M,N] = bf16( (A_q[M,K] * B_q[K,N]) * scale_a * scale_b ).
  *   A   : e4m3 bytes, row-major [M, K] (lda multiple of 16)
  *   B   : e4m3 bytes, column-major [K, N] (B^T row-major [N, K], ldb multiple of 16)

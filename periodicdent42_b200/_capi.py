@@ -35,6 +35,13 @@ SIGNATURES = {
     "bsk_gemm_f16f32_splitk": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp]),
     "bsk_gemm_splitk_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32]),
     "bsk_gemm_f16f32_splitk_static": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp]),
+    "bsk_gemm_f16f32_splitk_scatter": (_i32, [_vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _i32, _i32,
+                                               ctypes.POINTER(ctypes.c_void_p), _i64, _vp]),
+    "bsk_splitk_slots_reduce": (_i32, [_vp, _i32, _i32, _i32, _i64, _vp, _i64, _vp]),
+    "bsk_peer_buffer_alloc": (_i32, [_i64, ctypes.POINTER(ctypes.c_void_p), ctypes.c_char_p]),
+    "bsk_peer_buffer_open": (_i32, [ctypes.c_char_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "bsk_peer_buffer_close": (_i32, [_vp]),
+    "bsk_peer_buffer_free": (_i32, [_vp]),
     "bsk_gemm_e4m3_bf16": (_i32, [_vp, _i64, _vp, _i64, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _vp]),
     "bsk_spmm_bsr_f16f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _i32, _i32, _i32,
                                    _i32, _i32, _vp]),

@@ -118,6 +118,8 @@ void init_device(DeviceState& st, int dev) {
       allow_smem(gemm_pair_sm100_kernel<2, Epi::F32, 1>, kPairSmemBytes),
       allow_smem(gemm_pair_sm100_kernel<1, Epi::BF16Scaled, 1>, kPairSmemBytes),
       allow_smem(gemm_pair_sm100_kernel<2, Epi::F32, 2>, kPairWideSmemBytes),
+      allow_smem(gemm_pair_sm100_kernel<2, Epi::F32PeerRows, 1>, kPairSmemBytes),
+      allow_smem(gemm_pair_sm100_kernel<2, Epi::F32PeerRows, 2>, kPairWideSmemBytes),
       allow_smem(gemm_pair_sm100_kernel<1, Epi::BF16Scaled, 2>, kPairWideSmemBytes),
   };
   for (cudaError_t x : errs) {
@@ -526,6 +528,117 @@ int bsk_gemm_f16f32_splitk_static(const void* A, int64_t lda, const void* B, int
   if (int rc = launch_pair_f16(*st, p, Ah, lda, Bh, ldb, M, N, K, ws, p.ld_ws, static_cast<int64_t>(M) * p.ld_ws, s))
     return rc;
   return splitk_reduce(*st, ws, p, C, ldc, M, N, s);
+}
+
+int bsk_peer_buffer_alloc(int64_t bytes, void** dev_ptr, void* ipc_handle) {
+  if (bytes <= 0 || !dev_ptr || !ipc_handle) return set_error(BSK_ERR_INVALID_ARG, "peer_buffer_alloc: bad arguments");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+  if (e != cudaSuccess) return cuda_fail(e, "peer_buffer_alloc: cudaMalloc");
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return cuda_fail(e, "peer_buffer_alloc: cudaIpcGetMemHandle");
+  }
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle is 64 bytes");
+  memcpy(ipc_handle, &h, sizeof(h));
+  *dev_ptr = p;
+  return BSK_OK;
+}
+
+int bsk_peer_buffer_open(const void* ipc_handle, void** dev_ptr) {
+  if (!ipc_handle || !dev_ptr) return set_error(BSK_ERR_INVALID_ARG, "peer_buffer_open: null argument");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  cudaIpcMemHandle_t h;
+  memcpy(&h, ipc_handle, sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "peer_buffer_open: cudaIpcOpenMemHandle");
+  *dev_ptr = p;
+  return BSK_OK;
+}
+
+int bsk_peer_buffer_close(void* dev_ptr) {
+  if (!dev_ptr) return BSK_OK;
+  cudaError_t e = cudaIpcCloseMemHandle(dev_ptr);
+  return e == cudaSuccess ? BSK_OK : cuda_fail(e, "peer_buffer_close");
+}
+
+int bsk_peer_buffer_free(void* dev_ptr) {
+  if (!dev_ptr) return BSK_OK;
+  cudaError_t e = cudaFree(dev_ptr);
+  return e == cudaSuccess ? BSK_OK : cuda_fail(e, "peer_buffer_free");
+}
+
+int bsk_gemm_f16f32_splitk_scatter(const void* A, int64_t lda, const void* B, int64_t ldb, int M, int N, int K,
+                                   int k_begin, int k_end, int world, int rank, void* const* slot_bufs,
+                                   int64_t ld_slot, void* stream) {
+  using namespace bsk;
+  if (world < 1 || world > kMaxPeers || rank < 0 || rank >= world)
+    return set_error(BSK_ERR_INVALID_ARG, "splitk_scatter: world %d / rank %d outside [1, %d]", world, rank, kMaxPeers);
+  if (M <= 0 || N <= 0 || K <= 0 || M % world)
+    return set_error(BSK_ERR_INVALID_ARG, "splitk_scatter: M (%d) must be a positive multiple of world (%d)", M, world);
+  if (k_begin < 0 || k_end > K || k_begin >= k_end || k_begin % 8)
+    return set_error(BSK_ERR_INVALID_ARG, "splitk_scatter: bad K range [%d, %d)", k_begin, k_end);
+  if (lda < K || ldb < K || lda % 8 || ldb % 8)
+    return set_error(BSK_ERR_INVALID_ARG, "splitk_scatter: lda/ldb must cover K and be multiples of 8");
+  if (ld_slot < N || ld_slot % 4) return set_error(BSK_ERR_INVALID_ARG, "splitk_scatter: ld_slot must be >= N, %4");
+  if (!A || !B || !slot_bufs) return set_error(BSK_ERR_INVALID_ARG, "splitk_scatter: null pointer");
+  for (int r = 0; r < world; ++r)
+    if (!slot_bufs[r] || !aligned16(slot_bufs[r]))
+      return set_error(BSK_ERR_INVALID_ARG, "splitk_scatter: slot buffer of rank %d missing or misaligned", r);
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  const int kr = k_end - k_begin;
+  const __half* Ah = static_cast<const __half*>(A) + k_begin;
+  const __half* Bh = static_cast<const __half*>(B) + k_begin;
+  const int kind = gemm_tile_kind(M, N, kr) == 2 ? 2 : 1;
+  CUtensorMap ta, tb;
+  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Ah, kr, M, lda * 2, 64, 128, "A")) return rc;
+  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, Bh, kr, N, ldb * 2, 64, 128, "B")) return rc;
+  GemmArgs a{};
+  const int tn = kind == 2 ? 512 : 256;
+  a.M = M;
+  a.N = N;
+  a.num_m_tiles = (M + kPairBM - 1) / kPairBM;
+  a.num_n_tiles = (N + tn - 1) / tn;
+  a.num_k_blocks = (kr + 63) / 64;
+  a.group_m = pick_group_m(a.num_m_tiles, kind);
+  a.k_splits = 1;
+  a.kb_per_split = a.num_k_blocks;
+  a.ldo = ld_slot;
+  a.vec_ok = 1;
+  for (int r = 0; r < world; ++r) a.peer_out[r] = static_cast<float*>(slot_bufs[r]);
+  a.rows_per_rank = M / world;
+  a.my_rank = rank;
+  a.err = st->err_word;
+  a.timeout_ns = t_timeout_ns;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int tiles = a.num_m_tiles * a.num_n_tiles;
+  const int clusters = tiles < st->pair_clusters ? tiles : st->pair_clusters;
+  if (kind == 2)
+    gemm_pair_sm100_kernel<2, Epi::F32PeerRows, 2><<<2 * clusters, kPairThreads, kPairWideSmemBytes, s>>>(ta, tb, a);
+  else
+    gemm_pair_sm100_kernel<2, Epi::F32PeerRows, 1><<<2 * clusters, kPairThreads, kPairSmemBytes, s>>>(ta, tb, a);
+  return launch_status("splitk_scatter launch");
+}
+
+int bsk_splitk_slots_reduce(const float* slots, int world, int rows, int N, int64_t ld_slot, float* C, int64_t ldc,
+                            void* stream) {
+  if (world < 1 || rows < 0 || N < 0 || ld_slot < N || ld_slot % 4 || ldc < N)
+    return set_error(BSK_ERR_INVALID_ARG, "slots_reduce: bad extents");
+  if (!slots || !C || !aligned16(slots)) return set_error(BSK_ERR_INVALID_ARG, "slots_reduce: null or misaligned");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  if (rows == 0 || N == 0) return BSK_OK;
+  SplitPlan p{};
+  p.splits = world;
+  p.ld_ws = ld_slot;
+  return splitk_reduce(*st, slots, p, C, ldc, rows, N, static_cast<cudaStream_t>(stream));
 }
 
 int bsk_bsr_validate_host(const int32_t* row_ptr, const int32_t* col_idx, int Mb, int Kb, int nnzb) {

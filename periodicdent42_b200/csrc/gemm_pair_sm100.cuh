@@ -235,9 +235,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
         ptx::tmem_wait_ld();
         const int col0 = n0 + c;
         if (row_ok) {
-          if constexpr (kEpi == Epi::F32) {
-            float* dst = reinterpret_cast<float*>(a.out) + split * a.split_stride + static_cast<int64_t>(row) * a.ldo +
-                         col0;
+          if constexpr (kEpi == Epi::F32 || kEpi == Epi::F32PeerRows) {
+            float* dst;
+            if constexpr (kEpi == Epi::F32PeerRows) {  // row -> its owner's slot `my_rank` (NVLink store)
+              const int owner = row / a.rows_per_rank;
+              const int local = row - owner * a.rows_per_rank;
+              dst = a.peer_out[owner] + (static_cast<int64_t>(a.my_rank) * a.rows_per_rank + local) * a.ldo + col0;
+            } else {
+              dst = reinterpret_cast<float*>(a.out) + split * a.split_stride + static_cast<int64_t>(row) * a.ldo +
+                    col0;
+            }
             if (a.vec_ok && col0 + 32 <= a.N) {
 #pragma unroll
               for (int v = 0; v < 8; ++v)
@@ -278,6 +285,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     }
   }
 
+  if constexpr (kEpi == Epi::F32PeerRows) __threadfence_system();  // peer-slot stores visible system-wide
   ptx::tc_fence_before();
   ptx::cluster_sync();  // no CTA leaves while its peer may still read its shared memory or signal its barriers
   ptx::tc_fence_after();

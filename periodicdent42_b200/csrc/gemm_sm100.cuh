@@ -30,7 +30,9 @@ constexpr int kGemmTmemCols = 512;
 constexpr int kGemmSmemBytes = 1024 /*align slack*/ + kGemmStages * (kGemmAStage + kGemmBStage) + 256;
 
 enum class Mainloop : int { Dense = 0, Bsr = 1 };
-enum class Epi : int { F32 = 0, BF16Scaled = 1 };
+// F32PeerRows: fp32 partial rows stored into their owner rank's receive slot (split-K reduce-scatter).
+enum class Epi : int { F32 = 0, BF16Scaled = 1, F32PeerRows = 2 };
+constexpr int kMaxPeers = 8;
 
 // Kernel ids recorded in the device error word.
 enum : uint32_t { kKidGemmF16 = 1, kKidGemmE4m3 = 2, kKidSpmmBsr = 3, kKidBsAttn = 4, kKidWaitProbe = 5 };
@@ -53,6 +55,9 @@ struct GemmArgs {
   int k_splits;              // CTA-pair kernels: K splits per output tile (1 = none)
   int kb_per_split;          // K stages per split (every split non-empty)
   int64_t split_stride;      // elements between the partial-output slabs of consecutive splits
+  float* peer_out[kMaxPeers];  // F32PeerRows: receive-slot buffer of each rank ([world][rows_per_rank][ldo])
+  int rows_per_rank;           // F32PeerRows: output rows owned by each rank
+  int my_rank;                 // F32PeerRows: slot this rank writes in every owner's buffer
   uint32_t* err;
   uint64_t timeout_ns;
 };
