@@ -150,7 +150,7 @@ int bsk_bsr_validate_host(const int32_t* row_ptr, const int32_t* col_idx, int Mb
 
 /*
  * Block-sparse attention forward, bf16:  O = softmax(scale * Q K^T, restricted to the block mask) V
- *   Q, K, V, O : bf16 contiguous [B, H, S, D], D = 128
+ *   Q, K, V, O : bf16 contiguous [B, H, S, D], D = 64 or 128 (fp32 accumulation, fp32 softmax statistics)
  *   row_ptr    : int32 [B*H*(S/blk) + 1], col_idx int32 [nnz]: for (b,h) pair p and query block-row i
  *                the nonzero key blocks are col_idx[row_ptr[p*(S/blk)+i] .. row_ptr[p*(S/blk)+i+1]).
  *                col_idx values are within-sequence block indices (0 .. S/blk-1).
@@ -165,6 +165,16 @@ int bsk_bsr_validate_host(const int32_t* row_ptr, const int32_t* col_idx, int Mb
 int bsk_bsattn_fwd_bf16(const void* Q, const void* K, const void* V, void* O, const int32_t* row_ptr,
                         const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale, int causal_diag,
                         int bh_begin, int bh_end, void* stream);
+
+/*
+ * The same forward for fp16 Q, K, V, O (the element type of the reference's launch_attention_forward,
+ * .archive/src_experiments/blackwell_sparsek/kernels/attention_fmha.cu:386-426, whose binding accepts
+ * head dims 64 and 128, kernel_bindings.cpp:53-54). Arguments as bsk_bsattn_fwd_bf16; P is rounded to
+ * fp16 before the P V product.
+ */
+int bsk_bsattn_fwd_f16(const void* Q, const void* K, const void* V, void* O, const int32_t* row_ptr,
+                       const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale, int causal_diag,
+                       int bh_begin, int bh_end, void* stream);
 
 /*
  * Drop-in for the reference's launcher signature (BlackwellSparseK/src/kernel_launch.cu:33-61).

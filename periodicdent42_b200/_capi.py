@@ -48,6 +48,8 @@ SIGNATURES = {
     "bsk_bsr_validate_host": (_i32, [_vp, _vp, _i32, _i32, _i32]),
     "bsk_bsattn_fwd_bf16": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32,
                                    _i32, _vp]),
+    "bsk_bsattn_fwd_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32,
+                                  _i32, _vp]),
     "launch_bsr_spmm_async": (None, [_vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _i32,
                                      _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
     "bsk_device_error": (_i32, [ctypes.POINTER(ctypes.c_uint32)]),
@@ -172,6 +174,16 @@ def bsattn_fwd_bf16(Q, K, V, O, row_ptr, col_idx, scale: float, causal_diag: boo
     check(lib().bsk_bsattn_fwd_bf16(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(row_ptr), _ptr(col_idx), B, H, S, D, blk,
                                     float(scale), int(bool(causal_diag)), bh_begin, bh_end, _stream(stream)),
           "bsk_bsattn_fwd_bf16")
+
+
+def bsattn_fwd_f16(Q, K, V, O, row_ptr, col_idx, scale: float, causal_diag: bool = True, bh_begin: int = 0,
+                   bh_end: int | None = None, blk: int = 128, stream=None) -> None:
+    """fp16 form of bsattn_fwd_bf16 (same arguments)."""
+    B, H, S, D = Q.shape
+    bh_end = B * H if bh_end is None else bh_end
+    check(lib().bsk_bsattn_fwd_f16(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(row_ptr), _ptr(col_idx), B, H, S, D, blk,
+                                   float(scale), int(bool(causal_diag)), bh_begin, bh_end, _stream(stream)),
+          "bsk_bsattn_fwd_f16")
 
 
 def device_error() -> int:

@@ -120,9 +120,9 @@ torch::Tensor bsattn_fwd(torch::Tensor Q, torch::Tensor K, torch::Tensor V, torc
                          torch::Tensor col_idx, double scale, bool causal_diag) {
   TORCH_CHECK(Q.is_cuda() && K.is_cuda() && V.is_cuda() && row_ptr.is_cuda() && col_idx.is_cuda(),
               "bsattn_fwd: CUDA tensors required");
-  TORCH_CHECK(Q.scalar_type() == torch::kBFloat16 && K.scalar_type() == torch::kBFloat16 &&
-                  V.scalar_type() == torch::kBFloat16,
-              "bsattn_fwd: bfloat16 Q, K, V");
+  const auto dt = Q.scalar_type();
+  TORCH_CHECK((dt == torch::kBFloat16 || dt == torch::kFloat16) && K.scalar_type() == dt && V.scalar_type() == dt,
+              "bsattn_fwd: Q, K, V all bfloat16 or all float16");
   TORCH_CHECK(Q.dim() == 4 && K.sizes() == Q.sizes() && V.sizes() == Q.sizes(), "bsattn_fwd: Q, K, V [B,H,S,D] of one shape");
   const at::cuda::CUDAGuard guard(Q.device());
   auto q = Q.contiguous(), k = K.contiguous(), v = V.contiguous();
@@ -132,10 +132,10 @@ torch::Tensor bsattn_fwd(torch::Tensor Q, torch::Tensor K, torch::Tensor V, torc
   TORCH_CHECK(S % 128 == 0, "bsattn_fwd: S must be a multiple of 128");
   TORCH_CHECK(rp.numel() == static_cast<int64_t>(B) * H * (S / 128) + 1, "bsattn_fwd: row_ptr must be [B*H*(S/128)+1]");
   auto O = torch::empty_like(q);
-  check_rc(bsk_bsattn_fwd_bf16(q.data_ptr(), k.data_ptr(), v.data_ptr(), O.data_ptr(), rp.data_ptr<int32_t>(),
-                               ci.data_ptr<int32_t>(), B, H, S, D, 128, static_cast<float>(scale), causal_diag ? 1 : 0,
-                               0, B * H, stream_of(O)),
-           "bsk_bsattn_fwd_bf16");
+  auto fn = dt == torch::kFloat16 ? bsk_bsattn_fwd_f16 : bsk_bsattn_fwd_bf16;
+  check_rc(fn(q.data_ptr(), k.data_ptr(), v.data_ptr(), O.data_ptr(), rp.data_ptr<int32_t>(), ci.data_ptr<int32_t>(), B,
+              H, S, D, 128, static_cast<float>(scale), causal_diag ? 1 : 0, 0, B * H, stream_of(O)),
+           dt == torch::kFloat16 ? "bsk_bsattn_fwd_f16" : "bsk_bsattn_fwd_bf16");
   return O;
 }
 

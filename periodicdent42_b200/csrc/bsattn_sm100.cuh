@@ -22,18 +22,27 @@
 #pragma once
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "ptx_sm100.cuh"
 
 namespace bsk {
 
 constexpr int kAttnBlk = 128;
-constexpr int kAttnD = 128;
 constexpr int kAttnThreads = 384;
-constexpr int kAttnTile = kAttnBlk * kAttnD * 2;  // 32 KB: one 128 x 128 bf16 tile (two 64-col SW128 chunks)
-constexpr int kAttnChunk = kAttnTile / 2;          // 16 KB
+constexpr int kAttnChunk = kAttnBlk * 64 * 2;  // 16 KB: 128 rows x 64 columns (one 128-B swizzle atom wide)
 constexpr int kAttnKVSlots = 5;
-constexpr int kAttnSmemBytes = 1024 + kAttnTile * (2 /*Q*/ + kAttnKVSlots) + 256;
+
+// Head dimension D (64 or 128) and element type (fp16 or bf16) of one instantiation.
+template <bool kF16, int kD>
+struct AttnShape {
+  static_assert(kD == 64 || kD == 128, "head dim 64 or 128");
+  static constexpr int kTile = kAttnBlk * kD * 2;  // one 128 x D tile: kD / 64 chunks of 16 KB
+  static constexpr int kChunks = kD / 64;
+  static constexpr int kSmemBytes = 1024 + kTile * (2 /*Q*/ + kAttnKVSlots) + 256;
+  static constexpr uint32_t kFmt = kF16 ? 0u : 1u;  // tcgen05 kind::f16 A/B format: 0 f16, 1 bf16
+};
+constexpr int kAttnSmemBytes = AttnShape<false, 128>::kSmemBytes;  // largest instantiation
 constexpr int kAttnTmemCols = 512;
 constexpr uint32_t kAttnRegsLaunch = 168;  // 65536 / 384, rounded down to a multiple of 8
 constexpr uint32_t kAttnRegsLow = 112;
@@ -42,7 +51,7 @@ static_assert(128 * kAttnRegsLow + 256 * kAttnRegsHigh <= kAttnThreads * kAttnRe
               "setmaxnreg split exceeds the launch allocation");
 
 struct AttnArgs {
-  __nv_bfloat16* O;
+  void* O;            // fp16 or bf16 [B*H*S, D]
   const int* row_ptr;
   const int* col_idx;
   int S;              // sequence length
@@ -138,16 +147,27 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&h);
 }
+__device__ __forceinline__ uint32_t pack_f16(float lo, float hi) {
+  __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+template <bool kF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  return kF16 ? pack_f16(lo, hi) : pack_bf16(lo, hi);
+}
 
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
 
+template <bool kF16, int kD>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     bsattn_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
-  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 128, 1, 1, 0, 0);   // bf16, both K-major
-  constexpr uint32_t IDESC_PV = ptx::instr_desc(128, 128, 1, 1, 0, 1);  // V MN-major
+  using Sh = AttnShape<kF16, kD>;
+  constexpr int kAttnTile = Sh::kTile;
+  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 128, Sh::kFmt, Sh::kFmt, 0, 0);  // K = D, both K-major
+  constexpr uint32_t IDESC_PV = ptx::instr_desc(128, kD, Sh::kFmt, Sh::kFmt, 0, 1);  // N = D, V MN-major
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -215,8 +235,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t fb = ptx::smem_u32(&kv_full[slot]);
         const uint32_t dst = kv0 + slot * kAttnTile;
         ptx::mbar_arrive_expect_tx(fb, kAttnTile);
-        ptx::tma_load_2d(dst, m, fb, 0, row);
-        ptx::tma_load_2d(dst + kAttnChunk, m, fb, 64, row);
+#pragma unroll
+        for (int c = 0; c < Sh::kChunks; ++c) ptx::tma_load_2d(dst + c * kAttnChunk, m, fb, 64 * c, row);
         ++kv_issued;
         if (++slot == kAttnKVSlots) { slot = 0; slot_phase ^= 1; }
         return true;
@@ -240,13 +260,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t qf = ptx::smem_u32(q_full);
         ptx::mbar_arrive_expect_tx(qf, (A.n > 0 ? kAttnTile : 0) + (B.n > 0 ? kAttnTile : 0));
         const int row0 = bh * a.S;
-        if (A.n > 0) {
-          ptx::tma_load_2d(ptx::smem_u32(sQ), &tmQ, qf, 0, row0 + A.qb * kAttnBlk);
-          ptx::tma_load_2d(ptx::smem_u32(sQ) + kAttnChunk, &tmQ, qf, 64, row0 + A.qb * kAttnBlk);
-        }
-        if (B.n > 0) {
-          ptx::tma_load_2d(ptx::smem_u32(sQ) + kAttnTile, &tmQ, qf, 0, row0 + B.qb * kAttnBlk);
-          ptx::tma_load_2d(ptx::smem_u32(sQ) + kAttnTile + kAttnChunk, &tmQ, qf, 64, row0 + B.qb * kAttnBlk);
+#pragma unroll
+        for (int c = 0; c < Sh::kChunks; ++c) {
+          if (A.n > 0)
+            ptx::tma_load_2d(ptx::smem_u32(sQ) + c * kAttnChunk, &tmQ, qf, 64 * c, row0 + A.qb * kAttnBlk);
+          if (B.n > 0)
+            ptx::tma_load_2d(ptx::smem_u32(sQ) + kAttnTile + c * kAttnChunk, &tmQ, qf, 64 * c,
+                             row0 + B.qb * kAttnBlk);
         }
         ++q_issued;
         q_phase ^= 1;
@@ -292,7 +312,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ptx::tc_fence_after();
         const uint32_t kA = kv0 + sl * kAttnTile, qA = sQa + x * kAttnTile;
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 0; k < kD / 16; ++k) {  // K = D in steps of 16: 4 steps per 64-column chunk
           const uint32_t off = (k >> 2) * kAttnChunk + (k & 3) * 32;
           ptx::mma_f16_ss(tmem_base + x * 128, ptx::smem_desc(qA + off, 16, 1024), ptx::smem_desc(kA + off, 16, 1024),
                           IDESC_S, k != 0);
@@ -360,11 +380,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       attn_item(a, item, bh, A, B);
       const AttnStream st = x == 0 ? A : B;
       if (st.qb < 0) continue;
-      __nv_bfloat16* orow = a.O + (static_cast<int64_t>(bh) * a.S + st.qb * kAttnBlk + r) * kAttnD;
+      uint16_t* orow = static_cast<uint16_t*>(a.O) + (static_cast<int64_t>(bh) * a.S + st.qb * kAttnBlk + r) * kD;
       if (st.n <= 0) {
         const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int cc = 0; cc < 16; ++cc) reinterpret_cast<uint4*>(orow)[cc] = z;
+        for (int cc = 0; cc < kD / 8; ++cc) reinterpret_cast<uint4*>(orow)[cc] = z;
         continue;
       }
       float m_run = -INFINITY, l_run = 0.0f;  // m_run in scaled log2 units
@@ -418,7 +438,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             e1 = ex2_approx(t1);
           }
           acc[(i >> 1) & 3] = f2_add(acc[(i >> 1) & 3], f2_pack(e0, e1));
-          sv[i >> 1] = pack_bf16(e0, e1);
+          sv[i >> 1] = pack2<kF16>(e0, e1);
         }
         float rs;
         {
@@ -431,7 +451,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (need_rescale) {  // O (complete through block j-1) *= alpha, in TMEM
           const float al = move ? alpha : 1.0f;
 #pragma unroll 1
-          for (int cc = 0; cc < 4; ++cc) {
+          for (int cc = 0; cc < kD / 32; ++cc) {
             uint32_t u[32];
             ptx::tmem_ld_32x32b_x32(tO + cc * 32, u);
             ptx::tmem_wait_ld();
@@ -456,17 +476,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ptx::tc_fence_after();
       const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
 #pragma unroll 1
-      for (int cc = 0; cc < 4; ++cc) {
+      for (int cc = 0; cc < kD / 32; ++cc) {
         uint32_t u[32];
         ptx::tmem_ld_32x32b_x32(tO + cc * 32, u);
         ptx::tmem_wait_ld();
         uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
 #pragma unroll
         for (int g = 0; g < 4; ++g) {
-          dst[g] = make_uint4(pack_bf16(__uint_as_float(u[8 * g + 0]) * inv_l, __uint_as_float(u[8 * g + 1]) * inv_l),
-                              pack_bf16(__uint_as_float(u[8 * g + 2]) * inv_l, __uint_as_float(u[8 * g + 3]) * inv_l),
-                              pack_bf16(__uint_as_float(u[8 * g + 4]) * inv_l, __uint_as_float(u[8 * g + 5]) * inv_l),
-                              pack_bf16(__uint_as_float(u[8 * g + 6]) * inv_l, __uint_as_float(u[8 * g + 7]) * inv_l));
+          dst[g] = make_uint4(pack2<kF16>(__uint_as_float(u[8 * g + 0]) * inv_l, __uint_as_float(u[8 * g + 1]) * inv_l),
+                              pack2<kF16>(__uint_as_float(u[8 * g + 2]) * inv_l, __uint_as_float(u[8 * g + 3]) * inv_l),
+                              pack2<kF16>(__uint_as_float(u[8 * g + 4]) * inv_l, __uint_as_float(u[8 * g + 5]) * inv_l),
+                              pack2<kF16>(__uint_as_float(u[8 * g + 6]) * inv_l, __uint_as_float(u[8 * g + 7]) * inv_l));
         }
       }
       ptx::tc_fence_before();

@@ -114,7 +114,10 @@ void init_device(DeviceState& st, int dev) {
       allow_smem(gemm_sm100_kernel<2, Mainloop::Dense, Epi::F32>, kGemmSmemBytes),
       allow_smem(gemm_sm100_kernel<1, Mainloop::Dense, Epi::BF16Scaled>, kGemmSmemBytes),
       allow_smem(gemm_sm100_kernel<2, Mainloop::Bsr, Epi::F32>, kGemmSmemBytes),
-      allow_smem(bsattn_sm100_kernel, kAttnSmemBytes),
+      allow_smem(bsattn_sm100_kernel<false, 128>, AttnShape<false, 128>::kSmemBytes),
+      allow_smem(bsattn_sm100_kernel<false, 64>, AttnShape<false, 64>::kSmemBytes),
+      allow_smem(bsattn_sm100_kernel<true, 128>, AttnShape<true, 128>::kSmemBytes),
+      allow_smem(bsattn_sm100_kernel<true, 64>, AttnShape<true, 64>::kSmemBytes),
       allow_smem(gemm_pair_sm100_kernel<2, Epi::F32, 1>, kPairSmemBytes),
       allow_smem(gemm_pair_sm100_kernel<1, Epi::BF16Scaled, 1>, kPairSmemBytes),
       allow_smem(gemm_pair_sm100_kernel<2, Epi::F32, 2>, kPairWideSmemBytes),
@@ -751,11 +754,15 @@ void launch_bsr_spmm_async(const int* A_row_ptr, const int* A_col_idx, const voi
   if (rc == BSK_OK) t_last_error.clear();
 }
 
-int bsk_bsattn_fwd_bf16(const void* Q, const void* K, const void* V, void* O, const int32_t* row_ptr,
-                        const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale, int causal_diag,
-                        int bh_begin, int bh_end, void* stream) {
+namespace {
+
+// Shared launcher of the fp16 and bf16 entry points: same argument checks, element type picks the
+// instantiation and the tensor-map data type.
+int bsattn_launch(bool f16, const void* Q, const void* K, const void* V, void* O, const int32_t* row_ptr,
+                  const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale, int causal_diag,
+                  int bh_begin, int bh_end, void* stream) {
   using namespace bsk;
-  if (D != kAttnD) return set_error(BSK_ERR_UNSUPPORTED, "bsattn: head_dim %d unsupported (needs %d)", D, kAttnD);
+  if (D != 64 && D != 128) return set_error(BSK_ERR_UNSUPPORTED, "bsattn: head_dim %d unsupported (64 or 128)", D);
   if (blk != kAttnBlk) return set_error(BSK_ERR_UNSUPPORTED, "bsattn: block size %d unsupported (needs %d)", blk, kAttnBlk);
   if (B < 0 || H < 0 || S < 0) return set_error(BSK_ERR_INVALID_ARG, "bsattn: negative extent");
   if (S % blk) return set_error(BSK_ERR_INVALID_ARG, "bsattn: S=%d not a multiple of the block size %d", S, blk);
@@ -770,12 +777,13 @@ int bsk_bsattn_fwd_bf16(const void* Q, const void* K, const void* V, void* O, co
   if (bh_end == bh_begin || S == 0) return BSK_OK;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const uint64_t rows = (uint64_t)B * H * S;
+  const CUtensorMapDataType dt = f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
   CUtensorMap tq, tk, tv;
-  if (int rc = make_map(&tq, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, Q, D, rows, D * 2, 64, kAttnBlk, "Q")) return rc;
-  if (int rc = make_map(&tk, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, K, D, rows, D * 2, 64, kAttnBlk, "K")) return rc;
-  if (int rc = make_map(&tv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, V, D, rows, D * 2, 64, kAttnBlk, "V")) return rc;
+  if (int rc = make_map(&tq, dt, 2, Q, D, rows, D * 2, 64, kAttnBlk, "Q")) return rc;
+  if (int rc = make_map(&tk, dt, 2, K, D, rows, D * 2, 64, kAttnBlk, "K")) return rc;
+  if (int rc = make_map(&tv, dt, 2, V, D, rows, D * 2, 64, kAttnBlk, "V")) return rc;
   AttnArgs a{};
-  a.O = static_cast<__nv_bfloat16*>(O);
+  a.O = O;
   a.row_ptr = row_ptr;
   a.col_idx = col_idx;
   a.S = S;
@@ -788,8 +796,31 @@ int bsk_bsattn_fwd_bf16(const void* Q, const void* K, const void* V, void* O, co
   a.err = st->err_word;
   a.timeout_ns = t_timeout_ns;
   const int grid = a.num_items < st->sm_count ? a.num_items : st->sm_count;
-  bsattn_sm100_kernel<<<grid, kAttnThreads, kAttnSmemBytes, s>>>(tq, tk, tv, a);
+  if (f16 && D == 128)
+    bsattn_sm100_kernel<true, 128><<<grid, kAttnThreads, AttnShape<true, 128>::kSmemBytes, s>>>(tq, tk, tv, a);
+  else if (f16)
+    bsattn_sm100_kernel<true, 64><<<grid, kAttnThreads, AttnShape<true, 64>::kSmemBytes, s>>>(tq, tk, tv, a);
+  else if (D == 128)
+    bsattn_sm100_kernel<false, 128><<<grid, kAttnThreads, AttnShape<false, 128>::kSmemBytes, s>>>(tq, tk, tv, a);
+  else
+    bsattn_sm100_kernel<false, 64><<<grid, kAttnThreads, AttnShape<false, 64>::kSmemBytes, s>>>(tq, tk, tv, a);
   return launch_status("bsattn launch");
+}
+
+}  // namespace
+
+int bsk_bsattn_fwd_bf16(const void* Q, const void* K, const void* V, void* O, const int32_t* row_ptr,
+                        const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale, int causal_diag,
+                        int bh_begin, int bh_end, void* stream) {
+  return bsattn_launch(false, Q, K, V, O, row_ptr, col_idx, B, H, S, D, blk, scale, causal_diag, bh_begin, bh_end,
+                       stream);
+}
+
+int bsk_bsattn_fwd_f16(const void* Q, const void* K, const void* V, void* O, const int32_t* row_ptr,
+                       const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale, int causal_diag,
+                       int bh_begin, int bh_end, void* stream) {
+  return bsattn_launch(true, Q, K, V, O, row_ptr, col_idx, B, H, S, D, blk, scale, causal_diag, bh_begin, bh_end,
+                       stream);
 }
 
 int bsk_device_error(uint32_t* out) {

@@ -206,7 +206,7 @@ def attention_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: 
 
     Keeps the reference's signature ``attention_forward(Q, K, V, scale=None)``
     (.archive/src_experiments/blackwell_sparsek/__init__.py:52-109) and its checks (CUDA, 4-D, equal
-    shapes), with the sm_100 kernel's constraints: bf16, D = 128, S a multiple of 128.
+    shapes, fp16, D in {64, 128}), and also accepts bf16; S must be a multiple of 128.
       block_mask: None (all blocks), a bool tensor [S/128, S/128] shared by every (b, h) or
                   [B, H, S/128, S/128], or a BSR tuple (row_ptr, col_idx) over the B*H*(S/128) block
                   rows (pairs in (b, h) order, within-sequence block indices).
@@ -220,10 +220,10 @@ def attention_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: 
     Bsz, H, S, D = Q.shape
     if K.shape != (Bsz, H, S, D) or V.shape != (Bsz, H, S, D):
         raise ValueError("Q, K, V must have the same shape")
-    if Q.dtype != torch.bfloat16 or K.dtype != torch.bfloat16 or V.dtype != torch.bfloat16:
-        raise ValueError("All tensors must be bfloat16 (torch.bfloat16)")
-    if D != 128:
-        raise ValueError(f"Head dimension must be 128, got {D}")
+    if Q.dtype not in (torch.float16, torch.bfloat16) or K.dtype != Q.dtype or V.dtype != Q.dtype:
+        raise ValueError("All tensors must be FP16 (torch.float16) or all BF16 (torch.bfloat16)")
+    if D not in (64, 128):
+        raise ValueError(f"Head dimension must be 64 or 128, got {D}")
     if block_size != 128:
         raise ValueError("block_size must be 128")
     if S % 128:

@@ -19,7 +19,7 @@ def declared_symbols():
 
 def test_header_declares_expected_entry_points():
     syms = declared_symbols()
-    for s in ["bsk_gemm_f16f32", "bsk_gemm_e4m3_bf16", "bsk_spmm_bsr_f16f32", "bsk_bsattn_fwd_bf16",
+    for s in ["bsk_gemm_f16f32", "bsk_gemm_e4m3_bf16", "bsk_spmm_bsr_f16f32", "bsk_bsattn_fwd_bf16", "bsk_bsattn_fwd_f16",
               "bsk_device_error", "launch_bsr_spmm_async", "bsk_last_error"]:
         assert s in syms, s
 
@@ -59,12 +59,14 @@ def test_spmm_rejects_unsupported_block_shape_on_host():
     assert e.value.code == _capi.BSK_ERR_UNSUPPORTED
 
 
-def test_attention_rejects_head_dim_on_host():
-    q = _fake((1, 1, 128, 64), torch.bfloat16)
+@pytest.mark.parametrize("D", [32, 256])
+def test_attention_rejects_head_dim_on_host(D):
     rp = torch.zeros(2, dtype=torch.int32)
-    with pytest.raises(_capi.BskError) as e:
-        _capi.bsattn_fwd_bf16(q, q, q, q, rp, rp, 0.1, stream=0)
-    assert e.value.code == _capi.BSK_ERR_UNSUPPORTED
+    for dt, fn in [(torch.bfloat16, _capi.bsattn_fwd_bf16), (torch.float16, _capi.bsattn_fwd_f16)]:
+        q = _fake((1, 1, 128, D), dt)
+        with pytest.raises(_capi.BskError) as e:
+            fn(q, q, q, q, rp, rp, 0.1, stream=0)
+        assert e.value.code == _capi.BSK_ERR_UNSUPPORTED
 
 
 @pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-device path")
