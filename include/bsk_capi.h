@@ -55,6 +55,35 @@ int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, floa
                     int K, int k_begin, int k_end, void* stream);
 
 /*
+ * bsk_gemm_f16f32 that accumulates: C[M,N] += A[M, k_begin:k_end] * B[k_begin:k_end, N] (each C element read
+ * once, the product added to it, stored). For callers that sweep K in pieces (K-chunked streaming, K shards
+ * summed on one GPU). No reference counterpart.
+ */
+int bsk_gemm_f16f32_acc(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc, int M, int N,
+                        int K, int k_begin, int k_end, void* stream);
+
+/*
+ * Dense GEMM from HOST memory: C_host[M,N] = A_host[M,K] * B_host[K,N] (same layouts as bsk_gemm_f16f32), streamed
+ * through the GPU in K chunks: the host-to-device copies of chunk i+1 (on a stream of this call's own) overlap
+ * the tensor-core work on chunk i, C accumulates in device memory and is copied back once at the end.
+ *   A_host, B_host, C_host : host memory; page-locked (cudaHostAlloc / cudaHostRegister) for the copies to be
+ *                            asynchronous and overlap; pageable memory works but serialises.
+ *   k_chunk   : K elements per chunk, a multiple of 64; <= 0 chooses (about 16 chunks of at least 4096).
+ *   workspace : device memory, 256-byte aligned, of bsk_gemm_host_workspace_bytes(M, N, K, k_chunk) bytes
+ *               (two A chunks, two B chunks, the fp32 C); used by this call until `stream` reaches its end.
+ * Everything is ordered on `stream`: the call returns once the work is enqueued and C_host is complete when
+ * the stream has synchronised. No reference counterpart (the reference's GEMM programs time device-resident
+ * operands only).
+ */
+int bsk_gemm_f16f32_host(const void* A_host, int64_t lda, const void* B_host, int64_t ldb, float* C_host,
+                         int64_t ldc, int M, int N, int K, int k_chunk, void* workspace, int64_t workspace_bytes,
+                         void* stream);
+
+/* Workspace bytes of bsk_gemm_f16f32_host for this shape and chunk (k_chunk <= 0: the automatic chunk), or a
+ * negative error code. */
+int64_t bsk_gemm_host_workspace_bytes(int M, int N, int K, int k_chunk);
+
+/*
  * Dense GEMM as bsk_gemm_f16f32 (k range = all of K) with the K dimension split across CTA pairs, for shapes
  * whose output has too few 256 x 256 tiles to occupy the GPU (e.g. 1024 x 1024 with long K). Each split writes
  * an fp32 partial slab into `workspace`; a second kernel sums the slabs in split order (deterministic) into C.

@@ -13,7 +13,7 @@ functions and signatures, backed by hand-written tcgen05/TMA kernels behind a C 
 
 __version__ = "0.9.0+sm100a"
 
-from .ops import (attention_forward, gemm, gemm_fp8, has_cuda_ext, quantize_e4m3, sparse_mm,
+from .ops import (attention_forward, gemm, gemm_fp8, gemm_from_host, has_cuda_ext, quantize_e4m3, sparse_mm,
                   sparse_mm_benchmark, synchronize_and_check)
 from .utils import convert_to_bsr, get_optimal_block_size, validate_sparse_matrix
 
@@ -25,6 +25,7 @@ __all__ = [
     "get_optimal_block_size",
     "gemm",
     "gemm_fp8",
+    "gemm_from_host",
     "quantize_e4m3",
     "attention_forward",
     "has_cuda_ext",

@@ -32,6 +32,9 @@ SIGNATURES = {
     "bsk_last_error": (ctypes.c_char_p, []),
     "bsk_device_sm_count": (_i32, []),
     "bsk_gemm_f16f32": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "bsk_gemm_f16f32_acc": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp]),
+    "bsk_gemm_f16f32_host": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp]),
+    "bsk_gemm_host_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32]),
     "bsk_gemm_f16f32_splitk": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp]),
     "bsk_gemm_splitk_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32]),
     "bsk_gemm_f16f32_splitk_static": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp]),
@@ -113,6 +116,33 @@ def gemm_f16f32(A, Bt, C, k_begin: int = 0, k_end: int | None = None, stream=Non
     k_end = K if k_end is None else k_end
     check(lib().bsk_gemm_f16f32(_ptr(A), A.stride(0), _ptr(Bt), Bt.stride(0), _ptr(C), C.stride(0), M, N, K,
                                 k_begin, k_end, _stream(stream)), "bsk_gemm_f16f32")
+
+
+def gemm_f16f32_acc(A, Bt, C, k_begin: int = 0, k_end: int | None = None, stream=None) -> None:
+    """C[M,N] += A[M, k_begin:k_end] @ B[k_begin:k_end, N] (fp32 C read and updated in place)."""
+    M, K = A.shape
+    N = Bt.shape[0]
+    k_end = K if k_end is None else k_end
+    check(lib().bsk_gemm_f16f32_acc(_ptr(A), A.stride(0), _ptr(Bt), Bt.stride(0), _ptr(C), C.stride(0), M, N, K,
+                                    k_begin, k_end, _stream(stream)), "bsk_gemm_f16f32_acc")
+
+
+def gemm_host_workspace_bytes(M: int, N: int, K: int, k_chunk: int = 0) -> int:
+    n = lib().bsk_gemm_host_workspace_bytes(M, N, K, k_chunk)
+    if n < 0:
+        raise BskError(n, "bsk_gemm_host_workspace_bytes", last_error())
+    return n
+
+
+def gemm_f16f32_host(A_h, Bt_h, C_h, workspace, k_chunk: int = 0, stream=None) -> None:
+    """C_h = A_h @ B for HOST tensors (pinned for overlap), streamed through the GPU in K chunks; `workspace` is
+    a CUDA uint8 tensor of gemm_host_workspace_bytes(M, N, K, k_chunk) bytes. Asynchronous on `stream`."""
+    M, K = A_h.shape
+    N = Bt_h.shape[0]
+    nbytes = workspace.numel() * workspace.element_size()
+    check(lib().bsk_gemm_f16f32_host(_ptr(A_h), A_h.stride(0), _ptr(Bt_h), Bt_h.stride(0), _ptr(C_h), C_h.stride(0),
+                                     M, N, K, k_chunk, _ptr(workspace), nbytes, _stream(stream)),
+          "bsk_gemm_f16f32_host")
 
 
 def gemm_splitk_workspace_bytes(M: int, N: int, K: int, splits: int = 0) -> int:

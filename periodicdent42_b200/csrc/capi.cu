@@ -262,8 +262,11 @@ int bsk_set_wait_timeout_ns(uint64_t ns) {
   return BSK_OK;
 }
 
-int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc, int M, int N,
-                    int K, int k_begin, int k_end, void* stream) {
+namespace {
+
+// Dense fp16 GEMM over K range [k_begin, k_end): C = A B (accumulate = 0) or C += A B (accumulate = 1).
+int gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc, int M, int N,
+                    int K, int k_begin, int k_end, int accumulate, void* stream) {
   using namespace bsk;
   if (M < 0 || N < 0 || K < 0) return set_error(BSK_ERR_INVALID_ARG, "gemm_f16f32: negative extent");
   if (k_begin < 0 || k_end > K || k_begin > k_end)
@@ -279,6 +282,7 @@ int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, floa
   const int kr = k_end - k_begin;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (kr == 0) {
+    if (accumulate) return BSK_OK;  // C += 0
     cudaError_t e = cudaMemset2DAsync(C, ldc * sizeof(float), 0, (size_t)N * sizeof(float), M, s);
     return e == cudaSuccess ? BSK_OK : cuda_fail(e, "gemm_f16f32: zero fill");
   }
@@ -303,6 +307,7 @@ int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, floa
   a.out = C;
   a.ldo = ldc;
   a.vec_ok = aligned16(C) && (ldc % 4 == 0);
+  a.accumulate = accumulate;
   a.err = st->err_word;
   a.timeout_ns = t_timeout_ns;
   const int tiles = a.num_m_tiles * a.num_n_tiles;
@@ -316,6 +321,140 @@ int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, floa
     gemm_sm100_kernel<2, Mainloop::Dense, Epi::F32><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
   }
   return launch_status("gemm_f16f32 launch");
+}
+
+}  // namespace
+
+int bsk_gemm_f16f32(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc, int M, int N,
+                    int K, int k_begin, int k_end, void* stream) {
+  return gemm_f16_launch(A, lda, B, ldb, C, ldc, M, N, K, k_begin, k_end, 0, stream);
+}
+
+int bsk_gemm_f16f32_acc(const void* A, int64_t lda, const void* B, int64_t ldb, float* C, int64_t ldc, int M, int N,
+                        int K, int k_begin, int k_end, void* stream) {
+  return gemm_f16_launch(A, lda, B, ldb, C, ldc, M, N, K, k_begin, k_end, 1, stream);
+}
+
+namespace {
+
+// K-chunk plan of the host-streaming GEMM: chunk width (multiple of 64), device workspace layout.
+struct HostPlan {
+  int kc = 0;             // K elements per chunk (pitch of the chunk buffers)
+  int64_t a_bytes = 0;    // one A chunk buffer [M, kc] fp16
+  int64_t b_bytes = 0;    // one B^T chunk buffer [N, kc] fp16
+  int64_t ldc_dev = 0;    // row stride of the device C
+  int64_t total = 0;      // A0, A1, B0, B1, C, each rounded up to 256 bytes
+};
+
+int64_t round256(int64_t x) { return (x + 255) / 256 * 256; }
+
+HostPlan plan_host(int M, int N, int K, int k_chunk) {
+  HostPlan p;
+  int kc = k_chunk;
+  if (kc <= 0) {  // ~16 chunks of >= 4096 (enough K per launch to keep the tiles busy), never above K
+    kc = (K + 15) / 16;
+    if (kc < 4096) kc = 4096;
+  }
+  kc = (kc + 63) / 64 * 64;
+  const int k_pad = (K + 63) / 64 * 64;
+  if (kc > k_pad) kc = k_pad > 0 ? k_pad : 64;
+  p.kc = kc;
+  p.a_bytes = round256((int64_t)M * kc * 2);
+  p.b_bytes = round256((int64_t)N * kc * 2);
+  p.ldc_dev = (N + 3) / 4 * 4;
+  p.total = 2 * p.a_bytes + 2 * p.b_bytes + round256((int64_t)M * p.ldc_dev * 4);
+  return p;
+}
+
+}  // namespace
+
+int64_t bsk_gemm_host_workspace_bytes(int M, int N, int K, int k_chunk) {
+  if (M < 0 || N < 0 || K < 0) return set_error(BSK_ERR_INVALID_ARG, "gemm_host: negative extent");
+  if (k_chunk > 0 && k_chunk % 64) return set_error(BSK_ERR_INVALID_ARG, "gemm_host: k_chunk must be a multiple of 64");
+  return plan_host(M, N, K, k_chunk).total;
+}
+
+int bsk_gemm_f16f32_host(const void* A_host, int64_t lda, const void* B_host, int64_t ldb, float* C_host,
+                         int64_t ldc, int M, int N, int K, int k_chunk, void* workspace, int64_t workspace_bytes,
+                         void* stream) {
+  using namespace bsk;
+  if (M < 0 || N < 0 || K < 0) return set_error(BSK_ERR_INVALID_ARG, "gemm_host: negative extent");
+  if (lda < K || ldb < K || ldc < N) return set_error(BSK_ERR_INVALID_ARG, "gemm_host: leading dimensions smaller than the extents");
+  if (k_chunk > 0 && k_chunk % 64) return set_error(BSK_ERR_INVALID_ARG, "gemm_host: k_chunk must be a multiple of 64");
+  if (!A_host || !B_host || !C_host) return set_error(BSK_ERR_INVALID_ARG, "gemm_host: null host pointer");
+  const HostPlan p = plan_host(M, N, K, k_chunk);
+  if (!workspace || workspace_bytes < p.total)
+    return set_error(BSK_ERR_INVALID_ARG, "gemm_host: workspace of %lld bytes needed, %lld given", (long long)p.total,
+                     (long long)workspace_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return set_error(BSK_ERR_INVALID_ARG, "gemm_host: workspace must be 256-byte aligned");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  if (M == 0 || N == 0) return BSK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  __half* abuf[2] = {reinterpret_cast<__half*>(ws), reinterpret_cast<__half*>(ws + p.a_bytes)};
+  __half* bbuf[2] = {reinterpret_cast<__half*>(ws + 2 * p.a_bytes),
+                     reinterpret_cast<__half*>(ws + 2 * p.a_bytes + p.b_bytes)};
+  float* Cd = reinterpret_cast<float*>(ws + 2 * p.a_bytes + 2 * p.b_bytes);
+  const int nchunks = K == 0 ? 0 : (K + p.kc - 1) / p.kc;
+
+  // Copies run on their own stream so chunk i+1 crosses PCIe while chunk i is on the tensor cores; events order
+  // them: ready[b] (chunk in buffer b has landed) before its GEMM, freed[b] (that GEMM has finished reading
+  // buffer b) before the copy two chunks later overwrites it. Stream and events are released at the end of
+  // this call; CUDA keeps them alive until the enqueued work that uses them has completed.
+  cudaStream_t cs = nullptr;
+  cudaEvent_t start = nullptr, ready[2] = {nullptr, nullptr}, freed[2] = {nullptr, nullptr};
+  int rc = BSK_OK;
+  cudaError_t e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&start, cudaEventDisableTiming);
+  for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
+    e = cudaEventCreateWithFlags(&ready[b], cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&freed[b], cudaEventDisableTiming);
+  }
+  if (e == cudaSuccess) e = cudaEventRecord(start, s);  // earlier work on `stream` (e.g. a previous user of the
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, start, 0);  // workspace) comes before the first copy
+  if (e != cudaSuccess) rc = cuda_fail(e, "gemm_host: stream/event setup");
+  for (int i = 0; i < nchunks && rc == BSK_OK; ++i) {
+    const int b = i & 1;
+    const int k0 = i * p.kc;
+    const int kw = K - k0 < p.kc ? K - k0 : p.kc;
+    if (i >= 2) e = cudaStreamWaitEvent(cs, freed[b], 0);
+    if (e == cudaSuccess)
+      e = cudaMemcpy2DAsync(abuf[b], (size_t)p.kc * 2, static_cast<const __half*>(A_host) + k0, (size_t)lda * 2,
+                            (size_t)kw * 2, M, cudaMemcpyHostToDevice, cs);
+    if (e == cudaSuccess)
+      e = cudaMemcpy2DAsync(bbuf[b], (size_t)p.kc * 2, static_cast<const __half*>(B_host) + k0, (size_t)ldb * 2,
+                            (size_t)kw * 2, N, cudaMemcpyHostToDevice, cs);
+    if (e == cudaSuccess) e = cudaEventRecord(ready[b], cs);
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ready[b], 0);
+    if (e != cudaSuccess) {
+      rc = cuda_fail(e, "gemm_host: chunk copy");
+      break;
+    }
+    rc = gemm_f16_launch(abuf[b], p.kc, bbuf[b], p.kc, Cd, p.ldc_dev, M, N, kw, 0, kw, i > 0 ? 1 : 0, stream);
+    if (rc == BSK_OK && (e = cudaEventRecord(freed[b], s)) != cudaSuccess) rc = cuda_fail(e, "gemm_host: event");
+  }
+  if (rc == BSK_OK && nchunks == 0) {
+    e = cudaMemset2DAsync(Cd, p.ldc_dev * 4, 0, (size_t)N * 4, M, s);
+    if (e != cudaSuccess) rc = cuda_fail(e, "gemm_host: zero fill");
+  }
+  if (rc == BSK_OK) {
+    e = cudaMemcpy2DAsync(C_host, (size_t)ldc * 4, Cd, (size_t)p.ldc_dev * 4, (size_t)N * 4, M,
+                          cudaMemcpyDeviceToHost, s);
+    if (e != cudaSuccess) rc = cuda_fail(e, "gemm_host: result copy");
+  }
+  // If a step failed part-way, `stream` must still not run ahead of copies already queued on cs.
+  if (cs && start) {
+    if (cudaEventRecord(start, cs) == cudaSuccess) cudaStreamWaitEvent(s, start, 0);
+  }
+  for (int b = 0; b < 2; ++b) {
+    if (ready[b]) cudaEventDestroy(ready[b]);
+    if (freed[b]) cudaEventDestroy(freed[b]);
+  }
+  if (start) cudaEventDestroy(start);
+  if (cs) cudaStreamDestroy(cs);
+  return rc;
 }
 
 int bsk_gemm_e4m3_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, const float* scale_a,

@@ -245,14 +245,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
               dst = reinterpret_cast<float*>(a.out) + split * a.split_stride + static_cast<int64_t>(row) * a.ldo +
                     col0;
             }
-            if (a.vec_ok && col0 + 32 <= a.N) {
-#pragma unroll
-              for (int v = 0; v < 8; ++v)
-                st_global_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
-            } else {
-              for (int i = 0; i < 32; ++i)
-                if (col0 + i < a.N) dst[i] = __uint_as_float(r[i]);
-            }
+            store_row32_f32(dst, r, a.vec_ok && col0 + 32 <= a.N, a.N - col0,
+                            kEpi == Epi::F32 ? a.accumulate : 0);
           } else {
             __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
             uint32_t pk[16];

@@ -58,6 +58,7 @@ struct GemmArgs {
   float* peer_out[kMaxPeers];  // F32PeerRows: receive-slot buffer of each rank ([world][rows_per_rank][ldo])
   int rows_per_rank;           // F32PeerRows: output rows owned by each rank
   int my_rank;                 // F32PeerRows: slot this rank writes in every owner's buffer
+  int accumulate;              // F32 only: C += result (C read before the store) instead of C = result
   uint32_t* err;
   uint64_t timeout_ns;
 };
@@ -84,6 +85,28 @@ __device__ __forceinline__ bool bsr_row_range(const GemmArgs& a, int r, int& j0,
 
 __device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.global.v4.b32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+
+// Stores 32 fp32 accumulator values of one output row at dst (columns col0 .. col0+31, `valid` of them inside
+// the matrix). vec: 16-byte aligned full chunk. accumulate: dst[i] = dst[i] + r[i] (the previous value first).
+__device__ __forceinline__ void store_row32_f32(float* dst, uint32_t (&r)[32], bool vec, int valid, int accumulate) {
+  if (vec) {
+    if (accumulate) {
+#pragma unroll
+      for (int v = 0; v < 8; ++v) {
+        const float4 c = *reinterpret_cast<const float4*>(dst + 4 * v);
+        r[4 * v + 0] = __float_as_uint(c.x + __uint_as_float(r[4 * v + 0]));
+        r[4 * v + 1] = __float_as_uint(c.y + __uint_as_float(r[4 * v + 1]));
+        r[4 * v + 2] = __float_as_uint(c.z + __uint_as_float(r[4 * v + 2]));
+        r[4 * v + 3] = __float_as_uint(c.w + __uint_as_float(r[4 * v + 3]));
+      }
+    }
+#pragma unroll
+    for (int v = 0; v < 8; ++v) st_global_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+  } else {
+    for (int i = 0; i < 32; ++i)
+      if (i < valid) dst[i] = accumulate ? dst[i] + __uint_as_float(r[i]) : __uint_as_float(r[i]);
+  }
 }
 
 template <int kElemBytes, Mainloop kML, Epi kEpi>
@@ -310,13 +333,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         if (row_ok) {
         if constexpr (kEpi == Epi::F32) {
           float* dst = reinterpret_cast<float*>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
-          if (a.vec_ok && col0 + 32 <= a.N) {
-#pragma unroll
-            for (int v = 0; v < 8; ++v) st_global_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
-          } else {
-            for (int i = 0; i < 32; ++i)
-              if (col0 + i < a.N) dst[i] = __uint_as_float(r[i]);
-          }
+          store_row32_f32(dst, r, a.vec_ok && col0 + 32 <= a.N, a.N - col0, a.accumulate);
         } else {
           __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + static_cast<int64_t>(row) * a.ldo + col0;
           uint32_t pk[16];

@@ -12,6 +12,8 @@ from typing import Optional, Tuple
 
 import torch
 
+from . import _capi
+
 from . import workloads as _wl
 
 _C_MOD = None
@@ -167,6 +169,40 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out_dtype: torch.dtype = torch.float3
         return _C().gemm_f16f32_splitk(A, Bt, int(split_k))
     kb, ke = (0, -1) if k_range is None else k_range
     return _C().gemm_f16f32(A, Bt, kb, ke)
+
+
+def gemm_from_host(A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor] = None, k_chunk: int = 0,
+                   device=None, sync: bool = True) -> torch.Tensor:
+    """C = A @ B for fp16 operands in HOST memory, fp32 result in host memory, computed on the GPU with the
+    K dimension streamed in chunks: the PCIe copy of chunk i+1 overlaps the tensor-core work on chunk i and C
+    accumulates on the device (one copy back at the end). A [M, K] row-major; B [K, N], column-major preferred
+    (``B = Bt.t()``). Use page-locked tensors (``pin_memory=True``) for A, B and ``out``: pageable memory works
+    but its copies do not overlap. ``k_chunk``: K per chunk (multiple of 64), 0 = automatic. ``sync``: wait for
+    the result (False leaves it pending on the current stream of ``device``)."""
+    for t in (A, B):
+        if t.is_cuda:
+            raise ValueError("gemm_from_host takes host tensors (use gemm for device tensors)")
+        if t.dtype != torch.float16:
+            raise ValueError("float16 tensors required")
+    if A.dim() != 2 or B.dim() != 2 or A.shape[1] != B.shape[0]:
+        raise ValueError(f"gemm_from_host: shape mismatch {tuple(A.shape)} @ {tuple(B.shape)}")
+    A = A if A.stride(1) == 1 else A.contiguous()
+    Bt = B.t()
+    Bt = Bt if Bt.stride(1) == 1 else Bt.contiguous()
+    M, K = A.shape
+    N = Bt.shape[0]
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.float32, pin_memory=True)
+    elif out.is_cuda or out.dtype != torch.float32 or tuple(out.shape) != (M, N) or out.stride(1) != 1:
+        raise ValueError(f"out must be a host float32 [{M}, {N}] tensor with unit column stride")
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        ws = torch.empty(_capi.gemm_host_workspace_bytes(M, N, K, k_chunk), dtype=torch.uint8, device=dev)
+        stream = torch.cuda.current_stream(dev)
+        _capi.gemm_f16f32_host(A, Bt, out, ws, k_chunk, stream)
+        if sync:
+            stream.synchronize()
+    return out
 
 
 def quantize_e4m3(x: torch.Tensor):
