@@ -290,14 +290,28 @@ def bench_dense(ctx: Ctx, args, res: dict):
         del A, Bt, Bt_r
         torch.cuda.empty_cache()
 
-        def e2e_step():  # K streamed in chunks: PCIe copies of chunk i+1 overlap the GEMM of chunk i
-            bsk.gemm_from_host(A_h, Bt_h.t(), out=C_h, k_chunk=args.e2e_k_chunk, sync=False)
+        if ctx.world == 1:
+            api = "periodicdent42_b200.gemm_from_host"
+
+            def e2e_step():  # K streamed in chunks: PCIe copies of chunk i+1 overlap the GEMM of chunk i
+                bsk.gemm_from_host(A_h, Bt_h.t(), out=C_h, k_chunk=args.e2e_k_chunk, sync=False)
+        else:  # each rank copies 1/world of A's rows per chunk; NCCL all-gathers the chunk over NVLink
+            from periodicdent42_b200.dist import HostShardedGemm
+            api = "periodicdent42_b200.dist.HostShardedGemm"
+            hsg = HostShardedGemm(cfg.M, Bt_h.shape[0], cfg.K, args.e2e_k_chunk)
+
+            def e2e_step():
+                hsg(A_h, Bt_h, C_h)
         ms_e2e = time_region(ctx, e2e_step, args.e2e_steps, 1, "dense_e2e")
+        h2d = A_h.numel() * 2 if ctx.world == 1 else (hsg.r1 - hsg.r0) * cfg.K * 2
         res["dense"]["e2e"] = {"value": total_flops / (ms_e2e * 1e-3) / 1e12, "unit": UNIT,
-                               "h2d_bytes_per_step": A_h.numel() * 2 + Bt_h.numel() * 2,
+                               "h2d_bytes_per_step": h2d + Bt_h.numel() * 2,
                                "d2h_bytes_per_step": C_h.numel() * 4, "ms_per_step": ms_e2e,
-                               "steps": args.e2e_steps, "api": "periodicdent42_b200.gemm_from_host",
-                               "k_chunk": args.e2e_k_chunk or "auto"}
+                               "steps": args.e2e_steps, "api": api, "k_chunk": args.e2e_k_chunk or "auto",
+                               "bytes_scope": "per rank"}
+        if ctx.world > 1:
+            res["dense"]["e2e"]["nvlink_gather_bytes_per_step"] = (ctx.world - 1) * hsg.mr * cfg.K * 2
+            del hsg
         del A_h, Bt_h, C_h
     torch.cuda.empty_cache()
 

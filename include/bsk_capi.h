@@ -79,6 +79,16 @@ int bsk_gemm_f16f32_host(const void* A_host, int64_t lda, const void* B_host, in
                          int64_t ldc, int M, int N, int K, int k_chunk, void* workspace, int64_t workspace_bytes,
                          void* stream);
 
+/* K elements per chunk that bsk_gemm_f16f32_host uses for this K and k_chunk request (k_chunk <= 0: automatic),
+ * or a negative error code; lets a caller that stages chunks itself use the same plan. */
+int bsk_gemm_host_chunk(int K, int k_chunk);
+
+/* Asynchronous 2-D copy on `stream`: `rows` rows of `width_bytes` bytes from src (row pitch spitch bytes) to dst
+ * (row pitch dpitch bytes), either side host or device (unified addressing decides the direction). A helper for
+ * callers that stage row ranges of host matrices into device chunk buffers. */
+int bsk_copy_2d_async(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width_bytes, int64_t rows,
+                      void* stream);
+
 /* Workspace bytes of bsk_gemm_f16f32_host for this shape and chunk (k_chunk <= 0: the automatic chunk), or a
  * negative error code. */
 int64_t bsk_gemm_host_workspace_bytes(int M, int N, int K, int k_chunk);

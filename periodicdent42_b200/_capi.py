@@ -35,6 +35,8 @@ SIGNATURES = {
     "bsk_gemm_f16f32_acc": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp]),
     "bsk_gemm_f16f32_host": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp]),
     "bsk_gemm_host_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32]),
+    "bsk_gemm_host_chunk": (_i32, [_i32, _i32]),
+    "bsk_copy_2d_async": (_i32, [_vp, _i64, _vp, _i64, _i64, _i64, _vp]),
     "bsk_gemm_f16f32_splitk": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp]),
     "bsk_gemm_splitk_workspace_bytes": (_i64, [_i32, _i32, _i32, _i32]),
     "bsk_gemm_f16f32_splitk_static": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp]),
@@ -132,6 +134,19 @@ def gemm_host_workspace_bytes(M: int, N: int, K: int, k_chunk: int = 0) -> int:
     if n < 0:
         raise BskError(n, "bsk_gemm_host_workspace_bytes", last_error())
     return n
+
+
+def gemm_host_chunk(K: int, k_chunk: int = 0) -> int:
+    """K elements per chunk of the host-streaming GEMM for this K and request (0 = automatic)."""
+    n = lib().bsk_gemm_host_chunk(K, k_chunk)
+    if n < 0:
+        raise BskError(n, "bsk_gemm_host_chunk", last_error())
+    return n
+
+
+def copy_2d_async(dst: int, dpitch: int, src: int, spitch: int, width_bytes: int, rows: int, stream=None) -> None:
+    """cudaMemcpy2DAsync between raw addresses (host or device, direction by unified addressing)."""
+    check(lib().bsk_copy_2d_async(dst, dpitch, src, spitch, width_bytes, rows, _stream(stream)), "bsk_copy_2d_async")
 
 
 def gemm_f16f32_host(A_h, Bt_h, C_h, workspace, k_chunk: int = 0, stream=None) -> None:

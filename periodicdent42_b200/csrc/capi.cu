@@ -368,6 +368,23 @@ HostPlan plan_host(int M, int N, int K, int k_chunk) {
 
 }  // namespace
 
+int bsk_gemm_host_chunk(int K, int k_chunk) {
+  if (K < 0) return set_error(BSK_ERR_INVALID_ARG, "gemm_host: negative K");
+  if (k_chunk > 0 && k_chunk % 64) return set_error(BSK_ERR_INVALID_ARG, "gemm_host: k_chunk must be a multiple of 64");
+  return plan_host(1, 1, K, k_chunk).kc;
+}
+
+int bsk_copy_2d_async(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width_bytes, int64_t rows,
+                      void* stream) {
+  if (width_bytes < 0 || rows < 0 || dpitch < width_bytes || spitch < width_bytes)
+    return set_error(BSK_ERR_INVALID_ARG, "copy_2d: bad extents");
+  if (width_bytes == 0 || rows == 0) return BSK_OK;
+  if (!dst || !src) return set_error(BSK_ERR_INVALID_ARG, "copy_2d: null pointer");
+  cudaError_t e = cudaMemcpy2DAsync(dst, (size_t)dpitch, src, (size_t)spitch, (size_t)width_bytes, (size_t)rows,
+                                    cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  return e == cudaSuccess ? BSK_OK : cuda_fail(e, "copy_2d");
+}
+
 int64_t bsk_gemm_host_workspace_bytes(int M, int N, int K, int k_chunk) {
   if (M < 0 || N < 0 || K < 0) return set_error(BSK_ERR_INVALID_ARG, "gemm_host: negative extent");
   if (k_chunk > 0 && k_chunk % 64) return set_error(BSK_ERR_INVALID_ARG, "gemm_host: k_chunk must be a multiple of 64");

@@ -135,3 +135,18 @@ def test_rank_that_never_joins_times_out():
     mp.start_processes(_worker_never_joins, args=(port, resq), nprocs=WORLD, start_method="spawn", join=True)
     msg = resq.get(timeout=60)
     assert msg.startswith("error"), msg
+
+
+@pytest.mark.parametrize("M,world", [(8192, 8), (10, 4), (2, 4), (301, 2), (1, 1), (0, 3)])
+def test_host_rows_cover_m_contiguously(M, world):
+    from periodicdent42_b200.dist import host_rows
+
+    spans = [host_rows(M, world, r) for r in range(world)]
+    mr = spans[0][2]
+    assert all(s[2] == mr for s in spans) and mr * world >= M
+    assert spans[0][0] == 0 and spans[-1][1] == M
+    for r in range(world):
+        r0, r1, _ = spans[r]
+        assert r0 == min(r * mr, M) and 0 <= r1 - r0 <= mr  # rank r's real rows sit at the start of its block
+        if r:
+            assert r0 == spans[r - 1][1]

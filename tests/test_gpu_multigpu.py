@@ -1,5 +1,6 @@
 """Multi-GPU paths on 2 GPUs (child processes, one per GPU, NCCL): the fused split-K GEMM + reduce-scatter
-(peer-memory epilogue) and the N-sharded GEMM, each rank's shard against fp64. Skipped with fewer than 2 GPUs."""
+(peer-memory epilogue), the N-sharded GEMM and the N-sharded GEMM fed from host memory (row slices staged
+per rank, NCCL all-gather), each rank's shard against fp64. Skipped with fewer than 2 GPUs."""
 import os
 import socket
 import traceback
@@ -27,7 +28,7 @@ def _worker(rank, port, q):
 
         from oracle import reference_path as ref
         from periodicdent42_b200 import _capi, sharding
-        from periodicdent42_b200.dist import SplitKReduceScatterGemm
+        from periodicdent42_b200.dist import HostShardedGemm, SplitKReduceScatterGemm
 
         os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         torch.cuda.set_device(rank)
@@ -52,6 +53,22 @@ def _worker(rank, port, q):
         _capi.gemm_f16f32(Ad, Btd[n0:n1], C)
         torch.cuda.synchronize()
         errs["nshard"] = ref.normwise_rel_err(C.cpu(), full64[:, n0:n1])
+        # host-resident operands: each rank stages half of A's rows per K chunk, NCCL gathers the chunk
+        A_h, Bt_h = A.pin_memory(), Bt[n0:n1].contiguous().pin_memory()
+        C_h = torch.empty(M, n1 - n0, pin_memory=True)
+        hsg = HostShardedGemm(M, n1 - n0, K, k_chunk=1024)
+        for call in range(2):
+            C_h.fill_(float("nan"))
+            hsg(A_h, Bt_h, C_h)
+            torch.cuda.synchronize()
+            errs[f"host_sharded_{call}"] = ref.normwise_rel_err(C_h, full64[:, n0:n1])
+        # ragged: M not divisible by the world size, K not a multiple of the chunk
+        Mr, Kr = 301, 3000
+        hs2 = HostShardedGemm(Mr, n1 - n0, Kr, k_chunk=512)
+        C2 = torch.empty(Mr, n1 - n0, pin_memory=True)
+        hs2(A_h[:Mr, :Kr], Bt_h[:, :Kr], C2)
+        torch.cuda.synchronize()
+        errs["host_sharded_ragged"] = ref.normwise_rel_err(C2, ref.dense_fp64(A[:Mr, :Kr], Bt[n0:n1, :Kr]))
         errs["device_error"] = _capi.device_error()
         dist.barrier()
         dist.destroy_process_group()
