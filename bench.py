@@ -48,7 +48,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--ops", default="dense,fp8,bsr,attn", help="comma list; dense is the headline")
+    p.add_argument("--ops", default="dense,fp8,bsr,attn,convert", help="comma list; dense is the headline")
     p.add_argument("--dense-mode", choices=["nshard", "splitk", "splitk_nccl"], default="nshard",
                    help="nshard: N-sharded, no communication; splitk: K split across ranks, reduce-scatter fused "
                         "into the GEMM (peer-memory epilogue); splitk_nccl: K split + NCCL reduce_scatter")
@@ -353,6 +353,76 @@ def bench_bsr(ctx: Ctx, args, res: dict):
     torch.cuda.empty_cache()
 
 
+# ----------------------------------------------------------------------------------------- BSR conversion
+def bench_convert(ctx: Ctx, args, res: dict):
+    """Dense -> BSR and CSR -> BSR on the device for the BSR workload's matrix (8192 x 8192 fp16, 1024 of 4096
+    128x128 blocks stored), through the C ABI with preallocated outputs. Headline step: the single-call form
+    (no host round trip) with room for every block (capacity M/bs x K/bs, so nothing about the pattern is known
+    in advance); the two-phase form (pattern call returns nnzb to the host, then fill) is timed beside it.
+    Replicas at N > 1 (every rank converts the whole matrix)."""
+    import ctypes
+
+    cfg = wl.BSR
+    crow, col, vals, _ = wl.bsr_inputs(cfg, ctx.dev)
+    M, K, bs = cfg.M, cfg.K, cfg.block
+    A = torch.sparse_bsr_tensor(crow, col, vals, size=(M, K)).to_dense()
+    nnzb = int(crow[-1].item())
+    cap = (M // bs) * (K // bs)
+    lib = _capi.lib()
+    ws = torch.empty(_capi.bsr_convert_workspace_bytes(M, K, bs), dtype=torch.uint8, device=ctx.dev)
+    rp = torch.empty(M // bs + 1, dtype=torch.int32, device=ctx.dev)
+    ci = torch.empty(cap, dtype=torch.int32, device=ctx.dev)
+    vo = torch.empty(cap, bs, bs, dtype=torch.float16, device=ctx.dev)
+    n_b, n_e = ctypes.c_int64(0), ctypes.c_int64(0)
+    st = ctx.stream.cuda_stream
+
+    def step_dense():
+        _capi.check(lib.bsk_dense_to_bsr_bounded(A.data_ptr(), K, 2, M, K, bs, rp.data_ptr(), ci.data_ptr(), 4,
+                                                 vo.data_ptr(), cap, ws.data_ptr(), ws.numel(), st), "dense")
+
+    def step_dense_2phase():
+        _capi.check(lib.bsk_dense_to_bsr_pattern(A.data_ptr(), K, 2, M, K, bs, rp.data_ptr(), 4, ws.data_ptr(),
+                                                 ws.numel(), ctypes.byref(n_b), ctypes.byref(n_e), st), "pattern")
+        _capi.check(lib.bsk_dense_to_bsr_fill(A.data_ptr(), K, 2, M, K, bs, rp.data_ptr(), ci.data_ptr(), 4,
+                                              vo.data_ptr(), n_b.value, ws.data_ptr(), ws.numel(), st), "fill")
+    ms_d = time_region(ctx, step_dense, args.op_steps, args.warmup, "convert_dense")
+    assert int(rp[-1].item()) == nnzb and torch.equal(ci[:nnzb].long(), col) and torch.equal(vo[:nnzb], vals), \
+        "dense->BSR mismatch"
+    ms_d2 = time_region(ctx, step_dense_2phase, args.op_steps, args.warmup, "convert_dense_2phase")
+    csr = A.to_sparse_csr()
+    c_rp, c_ci, c_v = csr.crow_indices().to(torch.int32), csr.col_indices().to(torch.int32), csr.values()
+    nnz = c_v.numel()
+    del A, csr
+
+    def step_csr():
+        _capi.check(lib.bsk_csr_to_bsr_bounded(c_rp.data_ptr(), c_ci.data_ptr(), 4, c_v.data_ptr(), 2, nnz, M, K, bs,
+                                               rp.data_ptr(), ci.data_ptr(), 4, vo.data_ptr(), cap, ws.data_ptr(),
+                                               ws.numel(), st), "csr")
+
+    def step_csr_2phase():
+        _capi.check(lib.bsk_csr_to_bsr_pattern(c_rp.data_ptr(), c_ci.data_ptr(), 4, c_v.data_ptr(), 2, nnz, M, K, bs,
+                                               rp.data_ptr(), 4, ws.data_ptr(), ws.numel(), ctypes.byref(n_b),
+                                               ctypes.byref(n_e), st), "pattern")
+        _capi.check(lib.bsk_csr_to_bsr_fill(c_rp.data_ptr(), c_ci.data_ptr(), 4, c_v.data_ptr(), 2, nnz, M, K, bs,
+                                            rp.data_ptr(), ci.data_ptr(), 4, vo.data_ptr(), n_b.value, ws.data_ptr(),
+                                            ws.numel(), st), "fill")
+    vo.fill_(1.0)
+    ms_c = time_region(ctx, step_csr, args.op_steps, args.warmup, "convert_csr")
+    assert int(rp[-1].item()) == nnzb and torch.equal(vo[:nnzb], vals), "CSR->BSR mismatch"
+    ms_c2 = time_region(ctx, step_csr_2phase, args.op_steps, args.warmup, "convert_csr_2phase")
+    blk_bytes = nnzb * bs * bs * 2
+    # algorithmic bytes: dense: read the matrix, read the stored blocks again, write them (+ indices);
+    # CSR: read crow, col, values twice (pattern and scatter), zero and write the values
+    dense_bytes = M * K * 2 + 2 * blk_bytes + (M // bs + 1 + nnzb) * 4
+    csr_bytes = (M + 1) * 4 * 2 + 2 * nnz * (4 + 2) + 2 * blk_bytes + (M // bs + 1 + nnzb) * 4
+    res["convert"] = {"ms_dense": ms_d, "gbs_dense": dense_bytes / (ms_d * 1e-3) / 1e9, "bytes_dense": dense_bytes,
+                      "ms_csr": ms_c, "gbs_csr": csr_bytes / (ms_c * 1e-3) / 1e9, "bytes_csr": csr_bytes,
+                      "ms_dense_two_phase": ms_d2, "ms_csr_two_phase": ms_c2,
+                      "nnzb": nnzb, "scaling": "replicas"}
+    del c_rp, c_ci, c_v, crow, col, vals, ws, rp, ci, vo
+    torch.cuda.empty_cache()
+
+
 # ----------------------------------------------------------------------------------------- attention
 def bench_attn(ctx: Ctx, args, res: dict):
     cfg = wl.ATTN
@@ -450,7 +520,8 @@ def main():
         clocks.start()
     try:
         for op in ops:
-            {"dense": bench_dense, "fp8": bench_fp8, "bsr": bench_bsr, "attn": bench_attn}[op](ctx, args, res)
+            {"dense": bench_dense, "fp8": bench_fp8, "bsr": bench_bsr, "attn": bench_attn,
+             "convert": bench_convert}[op](ctx, args, res)
     finally:
         clk = clocks.stop() if clocks else None
     err_word = _capi.device_error()
@@ -499,6 +570,16 @@ def main():
                 for kk in ("nnzb", "nnz_blocks"):
                     if kk in r:
                         opsum[name][kk] = r[kk]
+        if "convert" in res:
+            r = res["convert"]
+            opsum["bsr_convert"] = {"dense_gbs": r["gbs_dense"], "dense_ms": r["ms_dense"],
+                                    "csr_gbs": r["gbs_csr"], "csr_ms": r["ms_csr"], "peak_gbs": peaks["hbm_gbs"],
+                                    "dense_ms_two_phase": r["ms_dense_two_phase"],
+                                    "csr_ms_two_phase": r["ms_csr_two_phase"],
+                                    "dense_frac_of_peak": r["gbs_dense"] / peaks["hbm_gbs"],
+                                    "csr_frac_of_peak": r["gbs_csr"] / peaks["hbm_gbs"],
+                                    "peak_basis": f"{peak_src} HBM copy", "nnzb": r["nnzb"],
+                                    "scaling": r["scaling"]}
         line["ops"] = opsum
         line["device_error_word"] = err_word
         print(json.dumps(line), flush=True)

@@ -216,6 +216,51 @@ int bsk_bsattn_fwd_f16(const void* Q, const void* K, const void* V, void* O, con
                        int bh_begin, int bh_end, void* stream);
 
 /*
+ * Dense / CSR -> BSR conversion on the device, square bs x bs blocks, in two phases (the caller sizes the outputs
+ * from the first): the result equals torch's dense.to_sparse_bsr((bs, bs)) -- the conversion the reference's
+ * convert_to_bsr performs (BlackwellSparseK/python/utils.py:10-57; its CSR path goes through to_dense(),
+ * utils.py:32-35, and ops.py:193-197 left CSR -> BSR unimplemented):
+ *   - a block is stored iff one of its elements is nonzero (-0.0 counts as zero, NaN as nonzero);
+ *   - block columns ascend within a block-row; values [nnzb, bs, bs] hold the blocks bit for bit.
+ * elem_bytes: 2 (fp16 / bf16) or 4 (fp32); index_bytes: 4 (int32) or 8 (int64, torch's default) for the outputs
+ * row_ptr [M/bs + 1] and col_idx [nnzb]. M and K must be multiples of bs.
+ * workspace: device memory of bsk_bsr_convert_workspace_bytes(M, K, bs) bytes, 256-byte aligned; the fill call
+ * must get the workspace, row_ptr and nnzb its pattern call produced, unchanged (col_idx and values may be NULL
+ * when nnzb is 0).
+ * The pattern call synchronises `stream` to return *nnzb (stored blocks) and *nnz_elems (nonzero elements).
+ * CSR input: crow [M + 1], col [nnz] (index_bytes_in 4 or 8), vals [nnz]; a column index outside [0, K) fails the
+ * pattern call with BSK_ERR_INVALID_ARG. Entries stored twice for one (row, col) are not summed (one value wins).
+ */
+int64_t bsk_bsr_convert_workspace_bytes(int M, int K, int bs);
+int bsk_dense_to_bsr_pattern(const void* A, int64_t lda, int elem_bytes, int M, int K, int bs, void* row_ptr,
+                             int index_bytes, void* workspace, int64_t workspace_bytes, int64_t* nnzb,
+                             int64_t* nnz_elems, void* stream);
+int bsk_dense_to_bsr_fill(const void* A, int64_t lda, int elem_bytes, int M, int K, int bs, const void* row_ptr,
+                          void* col_idx, int index_bytes, void* values, int64_t nnzb, void* workspace,
+                          int64_t workspace_bytes, void* stream);
+int bsk_csr_to_bsr_pattern(const void* crow, const void* col, int index_bytes_in, const void* vals, int elem_bytes,
+                           int64_t nnz, int M, int K, int bs, void* row_ptr, int index_bytes, void* workspace,
+                           int64_t workspace_bytes, int64_t* nnzb, int64_t* nnz_elems, void* stream);
+int bsk_csr_to_bsr_fill(const void* crow, const void* col, int index_bytes_in, const void* vals, int elem_bytes,
+                        int64_t nnz, int M, int K, int bs, const void* row_ptr, void* col_idx, int index_bytes,
+                        void* values, int64_t nnzb, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * Single-call forms of the two conversions for callers that can bound the number of stored blocks: pattern and
+ * fill in one call, all on `stream`, with no host synchronisation (so they can be captured in a CUDA graph).
+ * col_idx and values have room for max_nnzb blocks. When the stream has reached the end of the call,
+ * row_ptr[M/bs] holds the true nnzb; if it exceeds max_nnzb, only the first max_nnzb blocks (in BSR order) were
+ * written. A CSR column index outside [0, K) is skipped (the two-phase pattern call reports it instead).
+ * No reference counterpart.
+ */
+int bsk_dense_to_bsr_bounded(const void* A, int64_t lda, int elem_bytes, int M, int K, int bs, void* row_ptr,
+                             void* col_idx, int index_bytes, void* values, int64_t max_nnzb, void* workspace,
+                             int64_t workspace_bytes, void* stream);
+int bsk_csr_to_bsr_bounded(const void* crow, const void* col, int index_bytes_in, const void* vals, int elem_bytes,
+                           int64_t nnz, int M, int K, int bs, void* row_ptr, void* col_idx, int index_bytes,
+                           void* values, int64_t max_nnzb, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
  * Drop-in for the reference's launcher signature (BlackwellSparseK/src/kernel_launch.cu:33-61).
  * A is BSR with blocks of (M/A_M_blocks) x (K/A_K_blocks); B must be the all-blocks pattern the reference
  * Python layer builds (BlackwellSparseK/python/ops.py:104-107), whose value buffer is the dense row-major

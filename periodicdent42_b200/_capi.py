@@ -51,6 +51,19 @@ SIGNATURES = {
     "bsk_spmm_bsr_f16f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _i32, _i32, _i32,
                                    _i32, _i32, _vp]),
     "bsk_bsr_validate_host": (_i32, [_vp, _vp, _i32, _i32, _i32]),
+    "bsk_bsr_convert_workspace_bytes": (_i64, [_i32, _i32, _i32]),
+    "bsk_dense_to_bsr_pattern": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _vp, _i64,
+                                        ctypes.POINTER(_i64), ctypes.POINTER(_i64), _vp]),
+    "bsk_dense_to_bsr_fill": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _i32, _vp, _i64, _vp, _i64,
+                                     _vp]),
+    "bsk_csr_to_bsr_pattern": (_i32, [_vp, _vp, _i32, _vp, _i32, _i64, _i32, _i32, _i32, _vp, _i32, _vp, _i64,
+                                      ctypes.POINTER(_i64), ctypes.POINTER(_i64), _vp]),
+    "bsk_csr_to_bsr_fill": (_i32, [_vp, _vp, _i32, _vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp, _i32, _vp, _i64, _vp,
+                                   _i64, _vp]),
+    "bsk_dense_to_bsr_bounded": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _vp, _vp, _i32, _vp, _i64, _vp, _i64,
+                                        _vp]),
+    "bsk_csr_to_bsr_bounded": (_i32, [_vp, _vp, _i32, _vp, _i32, _i64, _i32, _i32, _i32, _vp, _vp, _i32, _vp, _i64,
+                                      _vp, _i64, _vp]),
     "bsk_bsattn_fwd_bf16": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32,
                                    _i32, _vp]),
     "bsk_bsattn_fwd_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32,
@@ -229,6 +242,101 @@ def bsattn_fwd_f16(Q, K, V, O, row_ptr, col_idx, scale: float, causal_diag: bool
     check(lib().bsk_bsattn_fwd_f16(_ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(row_ptr), _ptr(col_idx), B, H, S, D, blk,
                                    float(scale), int(bool(causal_diag)), bh_begin, bh_end, _stream(stream)),
           "bsk_bsattn_fwd_f16")
+
+
+def bsr_convert_workspace_bytes(M: int, K: int, bs: int) -> int:
+    n = lib().bsk_bsr_convert_workspace_bytes(M, K, bs)
+    if n < 0:
+        raise BskError(n, "bsk_bsr_convert_workspace_bytes", last_error())
+    return n
+
+
+def _index_bytes(dtype) -> int:
+    import torch
+
+    if dtype not in (torch.int32, torch.int64):
+        raise ValueError("index tensors must be int32 or int64")
+    return 4 if dtype == torch.int32 else 8
+
+
+def dense_to_bsr(A, bs: int, index_dtype=None, stream=None):
+    """Device dense [M, K] (fp16 / bf16 / fp32, unit column stride) -> (row_ptr, col_idx, values, nnz_elems), the
+    block pattern and blocks torch's A.to_sparse_bsr((bs, bs)) stores. Synchronises the stream once (to size
+    the outputs)."""
+    import torch
+
+    index_dtype = torch.int64 if index_dtype is None else index_dtype
+    ib = _index_bytes(index_dtype)
+    M, K = A.shape
+    if A.stride(1) != 1 and A.numel() > 0:
+        raise ValueError("dense_to_bsr: A needs unit column stride")
+    eb = A.element_size()
+    ws = torch.empty(bsr_convert_workspace_bytes(M, K, bs), dtype=torch.uint8, device=A.device)
+    row_ptr = torch.empty(M // bs + 1, dtype=index_dtype, device=A.device)
+    nnzb, nnz = ctypes.c_int64(0), ctypes.c_int64(0)
+    lda = A.stride(0) if A.numel() > 0 else max(K, 1)
+    s = _stream(stream)
+    check(lib().bsk_dense_to_bsr_pattern(_ptr(A), lda, eb, M, K, bs, _ptr(row_ptr), ib, _ptr(ws), ws.numel(),
+                                         ctypes.byref(nnzb), ctypes.byref(nnz), s), "bsk_dense_to_bsr_pattern")
+    col_idx = torch.empty(nnzb.value, dtype=index_dtype, device=A.device)
+    values = torch.empty(nnzb.value, bs, bs, dtype=A.dtype, device=A.device)
+    check(lib().bsk_dense_to_bsr_fill(_ptr(A), lda, eb, M, K, bs, _ptr(row_ptr), _ptr(col_idx), ib, _ptr(values),
+                                      nnzb.value, _ptr(ws), ws.numel(), s), "bsk_dense_to_bsr_fill")
+    return row_ptr, col_idx, values, nnz.value
+
+
+def csr_to_bsr(crow, col, vals, shape, bs: int, index_dtype=None, stream=None):
+    """Device CSR (crow [M+1], col [nnz], vals [nnz]) of `shape` (M, K) -> (row_ptr, col_idx, values, nnz_elems),
+    the result of to_dense().to_sparse_bsr((bs, bs)). Synchronises the stream once."""
+    import torch
+
+    index_dtype = torch.int64 if index_dtype is None else index_dtype
+    ib = _index_bytes(index_dtype)
+    ib_in = _index_bytes(crow.dtype)
+    if col.dtype != crow.dtype:
+        raise ValueError("crow and col indices must have one dtype")
+    M, K = shape
+    nnz_in = vals.numel()
+    eb = vals.element_size()
+    dev = vals.device
+    ws = torch.empty(bsr_convert_workspace_bytes(M, K, bs), dtype=torch.uint8, device=dev)
+    row_ptr = torch.empty(M // bs + 1, dtype=index_dtype, device=dev)
+    nnzb, nnz = ctypes.c_int64(0), ctypes.c_int64(0)
+    s = _stream(stream)
+    check(lib().bsk_csr_to_bsr_pattern(_ptr(crow), _ptr(col), ib_in, _ptr(vals), eb, nnz_in, M, K, bs, _ptr(row_ptr),
+                                       ib, _ptr(ws), ws.numel(), ctypes.byref(nnzb), ctypes.byref(nnz), s),
+          "bsk_csr_to_bsr_pattern")
+    col_idx = torch.empty(nnzb.value, dtype=index_dtype, device=dev)
+    values = torch.empty(nnzb.value, bs, bs, dtype=vals.dtype, device=dev)
+    check(lib().bsk_csr_to_bsr_fill(_ptr(crow), _ptr(col), ib_in, _ptr(vals), eb, nnz_in, M, K, bs, _ptr(row_ptr),
+                                    _ptr(col_idx), ib, _ptr(values), nnzb.value, _ptr(ws), ws.numel(), s),
+          "bsk_csr_to_bsr_fill")
+    return row_ptr, col_idx, values, nnz.value
+
+
+def dense_to_bsr_bounded(A, bs: int, row_ptr, col_idx, values, workspace, stream=None) -> None:
+    """Single-call dense -> BSR into preallocated outputs (capacity = len(col_idx) blocks); no host sync.
+    row_ptr[-1] holds the true block count once the stream gets there."""
+    M, K = A.shape
+    cap = col_idx.numel()
+    if values.shape[0] < cap:
+        raise ValueError("values must hold as many blocks as col_idx")
+    check(lib().bsk_dense_to_bsr_bounded(_ptr(A), A.stride(0) if A.numel() else max(K, 1), A.element_size(), M, K, bs,
+                                         _ptr(row_ptr), _ptr(col_idx), _index_bytes(col_idx.dtype), _ptr(values), cap,
+                                         _ptr(workspace), workspace.numel(), _stream(stream)),
+          "bsk_dense_to_bsr_bounded")
+
+
+def csr_to_bsr_bounded(crow, col, vals, shape, bs: int, row_ptr, col_idx, values, workspace, stream=None) -> None:
+    """Single-call CSR -> BSR into preallocated outputs (capacity = len(col_idx) blocks); no host sync."""
+    M, K = shape
+    cap = col_idx.numel()
+    if values.shape[0] < cap:
+        raise ValueError("values must hold as many blocks as col_idx")
+    check(lib().bsk_csr_to_bsr_bounded(_ptr(crow), _ptr(col), _index_bytes(crow.dtype), _ptr(vals),
+                                       vals.element_size(), vals.numel(), M, K, bs, _ptr(row_ptr), _ptr(col_idx),
+                                       _index_bytes(col_idx.dtype), _ptr(values), cap, _ptr(workspace),
+                                       workspace.numel(), _stream(stream)), "bsk_csr_to_bsr_bounded")
 
 
 def device_error() -> int:

@@ -26,9 +26,9 @@ TORCH_EXT = os.path.join(PKG_DIR, "_C.so")
 
 NVCC_ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 CAPI_SOURCES = [os.path.join(CSRC, "capi.cu")]
-CAPI_DEPS = CAPI_SOURCES + [
-    os.path.join(CSRC, f) for f in ("ptx_sm100.cuh", "gemm_sm100.cuh", "gemm_pair_sm100.cuh", "bsattn_sm100.cuh")
-] + [os.path.join(INCLUDE, "bsk_capi.h")]
+CAPI_DEPS = CAPI_SOURCES + sorted(
+    os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith(".cuh")
+) + [os.path.join(INCLUDE, "bsk_capi.h")]
 
 
 def _nvcc() -> str:

@@ -16,6 +16,7 @@
 #include "gemm_sm100.cuh"
 #include "gemm_pair_sm100.cuh"
 #include "bsattn_sm100.cuh"
+#include "bsr_convert.cuh"
 
 namespace {
 
@@ -977,6 +978,346 @@ int bsk_bsattn_fwd_f16(const void* Q, const void* K, const void* V, void* O, con
                        int bh_begin, int bh_end, void* stream) {
   return bsattn_launch(true, Q, K, V, O, row_ptr, col_idx, B, H, S, D, blk, scale, causal_diag, bh_begin, bh_end,
                        stream);
+}
+
+namespace {
+
+// Workspace of the BSR converters: int32 flags / block-index map [Mb * Kb], int32 block_row [Mb * Kb], int32
+// counts [Mb], then a 256-byte tail: ConvTail (element nonzero counter, bad-index flag, nnzb).
+struct ConvTail {
+  unsigned long long nnz_elems;
+  int bad;
+  int pad;
+  long long nnzb;
+};
+
+struct ConvPlan {
+  int Mb = 0, Kb = 0;
+  int64_t flags_bytes = 0, counts_bytes = 0, total = 0;
+};
+
+int conv_plan(int M, int K, int bs, ConvPlan* p, const char* what) {
+  if (M < 0 || K < 0) return set_error(BSK_ERR_INVALID_ARG, "%s: negative extent", what);
+  if (bs <= 0) return set_error(BSK_ERR_INVALID_ARG, "%s: block size must be positive", what);
+  if (M % bs || K % bs)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: shape %dx%d is not divisible by the block size %d", what, M, K, bs);
+  p->Mb = M / bs;
+  p->Kb = K / bs;
+  if ((int64_t)p->Mb * p->Kb >= (int64_t)1 << 31)
+    return set_error(BSK_ERR_UNSUPPORTED, "%s: %d x %d blocks exceed the int32 block map", what, p->Mb, p->Kb);
+  p->flags_bytes = round256((int64_t)p->Mb * p->Kb * 4);
+  p->counts_bytes = round256((int64_t)p->Mb * 4);
+  p->total = 2 * p->flags_bytes + p->counts_bytes + 256;
+  return BSK_OK;
+}
+
+struct ConvWs {
+  int* flags;
+  int* block_row;
+  int* counts;
+  ConvTail* tail;
+};
+
+ConvWs conv_ws(const ConvPlan& p, void* workspace) {
+  char* ws = static_cast<char*>(workspace);
+  return {reinterpret_cast<int*>(ws), reinterpret_cast<int*>(ws + p.flags_bytes),
+          reinterpret_cast<int*>(ws + 2 * p.flags_bytes),
+          reinterpret_cast<ConvTail*>(ws + 2 * p.flags_bytes + p.counts_bytes)};
+}
+
+int conv_common_checks(int elem_bytes, int index_bytes, const ConvPlan& p, const void* workspace,
+                       int64_t workspace_bytes, const char* what) {
+  if (elem_bytes != 2 && elem_bytes != 4)
+    return set_error(BSK_ERR_UNSUPPORTED, "%s: element size %d unsupported (2 or 4 bytes)", what, elem_bytes);
+  if (index_bytes != 4 && index_bytes != 8)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: index size must be 4 or 8 bytes", what);
+  if (!workspace || workspace_bytes < p.total)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: workspace of %lld bytes needed, %lld given", what, (long long)p.total,
+                     (long long)workspace_bytes);
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: workspace must be 256-byte aligned", what);
+  return BSK_OK;
+}
+
+int conv_grid(const DeviceState* st) { return st->sm_count * 8; }
+
+int conv_clear(const ConvPlan& p, void* ws, cudaStream_t s, const char* what) {
+  cudaError_t e = cudaMemsetAsync(ws, 0, p.total, s);  // flags, block_row, counts and the tail in one fill
+  return e == cudaSuccess ? BSK_OK : cuda_fail(e, what);
+}
+
+int conv_compact(const ConvPlan& p, const ConvWs& w, const void* row_ptr, void* col_idx, int index_bytes,
+                 int64_t cap, const DeviceState* st, cudaStream_t s) {
+  using namespace bsk;
+  if (p.Mb == 0) return BSK_OK;
+  const int g = p.Mb < conv_grid(st) ? p.Mb : conv_grid(st);
+  if (index_bytes == 4)
+    bsr_compact_kernel<int32_t><<<g, kConvThreads, 0, s>>>(w.flags, p.Mb, p.Kb, static_cast<const int32_t*>(row_ptr),
+                                                           static_cast<int32_t*>(col_idx), w.block_row, cap);
+  else
+    bsr_compact_kernel<int64_t><<<g, kConvThreads, 0, s>>>(w.flags, p.Mb, p.Kb, static_cast<const int64_t*>(row_ptr),
+                                                           static_cast<int64_t*>(col_idx), w.block_row, cap);
+  return launch_status("bsr compact");
+}
+
+bool dense_vec_ok(const void* A, int64_t lda, int elem_bytes, int bs) {
+  const int per = 16 / elem_bytes;
+  return aligned16(A) && lda % per == 0 && bs % per == 0;
+}
+
+}  // namespace
+
+namespace {
+
+// Pattern pass (no host synchronisation): workspace cleared, flags (+ element count, bad flag), counts, row_ptr
+// and nnzb in the workspace tail.
+int dense_pattern_enqueue(const void* A, int64_t lda, int elem_bytes, int M, int K, int bs, void* row_ptr,
+                          int index_bytes, const ConvPlan& p, void* workspace, const DeviceState* st, cudaStream_t s,
+                          const char* what) {
+  using namespace bsk;
+  if (int rc = conv_clear(p, workspace, s, what)) return rc;
+  const ConvWs w = conv_ws(p, workspace);
+  if ((int64_t)M * K > 0) {
+    const uint8_t* a = static_cast<const uint8_t*>(A);
+    const int g = conv_grid(st);
+    unsigned long long* counter = &w.tail->nnz_elems;
+    if (dense_vec_ok(A, lda, elem_bytes, bs)) {
+      if (elem_bytes == 2) dense_flags_vec_kernel<2><<<g, kConvThreads, 0, s>>>(a, lda, M, K, bs, p.Kb, w.flags, counter);
+      else dense_flags_vec_kernel<4><<<g, kConvThreads, 0, s>>>(a, lda, M, K, bs, p.Kb, w.flags, counter);
+    } else {
+      if (elem_bytes == 2) dense_flags_scalar_kernel<2><<<g, kConvThreads, 0, s>>>(a, lda, M, K, bs, p.Kb, w.flags, counter);
+      else dense_flags_scalar_kernel<4><<<g, kConvThreads, 0, s>>>(a, lda, M, K, bs, p.Kb, w.flags, counter);
+    }
+  }
+  if (p.Mb > 0) {
+    const int g = p.Mb < conv_grid(st) ? p.Mb : conv_grid(st);
+    bsr_row_counts_kernel<<<g, kConvThreads, 0, s>>>(w.flags, p.Mb, p.Kb, w.counts);
+  }
+  if (index_bytes == 4)
+    bsr_row_ptr_kernel<int32_t><<<1, kConvThreads, 0, s>>>(w.counts, p.Mb, static_cast<int32_t*>(row_ptr), &w.tail->nnzb);
+  else
+    bsr_row_ptr_kernel<int64_t><<<1, kConvThreads, 0, s>>>(w.counts, p.Mb, static_cast<int64_t*>(row_ptr), &w.tail->nnzb);
+  return launch_status(what);
+}
+
+int csr_pattern_enqueue(const void* crow, const void* col, int index_bytes_in, const void* vals, int elem_bytes,
+                        int64_t nnz, int M, int K, int bs, void* row_ptr, int index_bytes, const ConvPlan& p,
+                        void* workspace, const DeviceState* st, cudaStream_t s, const char* what) {
+  using namespace bsk;
+  if (int rc = conv_clear(p, workspace, s, what)) return rc;
+  const ConvWs w = conv_ws(p, workspace);
+  if (M > 0 && nnz > 0) {
+    const int g = conv_grid(st);
+    if (index_bytes_in == 4)
+      launch_csr_flags<int32_t>(elem_bytes, crow, col, vals, nnz, M, K, bs, p.Kb, w.flags, &w.tail->nnz_elems,
+                                &w.tail->bad, g, s);
+    else
+      launch_csr_flags<int64_t>(elem_bytes, crow, col, vals, nnz, M, K, bs, p.Kb, w.flags, &w.tail->nnz_elems,
+                                &w.tail->bad, g, s);
+  }
+  if (p.Mb > 0) {
+    const int g = p.Mb < conv_grid(st) ? p.Mb : conv_grid(st);
+    bsr_row_counts_kernel<<<g, kConvThreads, 0, s>>>(w.flags, p.Mb, p.Kb, w.counts);
+  }
+  if (index_bytes == 4)
+    bsr_row_ptr_kernel<int32_t><<<1, kConvThreads, 0, s>>>(w.counts, p.Mb, static_cast<int32_t*>(row_ptr), &w.tail->nnzb);
+  else
+    bsr_row_ptr_kernel<int64_t><<<1, kConvThreads, 0, s>>>(w.counts, p.Mb, static_cast<int64_t*>(row_ptr), &w.tail->nnzb);
+  return launch_status(what);
+}
+
+// Reads the workspace tail back (one copy, synchronising the stream).
+int conv_read_tail(const ConvPlan& p, void* workspace, int index_bytes, int64_t* nnzb, int64_t* nnz_elems,
+                   cudaStream_t s, const char* what) {
+  const ConvWs w = conv_ws(p, workspace);
+  ConvTail t{};
+  cudaError_t e = cudaMemcpyAsync(&t, w.tail, sizeof(t), cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  if (t.bad) return set_error(BSK_ERR_INVALID_ARG, "%s: CSR column index outside [0, K)", what);
+  if (index_bytes == 4 && t.nnzb > INT32_MAX)
+    return set_error(BSK_ERR_UNSUPPORTED, "%s: %lld blocks overflow int32 indices", what, (long long)t.nnzb);
+  if (nnzb) *nnzb = t.nnzb;
+  if (nnz_elems) *nnz_elems = static_cast<int64_t>(t.nnz_elems);
+  return BSK_OK;
+}
+
+// Fill pass: col_idx, block_row and the map, then the values of the first min(nnzb, cap) blocks.
+int dense_fill_enqueue(const void* A, int64_t lda, int elem_bytes, int bs, const void* row_ptr, void* col_idx,
+                       int index_bytes, void* values, int64_t cap, const ConvPlan& p, void* workspace,
+                       const DeviceState* st, cudaStream_t s, const char* what) {
+  using namespace bsk;
+  const ConvWs w = conv_ws(p, workspace);
+  if (int rc = conv_compact(p, w, row_ptr, col_idx, index_bytes, cap, st, s)) return rc;
+  const uint8_t* a = static_cast<const uint8_t*>(A);
+  uint8_t* v = static_cast<uint8_t*>(values);
+  const bool vec = dense_vec_ok(A, lda, elem_bytes, bs) && aligned16(values);
+  const int g = conv_grid(st);
+  const int* br = w.block_row;
+  const long long* nz = &w.tail->nnzb;
+#define BSK_COPY(E, V, I) \
+  dense_block_copy_kernel<E, V, I><<<g, kConvThreads, 0, s>>>(a, lda, bs, br, static_cast<const I*>(col_idx), nz, cap, v)
+  if (index_bytes == 4) {
+    if (elem_bytes == 2) { if (vec) BSK_COPY(2, true, int32_t); else BSK_COPY(2, false, int32_t); }
+    else { if (vec) BSK_COPY(4, true, int32_t); else BSK_COPY(4, false, int32_t); }
+  } else {
+    if (elem_bytes == 2) { if (vec) BSK_COPY(2, true, int64_t); else BSK_COPY(2, false, int64_t); }
+    else { if (vec) BSK_COPY(4, true, int64_t); else BSK_COPY(4, false, int64_t); }
+  }
+#undef BSK_COPY
+  return launch_status(what);
+}
+
+int csr_fill_enqueue(const void* crow, const void* col, int index_bytes_in, const void* vals, int elem_bytes,
+                     int64_t nnz, int M, int K, int bs, const void* row_ptr, void* col_idx, int index_bytes,
+                     void* values, int64_t cap, const ConvPlan& p, void* workspace, const DeviceState* st,
+                     cudaStream_t s, const char* what) {
+  using namespace bsk;
+  const ConvWs w = conv_ws(p, workspace);
+  if (int rc = conv_compact(p, w, row_ptr, col_idx, index_bytes, cap, st, s)) return rc;
+  const int g = conv_grid(st);
+  zero_blocks_kernel<<<g, kConvThreads, 0, s>>>(static_cast<uint8_t*>(values), &w.tail->nnzb, cap,
+                                                (int64_t)bs * bs * elem_bytes);
+  if (M > 0 && nnz > 0) {
+    if (index_bytes_in == 4)
+      launch_csr_scatter<int32_t>(elem_bytes, crow, col, vals, nnz, M, K, bs, p.Kb, w.flags, cap, values, g, s);
+    else
+      launch_csr_scatter<int64_t>(elem_bytes, crow, col, vals, nnz, M, K, bs, p.Kb, w.flags, cap, values, g, s);
+  }
+  return launch_status(what);
+}
+
+int csr_checks(const void* crow, const void* col, int index_bytes_in, const void* vals, int64_t nnz, int M,
+               const char* what) {
+  if (index_bytes_in != 4 && index_bytes_in != 8)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: CSR index size must be 4 or 8 bytes", what);
+  if (nnz < 0) return set_error(BSK_ERR_INVALID_ARG, "%s: negative nnz", what);
+  if (!crow && M > 0) return set_error(BSK_ERR_INVALID_ARG, "%s: null crow_indices", what);
+  if (nnz > 0 && (!col || !vals)) return set_error(BSK_ERR_INVALID_ARG, "%s: null col_indices/values", what);
+  return BSK_OK;
+}
+
+int dense_checks(const void* A, int64_t lda, int elem_bytes, int index_bytes, int M, int K, int bs, ConvPlan* p,
+                 const void* workspace, int64_t workspace_bytes, const char* what) {
+  if (int rc = conv_plan(M, K, bs, p, what)) return rc;
+  if (int rc = conv_common_checks(elem_bytes, index_bytes, *p, workspace, workspace_bytes, what)) return rc;
+  if (lda < K) return set_error(BSK_ERR_INVALID_ARG, "%s: lda < K", what);
+  if (!A && M > 0 && K > 0) return set_error(BSK_ERR_INVALID_ARG, "%s: null A", what);
+  return BSK_OK;
+}
+
+}  // namespace
+
+int64_t bsk_bsr_convert_workspace_bytes(int M, int K, int bs) {
+  ConvPlan p;
+  if (int rc = conv_plan(M, K, bs, &p, "bsr_convert")) return rc;
+  return p.total;
+}
+
+int bsk_dense_to_bsr_pattern(const void* A, int64_t lda, int elem_bytes, int M, int K, int bs, void* row_ptr,
+                             int index_bytes, void* workspace, int64_t workspace_bytes, int64_t* nnzb,
+                             int64_t* nnz_elems, void* stream) {
+  const char* what = "dense_to_bsr_pattern";
+  ConvPlan p;
+  if (int rc = dense_checks(A, lda, elem_bytes, index_bytes, M, K, bs, &p, workspace, workspace_bytes, what)) return rc;
+  if (!row_ptr) return set_error(BSK_ERR_INVALID_ARG, "%s: null row_ptr", what);
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (int rc = dense_pattern_enqueue(A, lda, elem_bytes, M, K, bs, row_ptr, index_bytes, p, workspace, st, s, what))
+    return rc;
+  return conv_read_tail(p, workspace, index_bytes, nnzb, nnz_elems, s, what);
+}
+
+int bsk_dense_to_bsr_fill(const void* A, int64_t lda, int elem_bytes, int M, int K, int bs, const void* row_ptr,
+                          void* col_idx, int index_bytes, void* values, int64_t nnzb, void* workspace,
+                          int64_t workspace_bytes, void* stream) {
+  const char* what = "dense_to_bsr_fill";
+  ConvPlan p;
+  if (int rc = dense_checks(A, lda, elem_bytes, index_bytes, M, K, bs, &p, workspace, workspace_bytes, what)) return rc;
+  if (nnzb < 0) return set_error(BSK_ERR_INVALID_ARG, "%s: negative nnzb", what);
+  if ((int64_t)M * K == 0 || nnzb == 0) return BSK_OK;
+  if (!row_ptr || !col_idx || !values) return set_error(BSK_ERR_INVALID_ARG, "%s: null pointer", what);
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  return dense_fill_enqueue(A, lda, elem_bytes, bs, row_ptr, col_idx, index_bytes, values, nnzb, p, workspace, st,
+                            static_cast<cudaStream_t>(stream), what);
+}
+
+int bsk_dense_to_bsr_bounded(const void* A, int64_t lda, int elem_bytes, int M, int K, int bs, void* row_ptr,
+                             void* col_idx, int index_bytes, void* values, int64_t max_nnzb, void* workspace,
+                             int64_t workspace_bytes, void* stream) {
+  const char* what = "dense_to_bsr_bounded";
+  ConvPlan p;
+  if (int rc = dense_checks(A, lda, elem_bytes, index_bytes, M, K, bs, &p, workspace, workspace_bytes, what)) return rc;
+  if (max_nnzb < 0) return set_error(BSK_ERR_INVALID_ARG, "%s: negative max_nnzb", what);
+  if (!row_ptr || (max_nnzb > 0 && (!col_idx || !values)))
+    return set_error(BSK_ERR_INVALID_ARG, "%s: null output pointer", what);
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (int rc = dense_pattern_enqueue(A, lda, elem_bytes, M, K, bs, row_ptr, index_bytes, p, workspace, st, s, what))
+    return rc;
+  if (max_nnzb == 0 || (int64_t)M * K == 0) return BSK_OK;
+  return dense_fill_enqueue(A, lda, elem_bytes, bs, row_ptr, col_idx, index_bytes, values, max_nnzb, p, workspace,
+                            st, s, what);
+}
+
+int bsk_csr_to_bsr_pattern(const void* crow, const void* col, int index_bytes_in, const void* vals, int elem_bytes,
+                           int64_t nnz, int M, int K, int bs, void* row_ptr, int index_bytes, void* workspace,
+                           int64_t workspace_bytes, int64_t* nnzb, int64_t* nnz_elems, void* stream) {
+  const char* what = "csr_to_bsr_pattern";
+  ConvPlan p;
+  if (int rc = conv_plan(M, K, bs, &p, what)) return rc;
+  if (int rc = conv_common_checks(elem_bytes, index_bytes, p, workspace, workspace_bytes, what)) return rc;
+  if (int rc = csr_checks(crow, col, index_bytes_in, vals, nnz, M, what)) return rc;
+  if (!row_ptr) return set_error(BSK_ERR_INVALID_ARG, "%s: null row_ptr", what);
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (int rc = csr_pattern_enqueue(crow, col, index_bytes_in, vals, elem_bytes, nnz, M, K, bs, row_ptr, index_bytes, p,
+                                   workspace, st, s, what))
+    return rc;
+  return conv_read_tail(p, workspace, index_bytes, nnzb, nnz_elems, s, what);
+}
+
+int bsk_csr_to_bsr_fill(const void* crow, const void* col, int index_bytes_in, const void* vals, int elem_bytes,
+                        int64_t nnz, int M, int K, int bs, const void* row_ptr, void* col_idx, int index_bytes,
+                        void* values, int64_t nnzb, void* workspace, int64_t workspace_bytes, void* stream) {
+  const char* what = "csr_to_bsr_fill";
+  ConvPlan p;
+  if (int rc = conv_plan(M, K, bs, &p, what)) return rc;
+  if (int rc = conv_common_checks(elem_bytes, index_bytes, p, workspace, workspace_bytes, what)) return rc;
+  if (int rc = csr_checks(crow, col, index_bytes_in, vals, nnz, M, what)) return rc;
+  if (nnzb < 0) return set_error(BSK_ERR_INVALID_ARG, "%s: negative nnzb", what);
+  if (nnzb == 0) return BSK_OK;
+  if (!row_ptr || !col_idx || !values) return set_error(BSK_ERR_INVALID_ARG, "%s: null output pointer", what);
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  return csr_fill_enqueue(crow, col, index_bytes_in, vals, elem_bytes, nnz, M, K, bs, row_ptr, col_idx, index_bytes,
+                          values, nnzb, p, workspace, st, static_cast<cudaStream_t>(stream), what);
+}
+
+int bsk_csr_to_bsr_bounded(const void* crow, const void* col, int index_bytes_in, const void* vals, int elem_bytes,
+                           int64_t nnz, int M, int K, int bs, void* row_ptr, void* col_idx, int index_bytes,
+                           void* values, int64_t max_nnzb, void* workspace, int64_t workspace_bytes, void* stream) {
+  const char* what = "csr_to_bsr_bounded";
+  ConvPlan p;
+  if (int rc = conv_plan(M, K, bs, &p, what)) return rc;
+  if (int rc = conv_common_checks(elem_bytes, index_bytes, p, workspace, workspace_bytes, what)) return rc;
+  if (int rc = csr_checks(crow, col, index_bytes_in, vals, nnz, M, what)) return rc;
+  if (max_nnzb < 0) return set_error(BSK_ERR_INVALID_ARG, "%s: negative max_nnzb", what);
+  if (!row_ptr || (max_nnzb > 0 && (!col_idx || !values)))
+    return set_error(BSK_ERR_INVALID_ARG, "%s: null output pointer", what);
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (int rc = csr_pattern_enqueue(crow, col, index_bytes_in, vals, elem_bytes, nnz, M, K, bs, row_ptr, index_bytes, p,
+                                   workspace, st, s, what))
+    return rc;
+  if (max_nnzb == 0) return BSK_OK;
+  return csr_fill_enqueue(crow, col, index_bytes_in, vals, elem_bytes, nnz, M, K, bs, row_ptr, col_idx, index_bytes,
+                          values, max_nnzb, p, workspace, st, s, what);
 }
 
 int bsk_device_error(uint32_t* out) {

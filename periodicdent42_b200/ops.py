@@ -76,8 +76,9 @@ def sparse_mm(A: torch.Tensor, B: torch.Tensor, block_size: int = 16, autotune: 
 
 
 def _to_kernel_bsr(A: torch.Tensor) -> torch.Tensor:
-    """BSR with 128x128 blocks, on A's device. CSR or other block sizes are re-blocked through the dense
-    form (the reference left CSR -> BSR unimplemented, ops.py:193-197)."""
+    """BSR with 128x128 blocks, on A's device: CSR / COO input through the device converter; BSR with another
+    block size re-blocked through its dense form (the reference left CSR -> BSR unimplemented,
+    ops.py:193-197)."""
     if A.layout == torch.sparse_bsr and tuple(A.values().shape[1:]) == (KERNEL_BLOCK, KERNEL_BLOCK):
         return A
     if A.layout not in (torch.sparse_csr, torch.sparse_bsr, torch.sparse_coo):
@@ -89,7 +90,14 @@ def _to_kernel_bsr(A: torch.Tensor) -> torch.Tensor:
 
 
 def _convert_csr_to_bsr(A_csr: torch.Tensor, block_size: int) -> torch.Tensor:
-    """Sparse (CSR / COO / BSR) -> BSR with square blocks, keeping only blocks that hold a nonzero."""
+    """Sparse (CSR / COO / BSR) -> BSR with square blocks, keeping only blocks that hold a nonzero (the
+    reference's stub, ops.py:193-197). On CUDA: CSR / COO by the device CSR converter, BSR of another block size
+    by the device dense converter on its dense form; on the CPU through torch's dense form."""
+    if A_csr.is_cuda and A_csr.dtype in (torch.float16, torch.bfloat16, torch.float32):
+        from .utils import convert_to_bsr
+
+        src = A_csr.to_dense() if A_csr.layout == torch.sparse_bsr else A_csr
+        return convert_to_bsr(src, block_size, sparsity_threshold=0.0)
     return A_csr.to_dense().to_sparse_bsr((block_size, block_size))
 
 

@@ -9,9 +9,32 @@ import torch
 def convert_to_bsr(matrix: torch.Tensor, block_size: int = 16, sparsity_threshold: float = 0.5) -> torch.Tensor:
     """Dense / CSR / COO -> BSR with square ``block_size`` blocks (utils.py:10-57). BSR input is returned
     unchanged. Warns (prints, as the reference does) when the matrix is less sparse than the threshold.
-    The sm_100 kernel computes on 128x128 blocks; ``sparse_mm`` re-blocks other sizes itself."""
+
+    CUDA matrices (fp16 / bf16 / fp32; dense, CSR, or COO) are converted on the GPU by the library's converter
+    kernels (one pass over the matrix for the block pattern and the nonzero count, one for the blocks), with
+    the result torch's ``to_sparse_bsr`` gives; CPU matrices go through torch as in the reference. The sm_100
+    SpMM computes on 128x128 blocks; ``sparse_mm`` re-blocks other sizes itself."""
     if matrix.layout == torch.sparse_bsr:
         return matrix
+    if matrix.is_cuda and matrix.dtype in (torch.float16, torch.bfloat16, torch.float32) and matrix.dim() == 2:
+        from . import _capi
+
+        M, K = matrix.shape
+        if matrix.layout == torch.sparse_coo:
+            matrix = matrix.coalesce().to_sparse_csr()
+        if matrix.layout == torch.sparse_csr:
+            rp, ci, vals, nnz = _capi.csr_to_bsr(matrix.crow_indices(), matrix.col_indices(), matrix.values(),
+                                                 (M, K), block_size)
+        elif matrix.layout == torch.strided:
+            dense = matrix if matrix.stride(1) == 1 or matrix.numel() == 0 else matrix.contiguous()
+            rp, ci, vals, nnz = _capi.dense_to_bsr(dense, block_size)
+        else:
+            raise ValueError(f"Unsupported layout: {matrix.layout}")
+        total = M * K
+        sparsity = 1.0 - (nnz / total) if total else 0.0
+        if sparsity < sparsity_threshold:
+            print(f"Warning: Matrix is only {sparsity:.1%} sparse. Dense operations may be faster.")
+        return torch.sparse_bsr_tensor(rp, ci, vals, size=(M, K))
     if matrix.layout != torch.strided:
         matrix = matrix.to_dense()
     nnz = torch.count_nonzero(matrix).item()
