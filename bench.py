@@ -48,7 +48,7 @@ def parse_args():
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--ops", default="dense,fp8,bsr,attn,convert", help="comma list; dense is the headline")
+    p.add_argument("--ops", default="dense,fp8,bsr,attn,convert,bsr_bsr", help="comma list; dense is the headline")
     p.add_argument("--dense-mode", choices=["nshard", "splitk", "splitk_nccl"], default="nshard",
                    help="nshard: N-sharded, no communication; splitk: K split across ranks, reduce-scatter fused "
                         "into the GEMM (peer-memory epilogue); splitk_nccl: K split + NCCL reduce_scatter")
@@ -353,6 +353,34 @@ def bench_bsr(ctx: Ctx, args, res: dict):
     torch.cuda.empty_cache()
 
 
+# ----------------------------------------------------------------------------------------- BSR x BSR
+def bench_bsr_bsr(ctx: Ctx, args, res: dict):
+    """A = the BSR workload's matrix (8192 x 8192, 16 of 64 128x128 blocks per block-row); B = a second 8192 x 8192
+    BSR matrix with the same density (seed 5). Useful FLOPs = 2 * 128^3 per (A block, B block) pair that meet.
+    Block-rows sharded like the BSR SpMM at N > 1."""
+    cfg = wl.BSR
+    crow, col, vals, _ = wl.bsr_inputs(cfg, ctx.dev)
+    Kb, Nb = cfg.K // cfg.block, cfg.N // cfg.block
+    bcrow, bcol = wl.bsr_pattern(Kb, Nb, cfg.nnz_per_row, torch.Generator().manual_seed(5))
+    g = torch.Generator(device=ctx.dev).manual_seed(5)
+    bvals = torch.randn(int(bcrow[-1]), 128, 128, generator=g, device=ctx.dev).half()
+    b_per_row = (bcrow[1:] - bcrow[:-1])
+    pairs = int(b_per_row[col.cpu().long()].sum())  # sum over A blocks (i, k) of B's blocks in row k
+    flops = 2 * 128 ** 3 * pairs
+    r0, r1 = sharding.bsr_block_rows(crow.cpu(), ctx.world, ctx.rank)
+    rp, ci = crow.to(torch.int32), col.to(torch.int32)
+    brp, bci = bcrow.to(torch.int32).to(ctx.dev), bcol.to(torch.int32).to(ctx.dev)
+    C = torch.empty(cfg.M, cfg.N, device=ctx.dev)
+
+    def step():
+        _capi.spmm_bsr_bsr_f16f32(rp, ci, vals, brp, bci, bvals, C, cfg.M, cfg.N, cfg.K, r0, r1, stream=ctx.stream)
+    ms = time_region(ctx, step, args.op_steps, args.warmup, "bsr_bsr")
+    res["bsr_bsr"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "flops": flops, "launches_per_step": 1,
+                      "block_pairs": pairs, "nnzb": int(crow[-1].item()), "b_nnzb": int(bcrow[-1])}
+    del crow, col, vals, bvals, C
+    torch.cuda.empty_cache()
+
+
 # ----------------------------------------------------------------------------------------- BSR conversion
 def bench_convert(ctx: Ctx, args, res: dict):
     """Dense -> BSR and CSR -> BSR on the device for the BSR workload's matrix (8192 x 8192 fp16, 1024 of 4096
@@ -521,7 +549,7 @@ def main():
     try:
         for op in ops:
             {"dense": bench_dense, "fp8": bench_fp8, "bsr": bench_bsr, "attn": bench_attn,
-             "convert": bench_convert}[op](ctx, args, res)
+             "convert": bench_convert, "bsr_bsr": bench_bsr_bsr}[op](ctx, args, res)
     finally:
         clk = clocks.stop() if clocks else None
     err_word = _capi.device_error()
@@ -560,14 +588,14 @@ def main():
         line["cpu_baseline"] = cpu
         line["clocks"] = clk
         opsum = {}
-        for name in ("fp8", "bsr", "attn"):
+        for name in ("fp8", "bsr", "attn", "bsr_bsr"):
             if name in res:
                 r = res[name]
                 pk = peak_t * (2 if name == "fp8" else 1)
                 opsum[name] = {"tflops": r["tflops"], "ms": r["ms"],
                                "frac_of_peak": r["tflops"] / ctx.world / pk,
                                "peak": pk, "peak_basis": ("2 x " if name == "fp8" else "") + "measured bf16 sustained"}
-                for kk in ("nnzb", "nnz_blocks"):
+                for kk in ("nnzb", "nnz_blocks", "block_pairs", "b_nnzb"):
                     if kk in r:
                         opsum[name][kk] = r[kk]
         if "convert" in res:

@@ -181,6 +181,21 @@ int bsk_spmm_bsr_f16f32(const int32_t* row_ptr, const int32_t* col_idx, const vo
                         int row_begin, int row_end, void* stream);
 
 /*
+ * BSR x BSR SpMM, fp16 -> fp32:  C[M,N] = A_bsr[M,K] * B_bsr[K,N], both with 128 x 128 blocks, C dense.
+ *   A: a_row_ptr [Mb + 1], a_col_idx [a_nnzb], a_vals [a_nnzb, 128, 128] (as bsk_spmm_bsr_f16f32).
+ *   B: b_row_ptr [K/128 + 1], b_col_idx [b_nnzb] ascending within each block-row (the kernel binary-searches
+ *      them), b_vals [b_nnzb, 128, 128] row-major blocks. Missing blocks are zero.
+ *   M, K, N multiples of 128; block-rows [row_begin, row_end) of C are written.
+ * Replaces the sparse-B case of launch_bsr_spmm_async (BlackwellSparseK/src/kernel_launch.cu:33-61, whose
+ * kernel looks B blocks up by binary search, src/sparse_h100_async.cu:105-119); launch_bsr_spmm_async
+ * routes a B with fewer than (K/128) x (N/128) stored blocks here.
+ */
+int bsk_spmm_bsr_bsr_f16f32(const int32_t* a_row_ptr, const int32_t* a_col_idx, const void* a_vals, int Mb,
+                            int a_nnzb, const int32_t* b_row_ptr, const int32_t* b_col_idx, const void* b_vals,
+                            int b_nnzb, float* C, int64_t ldc, int M, int N, int K, int row_begin, int row_end,
+                            void* stream);
+
+/*
  * Host-side check of a BSR index structure held in HOST memory (row_ptr[0] == 0, non-decreasing,
  * row_ptr[Mb] == nnzb, 0 <= col_idx < Kb). Returns BSK_OK or BSK_ERR_INVALID_ARG with a message.
  * The reference performs no such check (BlackwellSparseK/python/ops.py:56-69 validates shapes only).
@@ -262,9 +277,9 @@ int bsk_csr_to_bsr_bounded(const void* crow, const void* col, int index_bytes_in
 
 /*
  * Drop-in for the reference's launcher signature (BlackwellSparseK/src/kernel_launch.cu:33-61).
- * A is BSR with blocks of (M/A_M_blocks) x (K/A_K_blocks); B must be the all-blocks pattern the reference
- * Python layer builds (BlackwellSparseK/python/ops.py:104-107), whose value buffer is the dense row-major
- * [K, N] matrix. BM/BN/BK are accepted and ignored (the sm_100 kernel picks its own tiles). Returns
+ * A is BSR with blocks of (M/A_M_blocks) x (K/A_K_blocks). A B with every block present is read as the dense
+ * row-major [K, N] matrix the reference Python layer passes (BlackwellSparseK/python/ops.py:104-107); a B with
+ * fewer blocks is a true BSR operand (128 x 128 blocks) and goes to bsk_spmm_bsr_bsr_f16f32. BM/BN/BK are accepted and ignored (the sm_100 kernel picks its own tiles). Returns
  * nothing, like the reference; failures are reported through bsk_last_error().
  */
 void launch_bsr_spmm_async(const int* A_row_ptr, const int* A_col_idx, const void* A_vals, int A_M_blocks,

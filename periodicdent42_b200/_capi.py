@@ -51,6 +51,8 @@ SIGNATURES = {
     "bsk_spmm_bsr_f16f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp, _i64, _vp, _i64, _i32, _i32, _i32,
                                    _i32, _i32, _vp]),
     "bsk_bsr_validate_host": (_i32, [_vp, _vp, _i32, _i32, _i32]),
+    "bsk_spmm_bsr_bsr_f16f32": (_i32, [_vp, _vp, _vp, _i32, _i32, _vp, _vp, _vp, _i32, _vp, _i64, _i32, _i32, _i32,
+                                       _i32, _i32, _vp]),
     "bsk_bsr_convert_workspace_bytes": (_i64, [_i32, _i32, _i32]),
     "bsk_dense_to_bsr_pattern": (_i32, [_vp, _i64, _i32, _i32, _i32, _i32, _vp, _i32, _vp, _i64,
                                         ctypes.POINTER(_i64), ctypes.POINTER(_i64), _vp]),
@@ -222,6 +224,17 @@ def spmm_bsr_f16f32(row_ptr, col_idx, vals, B, C, M: int, row_begin: int = 0, ro
     check(lib().bsk_spmm_bsr_f16f32(_ptr(row_ptr), _ptr(col_idx), _ptr(vals), br, bc, Mb, nnzb, _ptr(B), B.stride(0),
                                     _ptr(C), C.stride(0), M, N, K, row_begin, row_end, _stream(stream)),
           "bsk_spmm_bsr_f16f32")
+
+
+def spmm_bsr_bsr_f16f32(a_row_ptr, a_col_idx, a_vals, b_row_ptr, b_col_idx, b_vals, C, M: int, N: int, K: int,
+                        row_begin: int = 0, row_end: int | None = None, stream=None) -> None:
+    """C = A_bsr @ B_bsr (both 128x128 blocks, int32 indices, fp16 values [nnzb, 128, 128]) into fp32 C."""
+    Mb = M // 128
+    row_end = Mb if row_end is None else row_end
+    check(lib().bsk_spmm_bsr_bsr_f16f32(_ptr(a_row_ptr), _ptr(a_col_idx), _ptr(a_vals), Mb, a_col_idx.numel(),
+                                        _ptr(b_row_ptr), _ptr(b_col_idx), _ptr(b_vals), b_col_idx.numel(), _ptr(C),
+                                        C.stride(0), M, N, K, row_begin, row_end, _stream(stream)),
+          "bsk_spmm_bsr_bsr_f16f32")
 
 
 def bsattn_fwd_bf16(Q, K, V, O, row_ptr, col_idx, scale: float, causal_diag: bool = True, bh_begin: int = 0,

@@ -30,8 +30,6 @@ torch::Tensor as_int32(const torch::Tensor& t) {
 torch::Tensor sparse_mm_bsr(torch::Tensor A_row_ptr, torch::Tensor A_col_idx, torch::Tensor A_vals,
                             torch::Tensor B_row_ptr, torch::Tensor B_col_idx, torch::Tensor B_vals, int64_t M,
                             int64_t N, int64_t K, int64_t BM, int64_t BN, int64_t BK) {
-  (void)B_row_ptr;
-  (void)B_col_idx;
   (void)BM;
   (void)BN;
   (void)BK;
@@ -40,8 +38,33 @@ torch::Tensor sparse_mm_bsr(torch::Tensor A_row_ptr, torch::Tensor A_col_idx, to
   TORCH_CHECK(A_vals.scalar_type() == torch::kFloat16, "A_vals must be float16");
   TORCH_CHECK(B_vals.scalar_type() == torch::kFloat16, "B_vals must be float16");
   TORCH_CHECK(A_vals.dim() == 3, "A_vals must be [nnzb, block_rows, block_cols]");
-  TORCH_CHECK(B_vals.numel() == K * N, "B_vals must hold the dense K x N operand");
   const at::cuda::CUDAGuard guard(A_vals.device());
+  // A sparse B (fewer stored blocks than the full (K/128) x (N/128) grid): B_vals are its 128 x 128 blocks, located
+  // through B_row_ptr / B_col_idx (the reference kernel's binary search, src/sparse_h100_async.cu:105-119). With
+  // every block present, B_vals is read as the dense row-major K x N operand, as the reference's Python layer
+  // passes it (python/ops.py:104-107).
+  const int64_t full_b = (K / 128) * (N / 128);
+  if (B_vals.dim() == 3 && B_vals.size(1) == 128 && B_vals.size(2) == 128 && B_col_idx.numel() < full_b) {
+    TORCH_CHECK(B_row_ptr.is_cuda() && B_col_idx.is_cuda(), "sparse_mm_bsr: B indices must be CUDA tensors");
+    TORCH_CHECK(B_row_ptr.numel() == K / 128 + 1, "sparse_mm_bsr: B_row_ptr must have K/128 + 1 entries");
+    auto rp = as_int32(A_row_ptr);
+    auto ci = as_int32(A_col_idx);
+    auto brp = as_int32(B_row_ptr);
+    auto bci = as_int32(B_col_idx);
+    auto av = A_vals.contiguous();
+    auto bv = B_vals.contiguous();
+    const int Mb = static_cast<int>(rp.numel() - 1);
+    TORCH_CHECK(av.size(1) == 128 && av.size(2) == 128 && Mb * 128 == M, "sparse_mm_bsr: A needs 128x128 blocks");
+    auto C = torch::empty({M, N}, A_vals.options().dtype(torch::kFloat32));
+    check_rc(bsk_spmm_bsr_bsr_f16f32(rp.data_ptr<int32_t>(), ci.data_ptr<int32_t>(), av.data_ptr(), Mb,
+                                     static_cast<int>(ci.numel()), brp.data_ptr<int32_t>(), bci.data_ptr<int32_t>(),
+                                     bv.data_ptr(), static_cast<int>(bci.numel()), C.data_ptr<float>(), N,
+                                     static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), 0, Mb,
+                                     stream_of(C)),
+             "bsk_spmm_bsr_bsr_f16f32");
+    return C;
+  }
+  TORCH_CHECK(B_vals.numel() == K * N, "B_vals must hold the dense K x N operand");
   auto rp = as_int32(A_row_ptr);
   auto ci = as_int32(A_col_idx);
   auto vals = A_vals.contiguous();

@@ -115,6 +115,7 @@ void init_device(DeviceState& st, int dev) {
       allow_smem(gemm_sm100_kernel<2, Mainloop::Dense, Epi::F32>, kGemmSmemBytes),
       allow_smem(gemm_sm100_kernel<1, Mainloop::Dense, Epi::BF16Scaled>, kGemmSmemBytes),
       allow_smem(gemm_sm100_kernel<2, Mainloop::Bsr, Epi::F32>, kGemmSmemBytes),
+      allow_smem(gemm_sm100_kernel<2, Mainloop::BsrBsr, Epi::F32>, kGemmSmemBytes),
       allow_smem(bsattn_sm100_kernel<false, 128>, AttnShape<false, 128>::kSmemBytes),
       allow_smem(bsattn_sm100_kernel<false, 64>, AttnShape<false, 64>::kSmemBytes),
       allow_smem(bsattn_sm100_kernel<true, 128>, AttnShape<true, 128>::kSmemBytes),
@@ -889,6 +890,69 @@ int bsk_spmm_bsr_f16f32(const int32_t* row_ptr, const int32_t* col_idx, const vo
   return launch_status("spmm_bsr launch");
 }
 
+int bsk_spmm_bsr_bsr_f16f32(const int32_t* a_row_ptr, const int32_t* a_col_idx, const void* a_vals, int Mb,
+                            int a_nnzb, const int32_t* b_row_ptr, const int32_t* b_col_idx, const void* b_vals,
+                            int b_nnzb, float* C, int64_t ldc, int M, int N, int K, int row_begin, int row_end,
+                            void* stream) {
+  using namespace bsk;
+  const char* what = "spmm_bsr_bsr";
+  if (M < 0 || N < 0 || K < 0 || Mb < 0 || a_nnzb < 0 || b_nnzb < 0)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: negative extent", what);
+  if (M != Mb * 128 || K % 128 || N % 128)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: M=%d, K=%d, N=%d must be multiples of the 128 block size (Mb=%d)", what,
+                     M, K, N, Mb);
+  if ((int64_t)b_nnzb * 128 + 128 >= ((int64_t)1 << 31))
+    return set_error(BSK_ERR_UNSUPPORTED, "%s: %d stored B blocks exceed the tensor-map row range", what, b_nnzb);
+  if (row_begin < 0 || row_end > Mb || row_begin > row_end)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: bad block-row range [%d, %d) for Mb=%d", what, row_begin, row_end, Mb);
+  if (ldc < N) return set_error(BSK_ERR_INVALID_ARG, "%s: ldc < N", what);
+  if (!a_row_ptr || !C || (K > 0 && !b_row_ptr) || (a_nnzb > 0 && (!a_col_idx || !a_vals)) ||
+      (b_nnzb > 0 && (!b_col_idx || !b_vals)))
+    return set_error(BSK_ERR_INVALID_ARG, "%s: null pointer", what);
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  if (row_end == row_begin || N == 0) return BSK_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (K == 0 || a_nnzb == 0 || b_nnzb == 0) {
+    float* c0 = C + static_cast<int64_t>(row_begin) * 128 * ldc;
+    cudaError_t e = cudaMemset2DAsync(c0, ldc * sizeof(float), 0, (size_t)N * sizeof(float),
+                                      (size_t)(row_end - row_begin) * 128, s);
+    return e == cudaSuccess ? BSK_OK : cuda_fail(e, what);
+  }
+  CUtensorMap ta, tb;
+  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, a_vals, 128, (uint64_t)a_nnzb * 128, 256, 64, 128,
+                        "A values"))
+    return rc;
+  // B's blocks stacked as rows: block p, K row r -> row p*128 + r; 64 x 64 boxes (one MN-major slab of a stage)
+  if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, b_vals, 128, (uint64_t)b_nnzb * 128, 256, 64, 64,
+                        "B values"))
+    return rc;
+  GemmArgs a{};
+  a.M = M;
+  a.N = N;
+  a.num_m_tiles = row_end - row_begin;
+  a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
+  a.group_m = pick_group_m(a.num_m_tiles);
+  a.k_splits = 1;
+  a.out = C;
+  a.ldo = ldc;
+  a.vec_ok = aligned16(C) && (ldc % 4 == 0);
+  a.row_ptr = a_row_ptr;
+  a.col_idx = a_col_idx;
+  a.row_begin = row_begin;
+  a.nnzb = a_nnzb;
+  a.kb_count = K / 128;
+  a.b_row_ptr = b_row_ptr;
+  a.b_col_idx = b_col_idx;
+  a.b_nnzb = b_nnzb;
+  a.err = st->err_word;
+  a.timeout_ns = t_timeout_ns;
+  const int tiles = a.num_m_tiles * a.num_n_tiles;
+  const int grid = tiles < st->sm_count ? tiles : st->sm_count;
+  gemm_sm100_kernel<2, Mainloop::BsrBsr, Epi::F32><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
+  return launch_status("spmm_bsr_bsr launch");
+}
+
 void launch_bsr_spmm_async(const int* A_row_ptr, const int* A_col_idx, const void* A_vals, int A_M_blocks,
                            int A_K_blocks, int A_nnzb, const int* B_row_ptr, const int* B_col_idx, const void* B_vals,
                            int B_K_blocks, int B_N_blocks, int B_nnzb, float* C, int M, int N, int K, int ldc, int BM,
@@ -902,8 +966,15 @@ void launch_bsr_spmm_async(const int* A_row_ptr, const int* A_col_idx, const voi
     set_error(BSK_ERR_INVALID_ARG, "launch_bsr_spmm_async: M/K not divisible by the block counts");
     return;
   }
-  if (B_nnzb != B_K_blocks * B_N_blocks) {
-    set_error(BSK_ERR_UNSUPPORTED, "launch_bsr_spmm_async: only the dense all-blocks B pattern is supported");
+  if (B_nnzb != B_K_blocks * B_N_blocks) {  // a sparse B: its values are blocks, found by B's row_ptr / col_idx
+    if (B_K_blocks != A_K_blocks || B_K_blocks <= 0 || B_N_blocks <= 0 || K / B_K_blocks != 128 ||
+        N / B_N_blocks != 128) {
+      set_error(BSK_ERR_UNSUPPORTED, "launch_bsr_spmm_async: a sparse B needs 128x128 blocks matching A's K blocking");
+      return;
+    }
+    const int rc = bsk_spmm_bsr_bsr_f16f32(A_row_ptr, A_col_idx, A_vals, A_M_blocks, A_nnzb, B_row_ptr, B_col_idx,
+                                           B_vals, B_nnzb, C, ldc, M, N, K, 0, A_M_blocks, stream);
+    if (rc == BSK_OK) t_last_error.clear();
     return;
   }
   const int rc = bsk_spmm_bsr_f16f32(A_row_ptr, A_col_idx, A_vals, M / A_M_blocks, K / A_K_blocks, A_M_blocks,

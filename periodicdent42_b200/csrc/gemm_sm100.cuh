@@ -29,13 +29,14 @@ constexpr int kGemmBStage = kGemmBN * kGemmRowBytes;  // 32 KB
 constexpr int kGemmTmemCols = 512;
 constexpr int kGemmSmemBytes = 1024 /*align slack*/ + kGemmStages * (kGemmAStage + kGemmBStage) + 256;
 
-enum class Mainloop : int { Dense = 0, Bsr = 1 };
+enum class Mainloop : int { Dense = 0, Bsr = 1, BsrBsr = 2 };
 // F32PeerRows: fp32 partial rows stored into their owner rank's receive slot (split-K reduce-scatter).
 enum class Epi : int { F32 = 0, BF16Scaled = 1, F32PeerRows = 2 };
 constexpr int kMaxPeers = 8;
 
 // Kernel ids recorded in the device error word.
-enum : uint32_t { kKidGemmF16 = 1, kKidGemmE4m3 = 2, kKidSpmmBsr = 3, kKidBsAttn = 4, kKidWaitProbe = 5 };
+enum : uint32_t { kKidGemmF16 = 1, kKidGemmE4m3 = 2, kKidSpmmBsr = 3, kKidBsAttn = 4, kKidWaitProbe = 5,
+                  kKidSpmmBsrBsr = 6 };
 
 struct GemmArgs {
   int M, N;                  // output extent (rows / cols of C that exist)
@@ -59,6 +60,9 @@ struct GemmArgs {
   int rows_per_rank;           // F32PeerRows: output rows owned by each rank
   int my_rank;                 // F32PeerRows: slot this rank writes in every owner's buffer
   int accumulate;              // F32 only: C += result (C read before the store) instead of C = result
+  const int* b_row_ptr;        // BSR x BSR only: B's block-row pointer (K/128 + 1 entries, int32)
+  const int* b_col_idx;        // BSR x BSR only: B's block columns, ascending within each block-row
+  int b_nnzb;                  // BSR x BSR only: B's stored blocks (a load at block b_nnzb reads zero fill)
   uint32_t* err;
   uint64_t timeout_ns;
 };
@@ -81,6 +85,44 @@ __device__ __forceinline__ bool bsr_row_range(const GemmArgs& a, int r, int& j0,
   j0 = min(max(p0, 0), a.nnzb);
   j1 = min(max(p1, j0), a.nnzb);
   return j0 == p0 && j1 == p1;
+}
+
+// Position of B block (kb, jc) in B's BSR arrays, or -1: binary search of the ascending block-row kb (row
+// pointers clamped to [0, b_nnzb]).
+__device__ __forceinline__ int bsr_b_find(const GemmArgs& a, int kb, int jc) {
+  int lo = min(max(__ldg(&a.b_row_ptr[kb]), 0), a.b_nnzb);
+  int hi = min(max(__ldg(&a.b_row_ptr[kb + 1]), lo), a.b_nnzb);
+  const int end = hi;
+  while (lo < hi) {
+    const int mid = (lo + hi) >> 1;
+    if (__ldg(&a.b_col_idx[mid]) < jc) lo = mid + 1; else hi = mid;
+  }
+  return (lo < end && __ldg(&a.b_col_idx[lo]) == jc) ? lo : -1;
+}
+
+// BSR x BSR: for A's stored block j (block column kb = col_idx[j]) and the output tile whose first block column
+// is jc, the B blocks (kb, jc) and (kb, jc + 1). Returns false when neither exists or kb is out of range (the
+// A block then contributes nothing to the tile).
+__device__ __forceinline__ bool bsrbsr_pair(const GemmArgs& a, int j, int jc, int& p0, int& p1) {
+  const int kb = __ldg(&a.col_idx[j]);
+  p0 = p1 = -1;
+  if (kb < 0 || kb >= a.kb_count) return false;
+  p0 = bsr_b_find(a, kb, jc);
+  p1 = bsr_b_find(a, kb, jc + 1);
+  return p0 >= 0 || p1 >= 0;
+}
+
+// Warp-collective: how many of A's blocks [j0, j1) contribute to the tile starting at block column jc (32 blocks
+// examined per round, one per lane). Same answer on every lane and in every role of the CTA.
+__device__ __forceinline__ int bsrbsr_count(const GemmArgs& a, int j0, int j1, int jc) {
+  const int lane = threadIdx.x & 31;
+  int n = 0;
+  for (int jb = j0; jb < j1; jb += 32) {
+    int p0, p1;
+    const bool on = jb + lane < j1 && bsrbsr_pair(a, jb + lane, jc, p0, p1);
+    n += __popc(__ballot_sync(0xFFFFFFFFu, on));
+  }
+  return n;
 }
 
 __device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -116,11 +158,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   constexpr int BK = kGemmRowBytes / kElemBytes;  // elements of K per stage (64 fp16 / 128 e4m3)
   constexpr int MMA_K = 32 / kElemBytes;          // K per tcgen05.mma (16 fp16 / 32 e4m3)
   constexpr int K_STEPS = BK / MMA_K;             // 4
-  constexpr bool kMNB = (kML == Mainloop::Bsr);   // B operand MN-major (row-major [K,N] source)
+  constexpr bool kMNB = (kML != Mainloop::Dense);  // B operand MN-major (row-major [K,N] source or blocks)
   constexpr uint32_t IDESC = ptx::instr_desc(kGemmBM, kGemmBN, 0, 0, 0, kMNB ? 1 : 0);
   constexpr uint32_t STAGE_TX = kGemmAStage + kGemmBStage;
   constexpr int BSR_STEPS = 128 / BK;             // stages per 128-wide nonzero block
-  constexpr uint32_t KID = kML == Mainloop::Bsr ? kKidSpmmBsr : (kElemBytes == 1 ? kKidGemmE4m3 : kKidGemmF16);
+  constexpr uint32_t KID = kML == Mainloop::Bsr      ? kKidSpmmBsr
+                           : kML == Mainloop::BsrBsr ? kKidSpmmBsrBsr
+                                                     : (kElemBytes == 1 ? kKidGemmE4m3 : kKidGemmF16);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -190,6 +234,46 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           ++issued;
           if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
         }
+      } else if constexpr (kML == Mainloop::BsrBsr) {
+        const int r = a.row_begin + mt;
+        const int jc = n0 / 128;
+        int j0, j1;
+        if (!bsr_row_range(a, r, j0, j1) && lane == 0) atomicCAS(a.err, 0u, kErrBounds | (KID << 8) | (7u << 16));
+        for (int jb = j0; jb < j1 && ok; jb += 32) {
+          // each lane resolves the B pair of one of the next 32 A blocks; then the warp walks them in order
+          int p0 = -1, p1 = -1;
+          bool on = false;
+          if (jb + lane < j1) {
+            on = bsrbsr_pair(a, jb + lane, jc, p0, p1);
+            const int kb = __ldg(&a.col_idx[jb + lane]);
+            if (kb < 0 || kb >= a.kb_count) atomicCAS(a.err, 0u, kErrBounds | (KID << 8) | (8u << 16));
+          }
+          unsigned live = __ballot_sync(0xFFFFFFFFu, on);
+          while (live && ok) {
+            const int jj = __ffs(live) - 1;
+            live &= live - 1;
+            const int q0 = __shfl_sync(0xFFFFFFFFu, p0, jj);
+            const int q1 = __shfl_sync(0xFFFFFFFFu, p1, jj);
+            const int r0 = (q0 >= 0 ? q0 : a.b_nnzb) * 128, r1 = (q1 >= 0 ? q1 : a.b_nnzb) * 128;
+            for (int s = 0; s < BSR_STEPS; ++s) {
+              ok = warp_wait_bounded(ptx::smem_u32(&empty[stage]), phase ^ 1, ctl, 1);
+              if (!ok) break;
+              if (lane == 0) {
+                const uint32_t fb = ptx::smem_u32(&full[stage]);
+                ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
+                ptx::tma_load_2d(ptx::smem_u32(sA + stage * kGemmAStage), &tmA, fb, s * BK, (jb + jj) * 128);
+                // B: K rows [s*BK, +BK) of blocks (kb, jc) -> columns [0,128) and (kb, jc+1) -> [128,256) of the
+                // tile; a missing block is read at row b_nnzb*128 (past the end), i.e. as zeros
+                const uint32_t bdst = ptx::smem_u32(sB + stage * kGemmBStage);
+#pragma unroll
+                for (int q = 0; q < 4; ++q)
+                  ptx::tma_load_2d(bdst + q * (BK * 128), &tmB, fb, (q & 1) * 64, (q < 2 ? r0 : r1) + s * BK);
+              }
+              ++issued;
+              if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
+            }
+          }
+        }
       } else {
         const int r = a.row_begin + mt;
         int j0, j1;
@@ -234,6 +318,57 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         dctl.abort = &never;
         wait_bounded(ptx::smem_u32(&full[i % kGemmStages]), (i / kGemmStages) & 1, dctl, 2);
       }
+    }
+    __syncwarp();
+  } else if (warp == 1 && kML == Mainloop::BsrBsr) {
+    // ------------------------------------------------------------------ MMA issuer, BSR x BSR
+    // The warp counts each tile's contributing A blocks together (lookups of B); lane 0 issues the MMAs.
+    uint32_t stage = 0, phase = 0;
+    uint32_t acc = 0, acc_phase = 0;
+    bool ok = true;
+    const uint32_t full0 = ptx::smem_u32(full), empty0 = ptx::smem_u32(empty);
+    const uint32_t tfull0 = ptx::smem_u32(tfull), tempty0 = ptx::smem_u32(tempty);
+    const uint64_t adesc0 = ptx::smem_desc(ptx::smem_u32(sA), 16, 1024);
+    const uint64_t bdesc0 = ptx::smem_desc(ptx::smem_u32(sB), BK * 128, 1024);
+    constexpr uint32_t B_KSTEP = (MMA_K * 128) >> 4;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mt, nt;
+      gemm_tile_coords(tile, a, mt, nt);
+      int j0, j1;
+      bsr_row_range(a, a.row_begin + mt, j0, j1);
+      const int nk = bsrbsr_count(a, j0, j1, nt * kGemmBN / 128) * BSR_STEPS;
+      if (lane == 0) {
+        ok = wait_bounded(tempty0 + acc * 8, acc_phase ^ 1, ctl, 3);
+        if (ok) {
+          ptx::tc_fence_after();
+          const uint32_t d_tmem = tmem_base + acc * kGemmBN;
+          for (int kb = 0; kb < nk; ++kb) {
+            ok = wait_bounded(full0 + stage * 8, phase, ctl, 4);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            const uint64_t ad = adesc0 + ((stage * kGemmAStage) >> 4);
+            const uint64_t bd = bdesc0 + ((stage * kGemmBStage) >> 4);
+#pragma unroll
+            for (int k = 0; k < K_STEPS; ++k) ptx::mma_f16_ss(d_tmem, ad + k * 2, bd + k * B_KSTEP, IDESC, (kb | k) != 0);
+            ptx::mma_commit(empty0 + stage * 8);
+            if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
+          }
+          if (ok) {
+            ptx::mma_commit(tfull0 + acc * 8);
+            acc ^= 1;
+            if (acc == 0) acc_phase ^= 1;
+          }
+        }
+      }
+      ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      if (!ok) break;
+    }
+    if (lane == 0) {  // all MMAs this thread issued complete before TMEM is released
+      ptx::mma_commit(ptx::smem_u32(drain));
+      WaitCtl dctl = ctl;
+      volatile int never = 0;
+      dctl.abort = &never;
+      wait_bounded(ptx::smem_u32(drain), 0, dctl, 5);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -310,7 +445,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         m0 = r * kGemmBM;
         int j0, j1;
         bsr_row_range(a, r, j0, j1);
-        nk = j1 - j0;
+        if constexpr (kML == Mainloop::BsrBsr)
+          nk = bsrbsr_count(a, j0, j1, nt * kGemmBN / 128);
+        else
+          nk = j1 - j0;
       }
       const int n0 = nt * kGemmBN;
       if (!warp_wait_bounded(ptx::smem_u32(&tfull[acc]), acc_phase, ctl, 6)) break;

@@ -46,12 +46,14 @@ KERNEL_BLOCK = 128  # block edge of the sm_100 BSR kernel (tcgen05 M = 128)
 
 # ----------------------------------------------------------------------------------------- BSR SpMM
 def sparse_mm(A: torch.Tensor, B: torch.Tensor, block_size: int = 16, autotune: bool = False) -> torch.Tensor:
-    """C = A @ B for sparse A (BSR or CSR, fp16, CUDA) and dense B (fp16, CUDA); returns fp32 [M, N].
+    """C = A @ B for sparse A (BSR or CSR, fp16, CUDA) and B dense or BSR / CSR (fp16, CUDA); returns fp32 [M, N].
 
     Same signature and argument checks as the reference (BlackwellSparseK/python/ops.py:25-69).
     ``block_size`` and ``autotune`` keep their meaning for the tile-config dicts
     (``_default_config`` / ``_autotune_config``) but the sm_100 kernel always computes on 128x128 blocks:
     inputs in another layout (CSR, or BSR with another block size) are re-blocked on the device first.
+    A B in BSR or CSR layout takes the BSR x BSR kernel (B's blocks looked up per A block, as the reference's
+    sparse-B kernel path does, src/sparse_h100_async.cu:105-119); a COO B is rejected as in the reference.
     """
     if not A.is_sparse and A.layout not in (torch.sparse_csr, torch.sparse_bsr):
         raise ValueError("A must be a sparse tensor")
@@ -69,7 +71,18 @@ def sparse_mm(A: torch.Tensor, B: torch.Tensor, block_size: int = 16, autotune: 
     A_bsr = _to_kernel_bsr(A)
     if B.dtype != torch.float16:
         raise ValueError("B must be float16")
-    Bc = B.contiguous()
+    if B.layout in (torch.sparse_bsr, torch.sparse_csr):
+        if N % KERNEL_BLOCK:
+            raise ValueError(f"a sparse B needs N divisible by {KERNEL_BLOCK}, got {N}")
+        B_bsr = _to_kernel_bsr(B)
+        crow, col = B_bsr.crow_indices(), B_bsr.col_indices()
+        if col.numel() == (K2 // KERNEL_BLOCK) * (N // KERNEL_BLOCK):  # every block stored: plain dense product
+            Bc = B_bsr.to_dense()
+        else:
+            return _C().sparse_mm_bsr(A_bsr.crow_indices(), A_bsr.col_indices(), A_bsr.values(), crow, col,
+                                      B_bsr.values(), M, N, K1, config["BM"], config["BN"], config["BK"])
+    else:
+        Bc = B.contiguous()
     dummy = torch.zeros(1, dtype=torch.int32, device=A.device)
     return _C().sparse_mm_bsr(A_bsr.crow_indices(), A_bsr.col_indices(), A_bsr.values(), dummy, dummy, Bc, M, N, K1,
                               config["BM"], config["BN"], config["BK"])
