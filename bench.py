@@ -56,6 +56,7 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=3)
+    p.add_argument("--tune-cache-out", action="store_true", help="write the autotune op's results as a cache file")
     p.add_argument("--e2e-k-chunk", type=int, default=0, help="K per streamed chunk of the e2e GEMM (0 = auto)")
     p.add_argument("--op-steps", type=int, default=20, help="timed steps of the fp8 / bsr / attn measurements")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
@@ -353,6 +354,33 @@ def bench_bsr(ctx: Ctx, args, res: dict):
     torch.cuda.empty_cache()
 
 
+# ----------------------------------------------------------------------------------------- autotune
+TUNE_SHAPES = [(8192, 1024, 237568), (8192, 2048, 237568), (8192, 4096, 237568), (8192, 8192, 8192),
+               (4096, 4096, 4096), (2048, 8192, 16384)]
+
+
+def bench_autotune(ctx: Ctx, args, res: dict):
+    """Dense GEMM launch-configuration tuning: per shape, after ~100 ms of settling, every (tile, group) variant
+    timed round-robin twice (3 warm-ups, 10 runs, CUDA events, best of the two), default policy vs the fastest. The first three shapes are the per-rank shards of the headline
+    GEMM at N = 8, 4, 2. Rank 0 only (the others idle); no data-path collective."""
+    from periodicdent42_b200 import autotune as at
+
+    out = []
+    if ctx.rank == 0:
+        cache = at.AutotuneCache(os.path.join(os.path.dirname(os.path.abspath(__file__)), "gpurun_out",
+                                              "autotune_bench.json")) if args.tune_cache_out else None
+        for (M, N, K) in TUNE_SHAPES:
+            e = at.tune_gemm(M, N, K, warmup=3, runs=10, rounds=2, cache=cache, save=cache is not None)
+            fl = 2.0 * M * N * K
+            out.append({"shape": [M, N, K], "default_tflops": fl / (e["default_ms"] * 1e-3) / 1e12,
+                        "tuned_tflops": fl / (e["ms"] * 1e-3) / 1e12, "speedup": e["default_ms"] / e["ms"],
+                        "tile": e["tile_name"], "group_m": e["group_m"], "variants": e["variants"]})
+            torch.cuda.empty_cache()
+        at.clear()
+    ctx.barrier()
+    res["autotune"] = out
+
+
 # ----------------------------------------------------------------------------------------- BSR x BSR
 def bench_bsr_bsr(ctx: Ctx, args, res: dict):
     """A = the BSR workload's matrix (8192 x 8192, 16 of 64 128x128 blocks per block-row); B = a second 8192 x 8192
@@ -549,7 +577,7 @@ def main():
     try:
         for op in ops:
             {"dense": bench_dense, "fp8": bench_fp8, "bsr": bench_bsr, "attn": bench_attn,
-             "convert": bench_convert, "bsr_bsr": bench_bsr_bsr}[op](ctx, args, res)
+             "convert": bench_convert, "bsr_bsr": bench_bsr_bsr, "autotune": bench_autotune}[op](ctx, args, res)
     finally:
         clk = clocks.stop() if clocks else None
     err_word = _capi.device_error()
@@ -608,6 +636,8 @@ def main():
                                     "csr_frac_of_peak": r["gbs_csr"] / peaks["hbm_gbs"],
                                     "peak_basis": f"{peak_src} HBM copy", "nnzb": r["nnzb"],
                                     "scaling": r["scaling"]}
+        if res.get("autotune"):
+            opsum["autotune_dense"] = res["autotune"]
         line["ops"] = opsum
         line["device_error_word"] = err_word
         print(json.dumps(line), flush=True)

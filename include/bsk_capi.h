@@ -42,6 +42,24 @@ const char* bsk_last_error(void);
 int bsk_device_sm_count(void);
 
 /*
+ * Per-shape launch configurations (what an autotuner found best, e.g. restored from its JSON cache). For an
+ * operator and an exact (M, N, K) -- K being the K extent of the launch -- the later launches use:
+ *   tile    : -1 the built-in policy, 0 single-CTA 128x256, 1 CTA pair 256x256, 2 CTA pair 256x512
+ *             (dense GEMMs only; ignored by the SpMMs)
+ *   group_m : tile-rasterisation group (M tiles walked together), 0 = the built-in choice
+ * Process-wide; bsk_config_get returns 1 and the entry when one is registered, 0 (tile -1, group 0) otherwise.
+ * Replaces the reference's size-bucketed _autotune_config (BlackwellSparseK/python/ops.py:209-217) and its
+ * variant cache (optim_local/src/sparse/autotune_sparse.h).
+ */
+#define BSK_OP_GEMM_F16F32 1
+#define BSK_OP_GEMM_E4M3_BF16 2
+#define BSK_OP_SPMM_BSR 3
+#define BSK_OP_SPMM_BSR_BSR 4
+int bsk_config_set(int op, int M, int N, int K, int tile, int group_m);
+int bsk_config_get(int op, int M, int N, int K, int* tile, int* group_m);
+int bsk_config_clear(void);
+
+/*
  * Dense GEMM, fp16 x fp16 -> fp32:  C[M,N] = A[M, k_begin:k_end] * B[k_begin:k_end, N].
  *   A   : fp16, row-major [M, K], row stride lda (elements, multiple of 8, 16-B aligned base)
  *   B   : fp16, column-major [K, N] (equivalently B^T row-major [N, K]), column stride ldb

@@ -31,6 +31,9 @@ SIGNATURES = {
     "bsk_version": (_i32, []),
     "bsk_last_error": (ctypes.c_char_p, []),
     "bsk_device_sm_count": (_i32, []),
+    "bsk_config_set": (_i32, [_i32, _i32, _i32, _i32, _i32, _i32]),
+    "bsk_config_get": (_i32, [_i32, _i32, _i32, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
+    "bsk_config_clear": (_i32, []),
     "bsk_gemm_f16f32": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp]),
     "bsk_gemm_f16f32_acc": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _i32, _vp]),
     "bsk_gemm_f16f32_host": (_i32, [_vp, _i64, _vp, _i64, _vp, _i64, _i32, _i32, _i32, _i32, _vp, _i64, _vp]),

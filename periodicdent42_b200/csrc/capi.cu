@@ -11,6 +11,7 @@
 #include <cstring>
 #include <mutex>
 #include <string>
+#include <vector>
 
 #include "bsk_capi.h"
 #include "gemm_sm100.cuh"
@@ -77,6 +78,26 @@ int max_clusters(K kernel, int threads, int smem) {
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(kernel), &cfg) != cudaSuccess) return -1;
   return n;
+}
+
+// Per-shape launch configurations registered by the caller (an autotuner and its persisted cache): for an
+// operator and an exact (M, N, K), the tile kind (-1 = the built-in policy) and the rasterisation group (<= 0 =
+// the built-in choice). Process-wide, guarded by a mutex; looked up once per launch.
+struct ShapeConfig {
+  int op, M, N, K, tile, group;
+};
+std::mutex g_cfg_mu;
+std::vector<ShapeConfig> g_cfg;
+
+bool find_config(int op, int M, int N, int K, int* tile, int* group) {
+  std::lock_guard<std::mutex> lk(g_cfg_mu);
+  for (const ShapeConfig& c : g_cfg)
+    if (c.op == op && c.M == M && c.N == N && c.K == K) {
+      *tile = c.tile;
+      *group = c.group;
+      return true;
+    }
+  return false;
 }
 
 // Tile policy of the dense GEMMs (0 = single-CTA 128x256, 1 = CTA pair 256x256, 2 = CTA pair 256x512):
@@ -243,6 +264,20 @@ int pick_group_m(int num_m_tiles, int kind = 0, int k_extent = 0) {
   return num_m_tiles < g ? num_m_tiles : g;
 }
 
+// Tile kind and rasterisation group for one launch: the registered configuration of (op, M, N, K) where one
+// exists (tile kinds the operator lacks fall back to the policy), else the built-in policy.
+void launch_config(int op, int M, int N, int K, bool has_tiles, int* kind, int* group_for_tiles) {
+  int tile = -1, group = 0;
+  find_config(op, M, N, K, &tile, &group);
+  *kind = has_tiles ? ((tile >= 0 && tile <= 2) ? tile : gemm_tile_kind(M, N, K)) : 0;
+  *group_for_tiles = group;
+}
+
+int resolve_group(int group, int num_m_tiles, int kind, int k_extent) {
+  if (group > 0) return group < num_m_tiles ? group : num_m_tiles;
+  return pick_group_m(num_m_tiles, kind, k_extent);
+}
+
 }  // namespace
 
 extern "C" {
@@ -255,6 +290,36 @@ int bsk_device_sm_count(void) {
   DeviceState* st;
   if (int rc = device_state(&st)) return rc;
   return st->sm_count;
+}
+
+int bsk_config_set(int op, int M, int N, int K, int tile, int group_m) {
+  if (op < BSK_OP_GEMM_F16F32 || op > BSK_OP_SPMM_BSR_BSR)
+    return set_error(BSK_ERR_INVALID_ARG, "config_set: unknown operator %d", op);
+  if (M < 0 || N < 0 || K < 0) return set_error(BSK_ERR_INVALID_ARG, "config_set: negative extent");
+  if (tile < -1 || tile > 2) return set_error(BSK_ERR_INVALID_ARG, "config_set: tile %d not in {-1, 0, 1, 2}", tile);
+  if (group_m < 0 || group_m > 4096) return set_error(BSK_ERR_INVALID_ARG, "config_set: group_m %d outside [0, 4096]", group_m);
+  std::lock_guard<std::mutex> lk(g_cfg_mu);
+  for (ShapeConfig& c : g_cfg)
+    if (c.op == op && c.M == M && c.N == N && c.K == K) {
+      c.tile = tile;
+      c.group = group_m;
+      return BSK_OK;
+    }
+  g_cfg.push_back({op, M, N, K, tile, group_m});
+  return BSK_OK;
+}
+
+int bsk_config_get(int op, int M, int N, int K, int* tile, int* group_m) {
+  if (!tile || !group_m) return set_error(BSK_ERR_INVALID_ARG, "config_get: null output");
+  *tile = -1;
+  *group_m = 0;
+  return find_config(op, M, N, K, tile, group_m) ? 1 : 0;
+}
+
+int bsk_config_clear(void) {
+  std::lock_guard<std::mutex> lk(g_cfg_mu);
+  g_cfg.clear();
+  return BSK_OK;
 }
 
 int bsk_set_wait_timeout_ns(uint64_t ns) {
@@ -290,7 +355,8 @@ int gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, floa
   }
   const __half* Ah = static_cast<const __half*>(A) + k_begin;
   const __half* Bh = static_cast<const __half*>(B) + k_begin;
-  const int kind = gemm_tile_kind(M, N, kr);
+  int kind, group;
+  launch_config(BSK_OP_GEMM_F16F32, M, N, kr, true, &kind, &group);
   const uint32_t a_rows = kind ? 128 : kGemmBM;  // rows per CTA of the A tile
   const uint32_t b_rows = kind ? 128 : kGemmBN;  // rows of B^T per TMA box
   CUtensorMap ta, tb;
@@ -303,7 +369,7 @@ int gemm_f16_launch(const void* A, int64_t lda, const void* B, int64_t ldb, floa
   a.num_m_tiles = (M + tm - 1) / tm;
   a.num_n_tiles = (N + tn - 1) / tn;
   a.num_k_blocks = (kr + 63) / 64;
-  a.group_m = pick_group_m(a.num_m_tiles, kind, kr);
+  a.group_m = resolve_group(group, a.num_m_tiles, kind, kr);
   a.k_splits = 1;
   a.kb_per_split = a.num_k_blocks;
   a.out = C;
@@ -492,7 +558,8 @@ int bsk_gemm_e4m3_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, c
     cudaError_t e = cudaMemset2DAsync(D, ldd * 2, 0, (size_t)N * 2, M, s);
     return e == cudaSuccess ? BSK_OK : cuda_fail(e, "gemm_e4m3: zero fill");
   }
-  const int kind = gemm_tile_kind(M, N, K);
+  int kind, group;
+  launch_config(BSK_OP_GEMM_E4M3_BF16, M, N, K, true, &kind, &group);
   CUtensorMap ta, tb;
   if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, A, K, M, lda, 128, kind ? 128 : kGemmBM, "A")) return rc;
   if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, B, K, N, ldb, 128, kind ? 128 : kGemmBN, "B")) return rc;
@@ -503,7 +570,7 @@ int bsk_gemm_e4m3_bf16(const void* A, int64_t lda, const void* B, int64_t ldb, c
   a.num_m_tiles = (M + tm - 1) / tm;
   a.num_n_tiles = (N + tn - 1) / tn;
   a.num_k_blocks = (K + 127) / 128;
-  a.group_m = pick_group_m(a.num_m_tiles, kind);
+  a.group_m = resolve_group(group, a.num_m_tiles, kind, 0);
   a.k_splits = 1;
   a.kb_per_split = a.num_k_blocks;
   a.out = D;
@@ -871,7 +938,11 @@ int bsk_spmm_bsr_f16f32(const int32_t* row_ptr, const int32_t* col_idx, const vo
   a.num_m_tiles = row_end - row_begin;
   a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
   a.num_k_blocks = 0;
-  a.group_m = pick_group_m(a.num_m_tiles);
+  {
+    int kind_unused, group;
+    launch_config(BSK_OP_SPMM_BSR, M, N, K, false, &kind_unused, &group);
+    a.group_m = resolve_group(group, a.num_m_tiles, 0, 0);
+  }
   a.k_splits = 1;
   a.kb_per_split = a.num_k_blocks;
   a.out = C;
@@ -932,7 +1003,11 @@ int bsk_spmm_bsr_bsr_f16f32(const int32_t* a_row_ptr, const int32_t* a_col_idx, 
   a.N = N;
   a.num_m_tiles = row_end - row_begin;
   a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
-  a.group_m = pick_group_m(a.num_m_tiles);
+  {
+    int kind_unused, group;
+    launch_config(BSK_OP_SPMM_BSR_BSR, M, N, K, false, &kind_unused, &group);
+    a.group_m = resolve_group(group, a.num_m_tiles, 0, 0);
+  }
   a.k_splits = 1;
   a.out = C;
   a.ldo = ldc;

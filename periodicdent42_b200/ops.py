@@ -71,6 +71,8 @@ def sparse_mm(A: torch.Tensor, B: torch.Tensor, block_size: int = 16, autotune: 
     A_bsr = _to_kernel_bsr(A)
     if B.dtype != torch.float16:
         raise ValueError("B must be float16")
+    if autotune and B.layout == torch.strided:
+        _ensure_tuned("spmm_bsr", M, N, K1, lambda: _tune_spmm(A_bsr, B.contiguous(), M))
     if B.layout in (torch.sparse_bsr, torch.sparse_csr):
         if N % KERNEL_BLOCK:
             raise ValueError(f"a sparse B needs N divisible by {KERNEL_BLOCK}, got {N}")
@@ -86,6 +88,29 @@ def sparse_mm(A: torch.Tensor, B: torch.Tensor, block_size: int = 16, autotune: 
     dummy = torch.zeros(1, dtype=torch.int32, device=A.device)
     return _C().sparse_mm_bsr(A_bsr.crow_indices(), A_bsr.col_indices(), A_bsr.values(), dummy, dummy, Bc, M, N, K1,
                               config["BM"], config["BN"], config["BK"])
+
+
+def _ensure_tuned(op: str, M: int, N: int, K: int, tune_fn) -> None:
+    """Registers the cached launch configuration of (op, M, N, K) for this device, tuning (and caching) it on
+    first use -- the reference's ``autotune=True`` switch, backed by measurements instead of size buckets."""
+    from . import autotune as at
+
+    if at.registered(op, M, N, K) is not None:
+        return
+    cache = at.AutotuneCache()
+    e = cache.get(at.device_key(), at.shape_key(op, M, N, K))
+    if e is not None:
+        at.register(op, M, N, K, int(e["tile"]), int(e["group_m"]))
+    else:
+        tune_fn()
+
+
+def _tune_spmm(A_bsr: torch.Tensor, B: torch.Tensor, M: int) -> None:
+    from . import autotune as at
+
+    rp = A_bsr.crow_indices().to(torch.int32)
+    ci = A_bsr.col_indices().to(torch.int32)
+    at.tune_spmm_bsr(rp, ci, A_bsr.values().contiguous(), B, M)
 
 
 def _to_kernel_bsr(A: torch.Tensor) -> torch.Tensor:
@@ -170,12 +195,13 @@ def sparse_mm_benchmark(A: torch.Tensor, B: torch.Tensor,
 
 # ----------------------------------------------------------------------------------------- dense GEMM
 def gemm(A: torch.Tensor, B: torch.Tensor, out_dtype: torch.dtype = torch.float32, k_range=None,
-         split_k: Optional[int] = None) -> torch.Tensor:
+         split_k: Optional[int] = None, autotune: bool = False) -> torch.Tensor:
     """C = A @ B, fp16 inputs, fp32 output. A [M, K] row-major; B [K, N], column-major preferred
     (``B = Bt.t()`` with Bt contiguous costs nothing; a row-major B is transposed once). ``k_range``
     = (k_begin, k_end) restricts the contraction (split-K shards across ranks). ``split_k``: None = one pass;
     0 = split K across CTA pairs automatically when the output has too few tiles to fill the GPU; n > 0 =
-    n splits (partials in a torch-allocated workspace, summed deterministically)."""
+    n splits (partials in a torch-allocated workspace, summed deterministically). ``autotune``: use the tuned
+    tile / rasterisation for this shape (measured and cached on first use, see ``autotune``)."""
     _check_cuda_f16(A, B)
     if out_dtype != torch.float32:
         raise ValueError("gemm computes fp16 x fp16 -> fp32; out_dtype must be torch.float32")
@@ -189,6 +215,12 @@ def gemm(A: torch.Tensor, B: torch.Tensor, out_dtype: torch.dtype = torch.float3
             raise ValueError("gemm: k_range and split_k are exclusive")
         return _C().gemm_f16f32_splitk(A, Bt, int(split_k))
     kb, ke = (0, -1) if k_range is None else k_range
+    if autotune:
+        from . import autotune as at
+
+        M, K = A.shape
+        kr = (K if ke < 0 else ke) - kb
+        _ensure_tuned("gemm_f16f32", M, Bt.shape[0], kr, lambda: at.tune_gemm(M, Bt.shape[0], kr))
     return _C().gemm_f16f32(A, Bt, kb, ke)
 
 
