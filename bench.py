@@ -48,7 +48,8 @@ def parse_args():
     p.add_argument("--steps", type=int, default=30)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--ops", default="dense,fp8,bsr,attn,convert,bsr_bsr", help="comma list; dense is the headline")
+    p.add_argument("--ops", default="dense,fp8,bsr,attn,attn_bwd,convert,bsr_bsr",
+                   help="comma list; dense is the headline")
     p.add_argument("--dense-mode", choices=["nshard", "splitk", "splitk_nccl"], default="nshard",
                    help="nshard: N-sharded, no communication; splitk: K split across ranks, reduce-scatter fused "
                         "into the GEMM (peer-memory epilogue); splitk_nccl: K split + NCCL reduce_scatter")
@@ -354,6 +355,49 @@ def bench_bsr(ctx: Ctx, args, res: dict):
     torch.cuda.empty_cache()
 
 
+# ----------------------------------------------------------------------------------------- attention backward
+def bench_attn_bwd(ctx: Ctx, args, res: dict):
+    """Backward of the attention workload (the forward's shapes and mask): delta + dK/dV pass + dQ pass, through
+    the C ABI, LSE and column lists prepared outside the timed region. Useful FLOPs: the standard count of 5
+    block GEMMs per nonzero block (2.5 x the forward's 2); the two-pass deterministic scheme executes 7."""
+    cfg = wl.ATTN
+    q, k, v = wl.attn_inputs(cfg, ctx.dev)
+    rp, ci = wl.attn_mask_bsr(cfg)
+    pairs, nqb = cfg.B * cfg.H, cfg.S // 128
+    b0, b1 = sharding.attn_pairs(rp, nqb, pairs, ctx.world, ctx.rank)
+    rp32, ci32 = rp.to(torch.int32).to(ctx.dev), ci.to(torch.int32).to(ctx.dev)
+    scale = 1.0 / math.sqrt(cfg.D)
+    O = torch.empty_like(q)
+    lse = torch.empty(pairs * cfg.S, dtype=torch.float32, device=ctx.dev)
+    _capi.bsattn_fwd_ex(q, k, v, O, lse, rp32, ci32, scale, True, stream=ctx.stream)
+    col_ptr, row_idx = _capi.bsattn_mask_transpose(rp32, ci32, pairs, nqb, stream=ctx.stream)
+    g = torch.Generator(device=ctx.dev).manual_seed(7)
+    dO = torch.randn(q.shape, generator=g, device=ctx.dev).to(q.dtype)
+    dQ, dK, dV = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    delta = torch.empty(pairs * cfg.S, dtype=torch.float32, device=ctx.dev)
+    # the (b,h) pairs of this rank: views starting at pair b0 (row lists rebased to that pair)
+    sl = slice(b0, b1)
+    Bv = lambda t: t.view(pairs, cfg.S, cfg.D)[sl].view(1, b1 - b0, cfg.S, cfg.D)  # noqa: E731
+    base = int(rp[b0 * nqb])
+    rp_r = (rp[b0 * nqb:b1 * nqb + 1] - base).to(torch.int32).to(ctx.dev)
+    ci_r = ci[base:int(rp[b1 * nqb])].to(torch.int32).to(ctx.dev)
+    cp_r = (col_ptr[b0 * nqb:b1 * nqb + 1] - base).contiguous()
+    ri_r = row_idx[base:int(rp[b1 * nqb])].contiguous()
+    lse_r = lse.view(pairs, cfg.S)[sl].reshape(-1)
+    dl_r = delta.view(pairs, cfg.S)[sl].reshape(-1)
+
+    def step():
+        _capi.bsattn_bwd(Bv(dO), Bv(q), Bv(k), Bv(v), Bv(O), lse_r, Bv(dQ), Bv(dK), Bv(dV), rp_r, ci_r, cp_r, ri_r,
+                         scale, True, delta=dl_r, stream=ctx.stream)
+    ms = time_region(ctx, step, args.op_steps, args.warmup, "attn_bwd")
+    nnz = int(rp[-1])
+    flops = 2.5 * 4 * 128 ** 2 * cfg.D * nnz
+    res["attn_bwd"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "flops": flops, "launches_per_step": 3,
+                       "nnz_blocks": nnz, "executed_gemm_ratio": 7 / 5}
+    del q, k, v, O, dO, dQ, dK, dV
+    torch.cuda.empty_cache()
+
+
 # ----------------------------------------------------------------------------------------- autotune
 TUNE_SHAPES = [(8192, 1024, 237568), (8192, 2048, 237568), (8192, 4096, 237568), (8192, 8192, 8192),
                (4096, 4096, 4096), (2048, 8192, 16384)]
@@ -577,7 +621,8 @@ def main():
     try:
         for op in ops:
             {"dense": bench_dense, "fp8": bench_fp8, "bsr": bench_bsr, "attn": bench_attn,
-             "convert": bench_convert, "bsr_bsr": bench_bsr_bsr, "autotune": bench_autotune}[op](ctx, args, res)
+             "convert": bench_convert, "bsr_bsr": bench_bsr_bsr, "autotune": bench_autotune,
+             "attn_bwd": bench_attn_bwd}[op](ctx, args, res)
     finally:
         clk = clocks.stop() if clocks else None
     err_word = _capi.device_error()
@@ -616,7 +661,7 @@ def main():
         line["cpu_baseline"] = cpu
         line["clocks"] = clk
         opsum = {}
-        for name in ("fp8", "bsr", "attn", "bsr_bsr"):
+        for name in ("fp8", "bsr", "attn", "attn_bwd", "bsr_bsr"):
             if name in res:
                 r = res[name]
                 pk = peak_t * (2 if name == "fp8" else 1)

@@ -294,6 +294,41 @@ int bsk_csr_to_bsr_bounded(const void* crow, const void* col, int index_bytes_in
                            void* values, int64_t max_nnzb, void* workspace, int64_t workspace_bytes, void* stream);
 
 /*
+ * Block-sparse attention forward with the row log-sum-exp: as bsk_bsattn_fwd_bf16 / _f16 (dtype 0 = bf16,
+ * 1 = fp16), and when lse is not NULL, lse[b*H*S + h*S + s] = natural-log log-sum-exp of query row s's scaled
+ * scores over its unmasked keys (-inf for a row with no key blocks) -- what the backward needs.
+ */
+int bsk_bsattn_fwd_ex(int dtype, const void* Q, const void* K, const void* V, void* O, float* lse,
+                      const int32_t* row_ptr, const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale,
+                      int causal_diag, int bh_begin, int bh_end, void* stream);
+
+/*
+ * Column lists of a block mask: for pair p (of `pairs`) and key block-column j, the query blocks whose row lists
+ * contain j, ascending: row_idx[col_ptr[p*nqb + j] .. col_ptr[p*nqb + j + 1]). col_ptr [pairs*nqb + 1] uses the
+ * numbering of row_ptr (pair p's entries start at row_ptr[p*nqb] in both); row_idx has row_ptr[pairs*nqb]
+ * entries. workspace: pairs*nqb*4 + 16 bytes of device scratch.
+ */
+int bsk_bsattn_mask_transpose(const int32_t* row_ptr, const int32_t* col_idx, int pairs, int nqb, int32_t* col_ptr,
+                              int32_t* row_idx, void* workspace, int64_t workspace_bytes, void* stream);
+
+/*
+ * Block-sparse attention backward (dtype 0 = bf16, 1 = fp16; D = 64 or 128; blk = 128):
+ *   dV = P^T dO,  dK = scale * dS^T Q,  dQ = scale * dS K,  dS = P * (dO V^T - rowsum(dO * O)),
+ *   P = exp(scale * Q K^T - lse) on the mask (the forward's; causal_diag as there).
+ * dO, Q, K, V, O, dQ, dK, dV: [B, H, S, D] contiguous; lse [B*H*S] from bsk_bsattn_fwd_ex; row_ptr/col_idx the
+ * forward's mask and col_ptr/row_idx its column lists (bsk_bsattn_mask_transpose); delta: device scratch of
+ * B*H*S floats. Deterministic: each output row is produced by one CTA in a fixed order (two passes recompute
+ * the scores: one per key block for dK/dV, one per query block for dQ). Rows of dK/dV whose key block no query
+ * block attends, and rows of dQ with no key blocks, are zero.
+ * The reference declares launch_attention_backward
+ * (.archive/src_experiments/blackwell_sparsek/kernels/attention_fmha.cu:436-453) but leaves it unimplemented.
+ */
+int bsk_bsattn_bwd(int dtype, const void* dO, const void* Q, const void* K, const void* V, const void* O,
+                   const float* lse, void* dQ, void* dK, void* dV, const int32_t* row_ptr, const int32_t* col_idx,
+                   const int32_t* col_ptr, const int32_t* row_idx, int B, int H, int S, int D, int blk, float scale,
+                   int causal_diag, float* delta, void* stream);
+
+/*
  * Drop-in for the reference's launcher signature (BlackwellSparseK/src/kernel_launch.cu:33-61).
  * A is BSR with blocks of (M/A_M_blocks) x (K/A_K_blocks). A B with every block present is read as the dense
  * row-major [K, N] matrix the reference Python layer passes (BlackwellSparseK/python/ops.py:104-107); a B with

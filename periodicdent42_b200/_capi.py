@@ -73,6 +73,11 @@ SIGNATURES = {
                                    _i32, _vp]),
     "bsk_bsattn_fwd_f16": (_i32, [_vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _i32, _i32,
                                   _i32, _vp]),
+    "bsk_bsattn_fwd_ex": (_i32, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _i32, _f32, _i32,
+                                 _i32, _i32, _vp]),
+    "bsk_bsattn_mask_transpose": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp, _i64, _vp]),
+    "bsk_bsattn_bwd": (_i32, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
+                              _i32, _i32, _f32, _i32, _vp, _vp]),
     "launch_bsr_spmm_async": (None, [_vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _i32,
                                      _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
     "bsk_device_error": (_i32, [ctypes.POINTER(ctypes.c_uint32)]),
@@ -353,6 +358,53 @@ def csr_to_bsr_bounded(crow, col, vals, shape, bs: int, row_ptr, col_idx, values
                                        vals.element_size(), vals.numel(), M, K, bs, _ptr(row_ptr), _ptr(col_idx),
                                        _index_bytes(col_idx.dtype), _ptr(values), cap, _ptr(workspace),
                                        workspace.numel(), _stream(stream)), "bsk_csr_to_bsr_bounded")
+
+
+def _attn_dtype(t) -> int:
+    import torch
+
+    if t.dtype == torch.bfloat16:
+        return 0
+    if t.dtype == torch.float16:
+        return 1
+    raise ValueError("attention tensors must be bfloat16 or float16")
+
+
+def bsattn_fwd_ex(Q, K, V, O, lse, row_ptr, col_idx, scale: float, causal_diag: bool = True, bh_begin: int = 0,
+                  bh_end: int | None = None, blk: int = 128, stream=None) -> None:
+    """Forward (bf16 or fp16 by Q's dtype) that also writes the natural-log LSE per query row (lse may be None)."""
+    B, H, S, D = Q.shape
+    bh_end = B * H if bh_end is None else bh_end
+    check(lib().bsk_bsattn_fwd_ex(_attn_dtype(Q), _ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(lse), _ptr(row_ptr),
+                                  _ptr(col_idx), B, H, S, D, blk, float(scale), int(bool(causal_diag)), bh_begin,
+                                  bh_end, _stream(stream)), "bsk_bsattn_fwd_ex")
+
+
+def bsattn_mask_transpose(row_ptr, col_idx, pairs: int, nqb: int, stream=None):
+    """(col_ptr, row_idx) int32 column lists of the block mask, on row_ptr's device."""
+    import torch
+
+    dev = row_ptr.device
+    col_ptr = torch.empty(pairs * nqb + 1, dtype=torch.int32, device=dev)
+    row_idx = torch.empty(max(col_idx.numel(), 1), dtype=torch.int32, device=dev)
+    ws = torch.empty(pairs * nqb * 4 + 16, dtype=torch.uint8, device=dev)
+    check(lib().bsk_bsattn_mask_transpose(_ptr(row_ptr), _ptr(col_idx), pairs, nqb, _ptr(col_ptr), _ptr(row_idx),
+                                          _ptr(ws), ws.numel(), _stream(stream)), "bsk_bsattn_mask_transpose")
+    return col_ptr, row_idx
+
+
+def bsattn_bwd(dO, Q, K, V, O, lse, dQ, dK, dV, row_ptr, col_idx, col_ptr, row_idx, scale: float,
+               causal_diag: bool = True, delta=None, blk: int = 128, stream=None) -> None:
+    """Backward of the block-sparse attention into dQ, dK, dV (same shape and dtype as Q)."""
+    import torch
+
+    B, H, S, D = Q.shape
+    if delta is None:
+        delta = torch.empty(B * H * S, dtype=torch.float32, device=Q.device)
+    check(lib().bsk_bsattn_bwd(_attn_dtype(Q), _ptr(dO), _ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(lse), _ptr(dQ),
+                               _ptr(dK), _ptr(dV), _ptr(row_ptr), _ptr(col_idx), _ptr(col_ptr), _ptr(row_idx), B, H, S,
+                               D, blk, float(scale), int(bool(causal_diag)), _ptr(delta), _stream(stream)),
+          "bsk_bsattn_bwd")
 
 
 def device_error() -> int:

@@ -1,0 +1,697 @@
+// Block-sparse attention backward for sm_100a (tcgen05 + TMA), deterministic (no atomics).
+//
+// Given Q, K, V, O, dO [B*H*S, D] (fp16 or bf16), the forward's natural-log LSE per query row, and the block mask
+// (row lists: query block -> key blocks; column lists: key block -> query blocks), computes
+//   Delta_i = sum_d dO[i,d] O[i,d]                                      (bsattn_bwd_delta_kernel)
+//   P = exp(scale * Q K^T - LSE), dP = dO V^T, dS = P * (dP - Delta)    (recomputed per block pair)
+//   dV = P^T dO, dK = scale * dS^T Q                                    (bsattn_bwd_dkdv_kernel, per key block)
+//   dQ = scale * dS K                                                   (bsattn_bwd_dq_kernel, per query block)
+// The causal diagonal block masks key position > query position, as the forward does. The dK/dV and dQ passes
+// each recompute the scores they need, so every output element is written by one CTA in a fixed order.
+//
+// The reference has no backward kernel (its launch_attention_backward in
+// .archive/src_experiments/blackwell_sparsek/kernels/attention_fmha.cu:436-453 is a stub and its autograd
+// function falls back to torch, kernels/sparsek.py:100-142).
+//
+// CTA layout (both passes, 384 threads): warp 0 producer (one thread, TMA), warp 1 MMA issuer (one thread),
+// warps 2-3 idle, warps 4-11 two warpgroups of elementwise work; warpgroup x takes columns [64x, 64x + 64) of
+// the 128 x 128 score tiles (each warp its 32-lane quarter of TMEM), and half of D for the output.
+#pragma once
+
+#include "bsattn_sm100.cuh"
+
+namespace bsk {
+
+constexpr uint32_t kKidBsAttnBwd = 7;
+
+struct AttnBwdArgs {
+  const void* dO;        // [B*H*S, D]
+  const void* O;         // [B*H*S, D]   (delta pass)
+  const float* lse;      // [B*H*S] natural log
+  float* delta;          // [B*H*S] written by the delta pass, read by the others
+  void* dQ;              // [B*H*S, D]
+  void* dK;
+  void* dV;
+  const int* row_ptr;    // [BH*nqb + 1] -> col_idx (key blocks of each query block-row)
+  const int* col_idx;
+  const int* col_ptr;    // [BH*nqb + 1] -> row_idx (query blocks of each key block-column), ascending
+  const int* row_idx;
+  int S, nqb, bh_begin, num_items;
+  float scale;           // softmax scale
+  float scale_log2;      // scale * log2(e)
+  int causal_diag;
+  uint32_t* err;
+  uint64_t timeout_ns;
+};
+
+// Delta_i = dO_i . O_i in fp32: 8 elements (16 bytes) per thread, D / 8 threads per row, grid-stride.
+template <bool kF16, int kD>
+__global__ void __launch_bounds__(256) bsattn_bwd_delta_kernel(const uint16_t* __restrict__ dO,
+                                                               const uint16_t* __restrict__ O,
+                                                               float* __restrict__ delta, int64_t rows) {
+  constexpr int kTpr = kD / 8;  // threads per row: 16 (D = 128) or 8 (D = 64), a power of two
+  const int64_t total = rows * kTpr;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i - (threadIdx.x & 31) < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float acc = 0.0f;
+    if (i < total) {
+      const uint4 a = reinterpret_cast<const uint4*>(dO)[i];
+      const uint4 b = reinterpret_cast<const uint4*>(O)[i];
+      const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float a0, a1, b0, b1;
+        if (kF16) {
+          const float2 fa = __half22float2(*reinterpret_cast<const __half2*>(&wa[k]));
+          const float2 fb = __half22float2(*reinterpret_cast<const __half2*>(&wb[k]));
+          a0 = fa.x; a1 = fa.y; b0 = fb.x; b1 = fb.y;
+        } else {
+          const float2 fa = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wa[k]));
+          const float2 fb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&wb[k]));
+          a0 = fa.x; a1 = fa.y; b0 = fb.x; b1 = fb.y;
+        }
+        acc = fmaf(a0, b0, acc);
+        acc = fmaf(a1, b1, acc);
+      }
+    }
+#pragma unroll
+    for (int o = kTpr / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
+    if (i < total && (i % kTpr) == 0) delta[i / kTpr] = acc;
+  }
+}
+
+// Column lists of the block mask: for every (b,h) pair, the query blocks of each key block-column in ascending
+// order (a counting sort of the row lists, one thread per pair). col_ptr shares row_ptr's numbering: pair p's
+// entries occupy [row_ptr[p*nqb], row_ptr[(p+1)*nqb]) in both. Out-of-range key blocks are dropped and flagged.
+__global__ void bsattn_mask_transpose_kernel(const int* __restrict__ row_ptr, const int* __restrict__ col_idx,
+                                             int pairs, int nqb, int* __restrict__ col_ptr,
+                                             int* __restrict__ row_idx, int* __restrict__ cursor,
+                                             int* __restrict__ bad) {
+  for (int p = blockIdx.x * blockDim.x + threadIdx.x; p < pairs; p += gridDim.x * blockDim.x) {
+    const int base = row_ptr[p * nqb];
+    int* cnt = cursor + static_cast<int64_t>(p) * nqb;
+    for (int j = 0; j < nqb; ++j) cnt[j] = 0;
+    for (int i = 0; i < nqb; ++i)
+      for (int e = row_ptr[p * nqb + i]; e < row_ptr[p * nqb + i + 1]; ++e) {
+        const int kb = col_idx[e];
+        if (kb < 0 || kb >= nqb) {
+          *bad = 1;
+          continue;
+        }
+        ++cnt[kb];
+      }
+    int run = base;
+    for (int j = 0; j < nqb; ++j) {
+      const int c = cnt[j];
+      col_ptr[p * nqb + j] = run;
+      cnt[j] = run;
+      run += c;
+    }
+    if (p == pairs - 1) col_ptr[pairs * nqb] = run;
+    for (int i = 0; i < nqb; ++i)
+      for (int e = row_ptr[p * nqb + i]; e < row_ptr[p * nqb + i + 1]; ++e) {
+        const int kb = col_idx[e];
+        if (kb >= 0 && kb < nqb) row_idx[cnt[kb]++] = i;
+      }
+  }
+}
+
+template <bool kF16>
+__device__ __forceinline__ void store_row_half(uint16_t* dst, const uint32_t (&u)[32], float mul) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+    d[g] = make_uint4(pack2<kF16>(__uint_as_float(u[8 * g + 0]) * mul, __uint_as_float(u[8 * g + 1]) * mul),
+                      pack2<kF16>(__uint_as_float(u[8 * g + 2]) * mul, __uint_as_float(u[8 * g + 3]) * mul),
+                      pack2<kF16>(__uint_as_float(u[8 * g + 4]) * mul, __uint_as_float(u[8 * g + 5]) * mul),
+                      pack2<kF16>(__uint_as_float(u[8 * g + 6]) * mul, __uint_as_float(u[8 * g + 7]) * mul));
+}
+
+// TMEM columns [t0 + 32 * (D/64) * x, ...) of this thread's row (kD/2 columns: warpgroup x's half of an
+// accumulator) -> scaled fp16/bf16 row segment.
+template <bool kF16, int kD>
+__device__ __forceinline__ void write_acc_half(uint32_t t_row, int x, uint16_t* row_out, float mul) {
+#pragma unroll 1
+  for (int cc = 0; cc < kD / 64; ++cc) {
+    const int col = x * (kD / 2) + cc * 32;
+    uint32_t u[32];
+    ptx::tmem_ld_32x32b_x32(t_row + col, u);
+    ptx::tmem_wait_ld();
+    store_row_half<kF16>(row_out + col, u, mul);
+  }
+}
+
+template <int kD>
+__device__ __forceinline__ void zero_row_half(int x, uint16_t* row_out) {
+  const uint4 z = make_uint4(0, 0, 0, 0);
+#pragma unroll
+  for (int cc = 0; cc < kD / 16; ++cc) reinterpret_cast<uint4*>(row_out + x * (kD / 2))[cc] = z;
+}
+
+// ------------------------------------------------------------------------------------------------ dQ pass
+// Item = (b,h) pair and query block i; streams the K_j / V_j tiles of row i's key blocks through a ring.
+// TMEM: S [0,128), dP [128,256), dQ accumulator [256, 256 + D), dS (packed pairs) [384, 448).
+template <bool kF16, int kD>
+struct BwdDqShape {
+  static constexpr int kTile = kAttnBlk * kD * 2;
+  static constexpr int kChunks = kD / 64;
+  static constexpr int kSlots = kD == 128 ? 4 : 8;
+  static constexpr int kSmemBytes = 1024 + kTile * (2 + kSlots) + 512;
+};
+
+template <bool kF16, int kD>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    bsattn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                         const AttnBwdArgs a) {
+  using Sh = BwdDqShape<kF16, kD>;
+  constexpr int kTile = Sh::kTile;
+  constexpr int kSlots = Sh::kSlots;
+  constexpr uint32_t kFmt = kF16 ? 0u : 1u;
+  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 128, kFmt, kFmt, 0, 0);   // S, dP: K = D, both K-major
+  constexpr uint32_t IDESC_DQ = ptx::instr_desc(128, kD, kFmt, kFmt, 0, 1);   // dQ += dS K: K MN-major
+  constexpr uint32_t T_S = 0, T_DP = 128, T_DQ = 256, T_DS = 384;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sdO = sQ + kTile;
+  uint8_t* sKV = sdO + kTile;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kSlots * kTile);
+  uint64_t* qd_full = bars + 0;
+  uint64_t* qd_empty = bars + 1;
+  uint64_t* kv_full = bars + 2;
+  uint64_t* kv_empty = kv_full + kSlots;
+  uint64_t* sdp_full = kv_empty + kSlots;
+  uint64_t* ds_full = sdp_full + 1;
+  uint64_t* dq_done = ds_full + 1;
+  uint64_t* drain = dq_done + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(ptx::smem_u32(qd_full), 1);
+    ptx::mbar_init(ptx::smem_u32(qd_empty), 1);
+    for (int s = 0; s < kSlots; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&kv_full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&kv_empty[s]), 1);
+    }
+    ptx::mbar_init(ptx::smem_u32(sdp_full), 1);
+    ptx::mbar_init(ptx::smem_u32(ds_full), 8);
+    ptx::mbar_init(ptx::smem_u32(dq_done), 1);
+    ptx::mbar_init(ptx::smem_u32(drain), 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmQ);
+    ptx::prefetch_tmap(&tmK);
+    ptx::prefetch_tmap(&tmV);
+    ptx::prefetch_tmap(&tmdO);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), kAttnTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  WaitCtl ctl{abort_flag, a.err, a.timeout_ns, kKidBsAttnBwd};
+  if (warp < 4) ptx::setmaxnreg_dec<kAttnRegsLow>();
+
+  // item -> (bh, query block), longest rows (last blocks under a causal mask) first
+  auto item_of = [&](int item, int& bh, int& qb, int& j0, int& n) {
+    bh = a.bh_begin + item / a.nqb;
+    qb = a.nqb - 1 - item % a.nqb;
+    const int p = bh * a.nqb + qb;
+    j0 = __ldg(&a.row_ptr[p]);
+    n = max(__ldg(&a.row_ptr[p + 1]) - j0, 0);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (one thread)
+    if (lane == 0) {
+      uint32_t qd_phase = 0, slot = 0, slot_phase = 0, qd_issued = 0, kv_issued = 0;
+      bool ok = true;
+      const uint32_t kv0 = ptx::smem_u32(sKV);
+      auto push = [&](const CUtensorMap* m, int row) -> bool {
+        if (!wait_bounded<false, 512>(ptx::smem_u32(&kv_empty[slot]), slot_phase ^ 1, ctl, 2)) return false;
+        const uint32_t fb = ptx::smem_u32(&kv_full[slot]);
+        ptx::mbar_arrive_expect_tx(fb, kTile);
+#pragma unroll
+        for (int c = 0; c < Sh::kChunks; ++c) ptx::tma_load_2d(kv0 + slot * kTile + c * kAttnChunk, m, fb, 64 * c, row);
+        ++kv_issued;
+        if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
+        return true;
+      };
+      for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
+        int bh, qb, j0, n;
+        item_of(item, bh, qb, j0, n);
+        if (n == 0) continue;
+        ok = wait_bounded<false, 512>(ptx::smem_u32(qd_empty), qd_phase ^ 1, ctl, 1);
+        if (!ok) break;
+        const uint32_t qf = ptx::smem_u32(qd_full);
+        ptx::mbar_arrive_expect_tx(qf, 2 * kTile);
+        const int qrow = bh * a.S + qb * kAttnBlk;
+#pragma unroll
+        for (int c = 0; c < Sh::kChunks; ++c) {
+          ptx::tma_load_2d(ptx::smem_u32(sQ) + c * kAttnChunk, &tmQ, qf, 64 * c, qrow);
+          ptx::tma_load_2d(ptx::smem_u32(sdO) + c * kAttnChunk, &tmdO, qf, 64 * c, qrow);
+        }
+        ++qd_issued;
+        qd_phase ^= 1;
+        for (int j = 0; j < n && ok; ++j) {
+          int kb = __ldg(&a.col_idx[j0 + j]);
+          if (kb < 0 || kb >= a.nqb) {  // out-of-range index: flag it; the loads read zero fill
+            atomicCAS(a.err, 0u, kErrBounds | (kKidBsAttnBwd << 8) | (7u << 16));
+            kb = a.nqb;
+          }
+          const int krow = bh * a.S + kb * kAttnBlk;
+          ok = push(&tmK, krow) && push(&tmV, krow);
+        }
+      }
+      WaitCtl dctl = ctl;
+      volatile int never = 0;
+      dctl.abort = &never;
+      if (qd_issued) wait_bounded(ptx::smem_u32(qd_full), (qd_issued - 1) & 1, dctl, 8);
+      const uint32_t first = kv_issued > kSlots ? kv_issued - kSlots : 0;
+      for (uint32_t i = first; i < kv_issued; ++i)
+        wait_bounded(ptx::smem_u32(&kv_full[i % kSlots]), (i / kSlots) & 1, dctl, 8);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      uint32_t qd_phase = 0, slot = 0, slot_phase = 0, ds_cnt = 0;
+      bool ok = true;
+      const uint32_t kv0 = ptx::smem_u32(sKV), q0 = ptx::smem_u32(sQ), do0 = ptx::smem_u32(sdO);
+      auto take = [&](uint32_t site) -> uint32_t {
+        if (!wait_bounded(ptx::smem_u32(&kv_full[slot]), slot_phase, ctl, site)) return 0xFFFFFFFFu;
+        const uint32_t s = slot;
+        if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
+        return s;
+      };
+      // D[tmem] = A B^T over K = D: both operands K-major 128-row tiles in 64-column chunks
+      auto mma_kmajor = [&](uint32_t d, uint32_t A, uint32_t B) {
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k) {
+          const uint32_t off = (k >> 2) * kAttnChunk + (k & 3) * 32;
+          ptx::mma_f16_ss(tmem_base + d, ptx::smem_desc(A + off, 16, 1024), ptx::smem_desc(B + off, 16, 1024),
+                          IDESC_S, k != 0);
+        }
+      };
+      for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
+        int bh, qb, j0, n;
+        item_of(item, bh, qb, j0, n);
+        if (n == 0) continue;
+        ok = wait_bounded(ptx::smem_u32(qd_full), qd_phase, ctl, 10);
+        if (!ok) break;
+        qd_phase ^= 1;
+        for (int j = 0; j < n && ok; ++j) {
+          const uint32_t sk = take(11);
+          if (sk == 0xFFFFFFFFu) { ok = false; break; }
+          const uint32_t sv = take(12);
+          if (sv == 0xFFFFFFFFu) { ok = false; break; }
+          ptx::tc_fence_after();
+          mma_kmajor(T_S, q0, kv0 + sk * kTile);    // S = Q K^T
+          mma_kmajor(T_DP, do0, kv0 + sv * kTile);  // dP = dO V^T
+          ptx::mma_commit(ptx::smem_u32(&kv_empty[sv]));
+          ptx::mma_commit(ptx::smem_u32(sdp_full));
+          ok = wait_bounded(ptx::smem_u32(ds_full), ds_cnt & 1, ctl, 13);  // dS of block j in TMEM
+          if (!ok) break;
+          ++ds_cnt;
+          ptx::tc_fence_after();
+          const uint32_t kA = kv0 + sk * kTile;
+#pragma unroll
+          for (int k = 0; k < 8; ++k)  // dQ += dS K: K step k = kv rows [16k, 16k + 16), dS columns [8k, 8k + 8)
+            ptx::mma_f16_ts(tmem_base + T_DQ, tmem_base + T_DS + 8 * k,
+                            ptx::smem_desc(kA + k * 2048, kAttnChunk, 1024), IDESC_DQ, (j == 0 && k == 0) ? 0u : 1u);
+          ptx::mma_commit(ptx::smem_u32(&kv_empty[sk]));
+        }
+        if (!ok) break;
+        ptx::mma_commit(ptx::smem_u32(dq_done));
+        ptx::mma_commit(ptx::smem_u32(qd_empty));
+      }
+      ptx::mma_commit(ptx::smem_u32(drain));
+      WaitCtl dctl = ctl;
+      volatile int never = 0;
+      dctl.abort = &never;
+      wait_bounded(ptx::smem_u32(drain), 0, dctl, 15);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ dS = P (dP - Delta), dQ out
+    ptx::setmaxnreg_inc<kAttnRegsHigh>();
+    const int x = (warp - 4) >> 2;  // column half
+    const int q = warp & 3;
+    const int r = 32 * q + lane;    // query row within the block == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
+    const float c = a.scale_log2;
+    uint32_t sdp_cnt = 0, dq_cnt = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
+      int bh, qb, j0, n;
+      item_of(item, bh, qb, j0, n);
+      const int64_t grow = static_cast<int64_t>(bh) * a.S + qb * kAttnBlk + r;
+      uint16_t* dq_row = static_cast<uint16_t*>(a.dQ) + grow * kD;
+      if (n == 0) {
+        zero_row_half<kD>(x, dq_row);
+        continue;
+      }
+      const float lse2 = __ldg(&a.lse[grow]) * 1.4426950408889634f;
+      const float dlt = __ldg(&a.delta[grow]);
+      for (int j = 0; j < n; ++j) {
+        const int kb = __ldg(&a.col_idx[j0 + j]);
+        const bool diag = a.causal_diag && kb == qb;
+        ok = warp_wait_bounded(ptx::smem_u32(sdp_full), sdp_cnt & 1, ctl, 20);
+        if (!ok) break;
+        ++sdp_cnt;
+        ptx::tc_fence_after();
+        uint32_t sv[64], dv[64];
+        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_S + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_S + 64 * x + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_DP + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
+        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_DP + 64 * x + 32, *reinterpret_cast<uint32_t(*)[32]>(&dv[32]));
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {
+          const int col = 64 * x + i;
+          float p0 = ex2_approx(fmaf(__uint_as_float(sv[i]), c, -lse2));
+          float p1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), c, -lse2));
+          if (diag && col > r) p0 = 0.0f;
+          if (diag && col + 1 > r) p1 = 0.0f;
+          const float d0 = p0 * (__uint_as_float(dv[i]) - dlt);
+          const float d1 = p1 * (__uint_as_float(dv[i + 1]) - dlt);
+          sv[i >> 1] = pack2<kF16>(d0, d1);
+        }
+        ptx::tmem_st_32x32b_x32(tmem_base + lane_off + T_DS + 32 * x, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(ds_full));
+      }
+      if (!ok) break;
+      ok = warp_wait_bounded<false, 256>(ptx::smem_u32(dq_done), dq_cnt & 1, ctl, 22);
+      if (!ok) break;
+      ++dq_cnt;
+      ptx::tc_fence_after();
+      write_acc_half<kF16, kD>(tmem_base + lane_off + T_DQ, x, dq_row, a.scale);
+      ptx::tc_fence_before();
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  if (warp == 1) ptx::tmem_dealloc(tmem_base, kAttnTmemCols);
+}
+
+// ------------------------------------------------------------------------------------------------ dK/dV pass
+// Item = (b,h) pair and key block j; streams Q_i, dO_i (+ LSE_i, Delta_i) of column j's query blocks.
+// TMEM: S^T [0,128) -> packed P^T in [0,32) and [64,96); dP^T [128,256) -> packed dS^T in [128,160) and
+// [192,224); dV accumulator [256, 256 + D), dK accumulator [256 + D, 256 + 2D).
+template <bool kF16, int kD>
+struct BwdDkdvShape {
+  static constexpr int kTile = kAttnBlk * kD * 2;
+  static constexpr int kChunks = kD / 64;
+  static constexpr int kSlotBytes = 2 * kTile + 1024;  // Q, dO, LSE[128], Delta[128]
+  static constexpr int kSlots = kD == 128 ? 2 : 4;
+  static constexpr int kSmemBytes = 1024 + 2 * kTile + kSlots * kSlotBytes + 512;
+};
+
+template <bool kF16, int kD>
+__global__ void __launch_bounds__(kAttnThreads, 1)
+    bsattn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                           const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
+                           const AttnBwdArgs a) {
+  using Sh = BwdDkdvShape<kF16, kD>;
+  constexpr int kTile = Sh::kTile;
+  constexpr int kSlots = Sh::kSlots;
+  constexpr int kSlotBytes = Sh::kSlotBytes;
+  constexpr uint32_t kFmt = kF16 ? 0u : 1u;
+  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 128, kFmt, kFmt, 0, 0);   // S^T, dP^T: K = D, K-major
+  constexpr uint32_t IDESC_ACC = ptx::instr_desc(128, kD, kFmt, kFmt, 0, 1);  // dV, dK: B (dO, Q) MN-major
+  constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + kD;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sK = smem;
+  uint8_t* sV = sK + kTile;
+  uint8_t* sQD = sV + kTile;  // [kSlots] x (Q tile, dO tile, LSE, Delta)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sQD + kSlots * kSlotBytes);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* kv_empty = bars + 1;
+  uint64_t* qd_full = bars + 2;
+  uint64_t* qd_empty = qd_full + kSlots;
+  uint64_t* sdp_full = qd_empty + kSlots;
+  uint64_t* p_full = sdp_full + 1;
+  uint64_t* acc_done = p_full + 1;
+  uint64_t* drain = acc_done + 1;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(ptx::smem_u32(kv_full), 1);
+    ptx::mbar_init(ptx::smem_u32(kv_empty), 1);
+    for (int s = 0; s < kSlots; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&qd_full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&qd_empty[s]), 1);
+    }
+    ptx::mbar_init(ptx::smem_u32(sdp_full), 1);
+    ptx::mbar_init(ptx::smem_u32(p_full), 8);
+    ptx::mbar_init(ptx::smem_u32(acc_done), 1);
+    ptx::mbar_init(ptx::smem_u32(drain), 1);
+    *abort_flag = 0;
+    ptx::fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    ptx::prefetch_tmap(&tmQ);
+    ptx::prefetch_tmap(&tmK);
+    ptx::prefetch_tmap(&tmV);
+    ptx::prefetch_tmap(&tmdO);
+  }
+  if (warp == 1) {
+    ptx::tmem_alloc(ptx::smem_u32(tmem_holder), kAttnTmemCols);
+    ptx::tmem_relinquish();
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tmem_base = *tmem_holder;
+  WaitCtl ctl{abort_flag, a.err, a.timeout_ns, kKidBsAttnBwd};
+  if (warp < 4) ptx::setmaxnreg_dec<kAttnRegsLow>();
+
+  // item -> (bh, key block), column list [i0, i0 + n) of query blocks
+  auto item_of = [&](int item, int& bh, int& kb, int& i0, int& n) {
+    bh = a.bh_begin + item / a.nqb;
+    kb = item % a.nqb;
+    const int p = bh * a.nqb + kb;
+    i0 = __ldg(&a.col_ptr[p]);
+    n = max(__ldg(&a.col_ptr[p + 1]) - i0, 0);
+  };
+  auto qblock = [&](int e) -> int {  // query block of column entry e, clamped (flagged) when out of range
+    int qb = __ldg(&a.row_idx[e]);
+    if (qb < 0 || qb >= a.nqb) {
+      atomicCAS(a.err, 0u, kErrBounds | (kKidBsAttnBwd << 8) | (9u << 16));
+      qb = a.nqb;
+    }
+    return qb;
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer (one thread)
+    if (lane == 0) {
+      uint32_t kv_phase = 0, slot = 0, slot_phase = 0, kv_issued = 0, qd_issued = 0;
+      bool ok = true;
+      const uint32_t qd0 = ptx::smem_u32(sQD);
+      for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
+        int bh, kb, i0, n;
+        item_of(item, bh, kb, i0, n);
+        if (n == 0) continue;
+        ok = wait_bounded<false, 512>(ptx::smem_u32(kv_empty), kv_phase ^ 1, ctl, 1);
+        if (!ok) break;
+        const uint32_t kf = ptx::smem_u32(kv_full);
+        ptx::mbar_arrive_expect_tx(kf, 2 * kTile);
+        const int krow = bh * a.S + kb * kAttnBlk;
+#pragma unroll
+        for (int c = 0; c < Sh::kChunks; ++c) {
+          ptx::tma_load_2d(ptx::smem_u32(sK) + c * kAttnChunk, &tmK, kf, 64 * c, krow);
+          ptx::tma_load_2d(ptx::smem_u32(sV) + c * kAttnChunk, &tmV, kf, 64 * c, krow);
+        }
+        ++kv_issued;
+        kv_phase ^= 1;
+        for (int t = 0; t < n && ok; ++t) {
+          const int qb = qblock(i0 + t);
+          ok = wait_bounded<false, 512>(ptx::smem_u32(&qd_empty[slot]), slot_phase ^ 1, ctl, 2);
+          if (!ok) break;
+          const uint32_t fb = ptx::smem_u32(&qd_full[slot]);
+          const uint32_t dst = qd0 + slot * kSlotBytes;
+          const int qrow = bh * a.S + qb * kAttnBlk;
+          if (qb < a.nqb) {
+            ptx::mbar_arrive_expect_tx(fb, 2 * kTile + 1024);
+            ptx::bulk_load_1d(dst + 2 * kTile, a.lse + qrow, 512, fb);
+            ptx::bulk_load_1d(dst + 2 * kTile + 512, a.delta + qrow, 512, fb);
+          } else {
+            ptx::mbar_arrive_expect_tx(fb, 2 * kTile);  // zero-filled tiles; LSE / Delta left unread (P = 0)
+          }
+#pragma unroll
+          for (int c = 0; c < Sh::kChunks; ++c) {
+            ptx::tma_load_2d(dst + c * kAttnChunk, &tmQ, fb, 64 * c, qrow);
+            ptx::tma_load_2d(dst + kTile + c * kAttnChunk, &tmdO, fb, 64 * c, qrow);
+          }
+          ++qd_issued;
+          if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
+        }
+      }
+      WaitCtl dctl = ctl;
+      volatile int never = 0;
+      dctl.abort = &never;
+      if (kv_issued) wait_bounded(ptx::smem_u32(kv_full), (kv_issued - 1) & 1, dctl, 8);
+      const uint32_t first = qd_issued > kSlots ? qd_issued - kSlots : 0;
+      for (uint32_t i = first; i < qd_issued; ++i)
+        wait_bounded(ptx::smem_u32(&qd_full[i % kSlots]), (i / kSlots) & 1, dctl, 8);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer (one thread)
+    if (lane == 0) {
+      uint32_t kv_phase = 0, slot = 0, slot_phase = 0, p_cnt = 0;
+      bool ok = true;
+      const uint32_t qd0 = ptx::smem_u32(sQD), k0 = ptx::smem_u32(sK), v0 = ptx::smem_u32(sV);
+      auto mma_kmajor = [&](uint32_t d, uint32_t A, uint32_t B) {
+#pragma unroll
+        for (int k = 0; k < kD / 16; ++k) {
+          const uint32_t off = (k >> 2) * kAttnChunk + (k & 3) * 32;
+          ptx::mma_f16_ss(tmem_base + d, ptx::smem_desc(A + off, 16, 1024), ptx::smem_desc(B + off, 16, 1024),
+                          IDESC_S, k != 0);
+        }
+      };
+      for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
+        int bh, kb, i0, n;
+        item_of(item, bh, kb, i0, n);
+        if (n == 0) continue;
+        ok = wait_bounded(ptx::smem_u32(kv_full), kv_phase, ctl, 10);
+        if (!ok) break;
+        kv_phase ^= 1;
+        for (int t = 0; t < n && ok; ++t) {
+          ok = wait_bounded(ptx::smem_u32(&qd_full[slot]), slot_phase, ctl, 11);
+          if (!ok) break;
+          ptx::tc_fence_after();
+          const uint32_t qA = qd0 + slot * kSlotBytes, dA = qA + kTile;
+          mma_kmajor(T_S, k0, qA);   // S^T = K Q^T
+          mma_kmajor(T_DP, v0, dA);  // dP^T = V dO^T
+          ptx::mma_commit(ptx::smem_u32(sdp_full));
+          ok = wait_bounded(ptx::smem_u32(p_full), p_cnt & 1, ctl, 12);  // P^T, dS^T in TMEM
+          if (!ok) break;
+          ++p_cnt;
+          ptx::tc_fence_after();
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {  // K step k = query rows [16k, 16k + 16): packed columns 8k (+32 for k >= 4)
+            const uint32_t acc = (t == 0 && k == 0) ? 0u : 1u;
+            const uint32_t pc = 8 * k + (k >= 4 ? 32 : 0);
+            ptx::mma_f16_ts(tmem_base + T_DV, tmem_base + T_S + pc,
+                            ptx::smem_desc(dA + k * 2048, kAttnChunk, 1024), IDESC_ACC, acc);   // dV += P^T dO
+            ptx::mma_f16_ts(tmem_base + T_DK, tmem_base + T_DP + pc,
+                            ptx::smem_desc(qA + k * 2048, kAttnChunk, 1024), IDESC_ACC, acc);   // dK += dS^T Q
+          }
+          ptx::mma_commit(ptx::smem_u32(&qd_empty[slot]));
+          if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
+        }
+        if (!ok) break;
+        ptx::mma_commit(ptx::smem_u32(acc_done));
+        ptx::mma_commit(ptx::smem_u32(kv_empty));
+      }
+      ptx::mma_commit(ptx::smem_u32(drain));
+      WaitCtl dctl = ctl;
+      volatile int never = 0;
+      dctl.abort = &never;
+      wait_bounded(ptx::smem_u32(drain), 0, dctl, 15);
+    }
+    __syncwarp();
+  } else if (warp >= 4) {
+    // ------------------------------------------------------------------ P^T, dS^T, dK / dV out
+    ptx::setmaxnreg_inc<kAttnRegsHigh>();
+    const int x = (warp - 4) >> 2;  // column half (query positions [64x, 64x + 64))
+    const int q = warp & 3;
+    const int r = 32 * q + lane;    // key row within the block == TMEM lane
+    const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
+    const float c = a.scale_log2;
+    uint32_t sdp_cnt = 0, acc_cnt = 0, slot = 0, slot_phase = 0;
+    bool ok = true;
+    const uint8_t* qd_base = sQD;
+    for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
+      int bh, kb, i0, n;
+      item_of(item, bh, kb, i0, n);
+      const int64_t grow = static_cast<int64_t>(bh) * a.S + kb * kAttnBlk + r;
+      uint16_t* dk_row = static_cast<uint16_t*>(a.dK) + grow * kD;
+      uint16_t* dv_row = static_cast<uint16_t*>(a.dV) + grow * kD;
+      if (n == 0) {
+        zero_row_half<kD>(x, dk_row);
+        zero_row_half<kD>(x, dv_row);
+        continue;
+      }
+      for (int t = 0; t < n; ++t) {
+        const int qb = __ldg(&a.row_idx[i0 + t]);
+        const bool valid = qb >= 0 && qb < a.nqb;
+        const bool diag = a.causal_diag && qb == kb;
+        ok = warp_wait_bounded(ptx::smem_u32(&qd_full[slot]), slot_phase, ctl, 19);  // LSE / Delta landed
+        if (ok) ok = warp_wait_bounded(ptx::smem_u32(sdp_full), sdp_cnt & 1, ctl, 20);
+        if (!ok) break;
+        ++sdp_cnt;
+        ptx::tc_fence_after();
+        const float* lse_s = reinterpret_cast<const float*>(qd_base + slot * kSlotBytes + 2 * kTile);
+        const float* dlt_s = lse_s + 128;
+        uint32_t sv[64], dv[64];
+        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_S + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_S + 64 * x + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_DP + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
+        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_DP + 64 * x + 32, *reinterpret_cast<uint32_t(*)[32]>(&dv[32]));
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {
+          const int col = 64 * x + i;  // query position within the block
+          float p0 = 0.0f, p1 = 0.0f, d0 = 0.0f, d1 = 0.0f;
+          if (valid) {
+            p0 = ex2_approx(fmaf(__uint_as_float(sv[i]), c, -lse_s[col] * 1.4426950408889634f));
+            p1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), c, -lse_s[col + 1] * 1.4426950408889634f));
+            if (diag && r > col) p0 = 0.0f;  // key position above the query position
+            if (diag && r > col + 1) p1 = 0.0f;
+            d0 = p0 * (__uint_as_float(dv[i]) - dlt_s[col]);
+            d1 = p1 * (__uint_as_float(dv[i + 1]) - dlt_s[col + 1]);
+          }
+          sv[i >> 1] = pack2<kF16>(p0, p1);
+          dv[i >> 1] = pack2<kF16>(d0, d1);
+        }
+        // Packed P^T / dS^T of this warpgroup's 64 query columns go to the first 32 of the columns it read itself
+        // ([64x, 64x + 32) of each buffer), so no other warp's pending reads are overwritten.
+        ptx::tmem_st_32x32b_x32(tmem_base + lane_off + T_S + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        ptx::tmem_st_32x32b_x32(tmem_base + lane_off + T_DP + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(p_full));
+        if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
+      }
+      if (!ok) break;
+      ok = warp_wait_bounded<false, 256>(ptx::smem_u32(acc_done), acc_cnt & 1, ctl, 22);
+      if (!ok) break;
+      ++acc_cnt;
+      ptx::tc_fence_after();
+      write_acc_half<kF16, kD>(tmem_base + lane_off + T_DV, x, dv_row, 1.0f);
+      write_acc_half<kF16, kD>(tmem_base + lane_off + T_DK, x, dk_row, a.scale);
+      ptx::tc_fence_before();
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  if (warp == 1) ptx::tmem_dealloc(tmem_base, kAttnTmemCols);
+}
+
+}  // namespace bsk

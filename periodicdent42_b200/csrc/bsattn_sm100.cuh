@@ -52,6 +52,7 @@ static_assert(128 * kAttnRegsLow + 256 * kAttnRegsHigh <= kAttnThreads * kAttnRe
 
 struct AttnArgs {
   void* O;            // fp16 or bf16 [B*H*S, D]
+  float* lse;         // optional [B*H*S]: natural-log log-sum-exp of each row's scaled scores (-inf: empty row)
   const int* row_ptr;
   const int* col_idx;
   int S;              // sequence length
@@ -380,11 +381,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       attn_item(a, item, bh, A, B);
       const AttnStream st = x == 0 ? A : B;
       if (st.qb < 0) continue;
-      uint16_t* orow = static_cast<uint16_t*>(a.O) + (static_cast<int64_t>(bh) * a.S + st.qb * kAttnBlk + r) * kD;
+      const int64_t grow = static_cast<int64_t>(bh) * a.S + st.qb * kAttnBlk + r;
+      uint16_t* orow = static_cast<uint16_t*>(a.O) + grow * kD;
       if (st.n <= 0) {
         const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
         for (int cc = 0; cc < kD / 8; ++cc) reinterpret_cast<uint4*>(orow)[cc] = z;
+        if (a.lse) a.lse[grow] = -INFINITY;
         continue;
       }
       float m_run = -INFINITY, l_run = 0.0f;  // m_run in scaled log2 units
@@ -475,6 +478,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ++o_cnt;
       ptx::tc_fence_after();
       const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
+      // l_run sums 2^(s*c - m_run) whatever m_run lagged behind, so m_run + log2(l_run) is exact
+      if (a.lse) a.lse[grow] = l_run > 0.0f ? (m_run + log2f(l_run)) * 0.6931471805599453f : -INFINITY;
 #pragma unroll 1
       for (int cc = 0; cc < kD / 32; ++cc) {
         uint32_t u[32];

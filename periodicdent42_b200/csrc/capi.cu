@@ -18,6 +18,7 @@
 #include "gemm_pair_sm100.cuh"
 #include "bsattn_sm100.cuh"
 #include "bsr_convert.cuh"
+#include "bsattn_bwd_sm100.cuh"
 
 namespace {
 
@@ -141,6 +142,14 @@ void init_device(DeviceState& st, int dev) {
       allow_smem(bsattn_sm100_kernel<false, 64>, AttnShape<false, 64>::kSmemBytes),
       allow_smem(bsattn_sm100_kernel<true, 128>, AttnShape<true, 128>::kSmemBytes),
       allow_smem(bsattn_sm100_kernel<true, 64>, AttnShape<true, 64>::kSmemBytes),
+      allow_smem(bsattn_bwd_dq_kernel<false, 128>, BwdDqShape<false, 128>::kSmemBytes),
+      allow_smem(bsattn_bwd_dq_kernel<false, 64>, BwdDqShape<false, 64>::kSmemBytes),
+      allow_smem(bsattn_bwd_dq_kernel<true, 128>, BwdDqShape<true, 128>::kSmemBytes),
+      allow_smem(bsattn_bwd_dq_kernel<true, 64>, BwdDqShape<true, 64>::kSmemBytes),
+      allow_smem(bsattn_bwd_dkdv_kernel<false, 128>, BwdDkdvShape<false, 128>::kSmemBytes),
+      allow_smem(bsattn_bwd_dkdv_kernel<false, 64>, BwdDkdvShape<false, 64>::kSmemBytes),
+      allow_smem(bsattn_bwd_dkdv_kernel<true, 128>, BwdDkdvShape<true, 128>::kSmemBytes),
+      allow_smem(bsattn_bwd_dkdv_kernel<true, 64>, BwdDkdvShape<true, 64>::kSmemBytes),
       allow_smem(gemm_pair_sm100_kernel<2, Epi::F32, 1>, kPairSmemBytes),
       allow_smem(gemm_pair_sm100_kernel<1, Epi::BF16Scaled, 1>, kPairSmemBytes),
       allow_smem(gemm_pair_sm100_kernel<2, Epi::F32, 2>, kPairWideSmemBytes),
@@ -1061,7 +1070,7 @@ namespace {
 
 // Shared launcher of the fp16 and bf16 entry points: same argument checks, element type picks the
 // instantiation and the tensor-map data type.
-int bsattn_launch(bool f16, const void* Q, const void* K, const void* V, void* O, const int32_t* row_ptr,
+int bsattn_launch(bool f16, const void* Q, const void* K, const void* V, void* O, float* lse, const int32_t* row_ptr,
                   const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale, int causal_diag,
                   int bh_begin, int bh_end, void* stream) {
   using namespace bsk;
@@ -1087,6 +1096,7 @@ int bsattn_launch(bool f16, const void* Q, const void* K, const void* V, void* O
   if (int rc = make_map(&tv, dt, 2, V, D, rows, D * 2, 64, kAttnBlk, "V")) return rc;
   AttnArgs a{};
   a.O = O;
+  a.lse = lse;
   a.row_ptr = row_ptr;
   a.col_idx = col_idx;
   a.S = S;
@@ -1115,15 +1125,15 @@ int bsattn_launch(bool f16, const void* Q, const void* K, const void* V, void* O
 int bsk_bsattn_fwd_bf16(const void* Q, const void* K, const void* V, void* O, const int32_t* row_ptr,
                         const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale, int causal_diag,
                         int bh_begin, int bh_end, void* stream) {
-  return bsattn_launch(false, Q, K, V, O, row_ptr, col_idx, B, H, S, D, blk, scale, causal_diag, bh_begin, bh_end,
-                       stream);
+  return bsattn_launch(false, Q, K, V, O, nullptr, row_ptr, col_idx, B, H, S, D, blk, scale, causal_diag, bh_begin,
+                       bh_end, stream);
 }
 
 int bsk_bsattn_fwd_f16(const void* Q, const void* K, const void* V, void* O, const int32_t* row_ptr,
                        const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale, int causal_diag,
                        int bh_begin, int bh_end, void* stream) {
-  return bsattn_launch(true, Q, K, V, O, row_ptr, col_idx, B, H, S, D, blk, scale, causal_diag, bh_begin, bh_end,
-                       stream);
+  return bsattn_launch(true, Q, K, V, O, nullptr, row_ptr, col_idx, B, H, S, D, blk, scale, causal_diag, bh_begin,
+                       bh_end, stream);
 }
 
 namespace {
@@ -1464,6 +1474,108 @@ int bsk_csr_to_bsr_bounded(const void* crow, const void* col, int index_bytes_in
   if (max_nnzb == 0) return BSK_OK;
   return csr_fill_enqueue(crow, col, index_bytes_in, vals, elem_bytes, nnz, M, K, bs, row_ptr, col_idx, index_bytes,
                           values, max_nnzb, p, workspace, st, s, what);
+}
+
+int bsk_bsattn_fwd_ex(int dtype, const void* Q, const void* K, const void* V, void* O, float* lse,
+                      const int32_t* row_ptr, const int32_t* col_idx, int B, int H, int S, int D, int blk, float scale,
+                      int causal_diag, int bh_begin, int bh_end, void* stream) {
+  if (dtype != 0 && dtype != 1) return set_error(BSK_ERR_INVALID_ARG, "bsattn_fwd_ex: dtype must be 0 (bf16) or 1 (f16)");
+  if (lse && reinterpret_cast<uintptr_t>(lse) % 4) return set_error(BSK_ERR_INVALID_ARG, "bsattn_fwd_ex: lse misaligned");
+  return bsattn_launch(dtype == 1, Q, K, V, O, lse, row_ptr, col_idx, B, H, S, D, blk, scale, causal_diag, bh_begin,
+                       bh_end, stream);
+}
+
+int bsk_bsattn_mask_transpose(const int32_t* row_ptr, const int32_t* col_idx, int pairs, int nqb, int32_t* col_ptr,
+                              int32_t* row_idx, void* workspace, int64_t workspace_bytes, void* stream) {
+  using namespace bsk;
+  if (pairs < 0 || nqb < 0) return set_error(BSK_ERR_INVALID_ARG, "bsattn_mask_transpose: negative extent");
+  if (!row_ptr || !col_ptr || (pairs > 0 && nqb > 0 && (!col_idx || !row_idx)))
+    return set_error(BSK_ERR_INVALID_ARG, "bsattn_mask_transpose: null pointer");
+  const int64_t need = (int64_t)pairs * nqb * 4 + 16;
+  if (!workspace || workspace_bytes < need)
+    return set_error(BSK_ERR_INVALID_ARG, "bsattn_mask_transpose: workspace of %lld bytes needed", (long long)need);
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (pairs == 0 || nqb == 0) {
+    cudaError_t e = cudaMemcpyAsync(col_ptr, row_ptr, sizeof(int32_t), cudaMemcpyDeviceToDevice, s);
+    return e == cudaSuccess ? BSK_OK : cuda_fail(e, "bsattn_mask_transpose");
+  }
+  int* cursor = static_cast<int*>(workspace);
+  int* bad = reinterpret_cast<int*>(static_cast<char*>(workspace) + (int64_t)pairs * nqb * 4);
+  cudaError_t e = cudaMemsetAsync(bad, 0, sizeof(int), s);
+  if (e != cudaSuccess) return cuda_fail(e, "bsattn_mask_transpose");
+  const int threads = 128, grid = (pairs + threads - 1) / threads;
+  bsattn_mask_transpose_kernel<<<grid, threads, 0, s>>>(row_ptr, col_idx, pairs, nqb, col_ptr, row_idx, cursor, bad);
+  return launch_status("bsattn_mask_transpose");
+}
+
+int bsk_bsattn_bwd(int dtype, const void* dO, const void* Q, const void* K, const void* V, const void* O,
+                   const float* lse, void* dQ, void* dK, void* dV, const int32_t* row_ptr, const int32_t* col_idx,
+                   const int32_t* col_ptr, const int32_t* row_idx, int B, int H, int S, int D, int blk, float scale,
+                   int causal_diag, float* delta, void* stream) {
+  using namespace bsk;
+  const char* what = "bsattn_bwd";
+  if (dtype != 0 && dtype != 1) return set_error(BSK_ERR_INVALID_ARG, "%s: dtype must be 0 (bf16) or 1 (f16)", what);
+  if (D != 64 && D != 128) return set_error(BSK_ERR_UNSUPPORTED, "%s: head_dim %d unsupported (64 or 128)", what, D);
+  if (blk != kAttnBlk) return set_error(BSK_ERR_UNSUPPORTED, "%s: block size %d unsupported (needs %d)", what, blk, kAttnBlk);
+  if (B < 0 || H < 0 || S < 0) return set_error(BSK_ERR_INVALID_ARG, "%s: negative extent", what);
+  if (S % blk) return set_error(BSK_ERR_INVALID_ARG, "%s: S=%d not a multiple of the block size %d", what, S, blk);
+  if (!(scale > 0.0f) || !(scale < 1e30f)) return set_error(BSK_ERR_INVALID_ARG, "%s: scale must be positive and finite", what);
+  const int pairs = B * H;
+  if (pairs == 0 || S == 0) return BSK_OK;
+  if (!dO || !Q || !K || !V || !O || !lse || !dQ || !dK || !dV || !row_ptr || !col_idx || !col_ptr || !row_idx || !delta)
+    return set_error(BSK_ERR_INVALID_ARG, "%s: null pointer", what);
+  if (!aligned16(dO) || !aligned16(Q) || !aligned16(K) || !aligned16(V) || !aligned16(O) || !aligned16(dQ) ||
+      !aligned16(dK) || !aligned16(dV) || !aligned16(lse) || !aligned16(delta))
+    return set_error(BSK_ERR_INVALID_ARG, "%s: tensors must be 16-byte aligned", what);
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const uint64_t rows = (uint64_t)pairs * S;
+  const CUtensorMapDataType dt = dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  CUtensorMap tq, tk, tv, tdo;
+  if (int rc = make_map(&tq, dt, 2, Q, D, rows, D * 2, 64, kAttnBlk, "Q")) return rc;
+  if (int rc = make_map(&tk, dt, 2, K, D, rows, D * 2, 64, kAttnBlk, "K")) return rc;
+  if (int rc = make_map(&tv, dt, 2, V, D, rows, D * 2, 64, kAttnBlk, "V")) return rc;
+  if (int rc = make_map(&tdo, dt, 2, dO, D, rows, D * 2, 64, kAttnBlk, "dO")) return rc;
+  AttnBwdArgs a{};
+  a.dO = dO;
+  a.O = O;
+  a.lse = lse;
+  a.delta = delta;
+  a.dQ = dQ;
+  a.dK = dK;
+  a.dV = dV;
+  a.row_ptr = row_ptr;
+  a.col_idx = col_idx;
+  a.col_ptr = col_ptr;
+  a.row_idx = row_idx;
+  a.S = S;
+  a.nqb = S / blk;
+  a.bh_begin = 0;
+  a.num_items = pairs * a.nqb;
+  a.scale = scale;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.causal_diag = causal_diag;
+  a.err = st->err_word;
+  a.timeout_ns = t_timeout_ns;
+  const int grid = a.num_items < st->sm_count ? a.num_items : st->sm_count;
+  const uint16_t* dO16 = static_cast<const uint16_t*>(dO);
+  const uint16_t* O16 = static_cast<const uint16_t*>(O);
+  const int dgrid = st->sm_count * 8;
+#define BSK_BWD(F16, DD)                                                                                            \
+  do {                                                                                                              \
+    bsattn_bwd_delta_kernel<F16, DD><<<dgrid, 256, 0, s>>>(dO16, O16, delta, (int64_t)rows);                        \
+    bsattn_bwd_dkdv_kernel<F16, DD><<<grid, kAttnThreads, BwdDkdvShape<F16, DD>::kSmemBytes, s>>>(tq, tk, tv, tdo, a); \
+    bsattn_bwd_dq_kernel<F16, DD><<<grid, kAttnThreads, BwdDqShape<F16, DD>::kSmemBytes, s>>>(tq, tk, tv, tdo, a);     \
+  } while (0)
+  if (dtype == 1 && D == 128) BSK_BWD(true, 128);
+  else if (dtype == 1) BSK_BWD(true, 64);
+  else if (D == 128) BSK_BWD(false, 128);
+  else BSK_BWD(false, 64);
+#undef BSK_BWD
+  return launch_status(what);
 }
 
 int bsk_device_error(uint32_t* out) {

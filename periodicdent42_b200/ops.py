@@ -320,7 +320,37 @@ def attention_forward(Q: torch.Tensor, K: torch.Tensor, V: torch.Tensor, scale: 
     if scale is None:
         scale = 1.0 / (D ** 0.5)
     row_ptr, col_idx = block_mask_to_bsr(block_mask, Bsz, H, S // 128, causal, Q.device)
+    if torch.is_grad_enabled() and (Q.requires_grad or K.requires_grad or V.requires_grad):
+        return _BlockSparseAttention.apply(Q, K, V, row_ptr, col_idx, float(scale), bool(causal))
     return _C().bsattn_fwd(Q, K, V, row_ptr, col_idx, float(scale), bool(causal))
+
+
+class _BlockSparseAttention(torch.autograd.Function):
+    """Autograd for block-sparse attention on the sm_100 kernels: the forward also keeps the row log-sum-exp,
+    the backward recomputes the scores block by block (dK/dV per key block, dQ per query block). Replaces the
+    reference's SparseKAttentionFunction (.archive/.../kernels/sparsek.py:100-142), whose CUDA backward was a
+    stub."""
+
+    @staticmethod
+    def forward(ctx, Q, K, V, row_ptr, col_idx, scale, causal):
+        Qc, Kc, Vc = Q.contiguous(), K.contiguous(), V.contiguous()
+        B, H, S, _ = Qc.shape
+        O = torch.empty_like(Qc)
+        lse = torch.empty(B * H * S, dtype=torch.float32, device=Qc.device)
+        _capi.bsattn_fwd_ex(Qc, Kc, Vc, O, lse, row_ptr, col_idx, scale, causal)
+        ctx.save_for_backward(Qc, Kc, Vc, O, lse, row_ptr, col_idx)
+        ctx.scale, ctx.causal = scale, causal
+        return O
+
+    @staticmethod
+    def backward(ctx, dO):
+        Q, K, V, O, lse, row_ptr, col_idx = ctx.saved_tensors
+        B, H, S, _ = Q.shape
+        col_ptr, row_idx = _capi.bsattn_mask_transpose(row_ptr, col_idx, B * H, S // 128)
+        dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
+        _capi.bsattn_bwd(dO.to(Q.dtype).contiguous(), Q, K, V, O, lse, dQ, dK, dV, row_ptr, col_idx, col_ptr,
+                         row_idx, ctx.scale, ctx.causal)
+        return dQ, dK, dV, None, None, None, None
 
 
 def block_mask_to_bsr(block_mask, B: int, H: int, nqb: int, causal: bool, device):
