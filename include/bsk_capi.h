@@ -20,6 +20,7 @@
 #define BSK_CAPI_H_
 
 #include <stdint.h>
+#include <stdbool.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -327,6 +328,20 @@ int bsk_bsattn_bwd(int dtype, const void* dO, const void* Q, const void* K, cons
                    const float* lse, void* dQ, void* dK, void* dV, const int32_t* row_ptr, const int32_t* col_idx,
                    const int32_t* col_ptr, const int32_t* row_idx, int B, int H, int S, int D, int blk, float scale,
                    int causal_diag, float* delta, void* stream);
+
+/*
+ * The reference's attention launchers, same signatures (.archive/src_experiments/blackwell_sparsek/kernels/
+ * attention_fmha.cu:386-426 and :436-453): fp16 [B, H, S, D] tensors, dense attention (causal: key position <=
+ * query position), D = 64 or 128, S a multiple of 128. Implemented with the block-sparse kernels on the full (or
+ * lower-triangular) block mask, built in stream-ordered scratch (cudaMallocAsync / cudaFreeAsync on `stream`).
+ * The backward takes no log-sum-exp, so it first runs the forward into scratch to recompute it. They return
+ * nothing, like the reference; failures are reported through bsk_last_error().
+ */
+void launch_attention_forward(const void* Q, const void* K, const void* V, void* O, int B, int H, int S, int D,
+                              float scale, bool causal, void* stream);
+void launch_attention_backward(const void* grad_out, const void* Q, const void* K, const void* V, const void* O,
+                               void* grad_Q, void* grad_K, void* grad_V, int B, int H, int S, int D, float scale,
+                               bool causal, void* stream);
 
 /*
  * Drop-in for the reference's launcher signature (BlackwellSparseK/src/kernel_launch.cu:33-61).

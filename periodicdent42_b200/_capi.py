@@ -78,6 +78,9 @@ SIGNATURES = {
     "bsk_bsattn_mask_transpose": (_i32, [_vp, _vp, _i32, _i32, _vp, _vp, _vp, _i64, _vp]),
     "bsk_bsattn_bwd": (_i32, [_i32, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32,
                               _i32, _i32, _f32, _i32, _vp, _vp]),
+    "launch_attention_forward": (None, [_vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _f32, ctypes.c_bool, _vp]),
+    "launch_attention_backward": (None, [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i32, _i32, _i32, _i32, _f32,
+                                         ctypes.c_bool, _vp]),
     "launch_bsr_spmm_async": (None, [_vp, _vp, _vp, _i32, _i32, _i32, _vp, _vp, _vp, _i32, _i32, _i32, _vp, _i32,
                                      _i32, _i32, _i32, _i32, _i32, _i32, _vp]),
     "bsk_device_error": (_i32, [ctypes.POINTER(ctypes.c_uint32)]),

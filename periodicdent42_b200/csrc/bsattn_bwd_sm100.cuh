@@ -116,6 +116,22 @@ __global__ void bsattn_mask_transpose_kernel(const int* __restrict__ row_ptr, co
   }
 }
 
+// Block mask of dense (every key block) or causal (key blocks 0..i of query block i) attention for `pairs`
+// (b,h) pairs: one thread per block-row writes its row pointer and column list.
+__global__ void attn_full_mask_kernel(int pairs, int nqb, int causal, int* __restrict__ row_ptr,
+                                      int* __restrict__ col_idx) {
+  const int rows = pairs * nqb;
+  const int64_t per_pair = causal ? static_cast<int64_t>(nqb) * (nqb + 1) / 2 : static_cast<int64_t>(nqb) * nqb;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < rows; t += gridDim.x * blockDim.x) {
+    const int p = t / nqb, i = t % nqb;
+    const int64_t start = p * per_pair + (causal ? static_cast<int64_t>(i) * (i + 1) / 2 : static_cast<int64_t>(i) * nqb);
+    const int n = causal ? i + 1 : nqb;
+    row_ptr[t] = static_cast<int>(start);
+    for (int j = 0; j < n; ++j) col_idx[start + j] = j;
+    if (t == rows - 1) row_ptr[rows] = static_cast<int>(start + n);
+  }
+}
+
 template <bool kF16>
 __device__ __forceinline__ void store_row_half(uint16_t* dst, const uint32_t (&u)[32], float mul) {
   uint4* d = reinterpret_cast<uint4*>(dst);

@@ -1578,6 +1578,101 @@ int bsk_bsattn_bwd(int dtype, const void* dO, const void* Q, const void* K, cons
   return launch_status(what);
 }
 
+namespace {
+
+// Stream-ordered scratch for the reference-signature attention launchers (freed on the same stream).
+struct StreamScratch {
+  cudaStream_t s;
+  std::vector<void*> ptrs;
+  explicit StreamScratch(cudaStream_t st) : s(st) {}
+  void* get(size_t bytes, cudaError_t* e) {
+    void* p = nullptr;
+    if (*e == cudaSuccess) *e = cudaMallocAsync(&p, bytes < 16 ? 16 : bytes, s);
+    if (*e == cudaSuccess) ptrs.push_back(p);
+    return p;
+  }
+  ~StreamScratch() {
+    for (void* p : ptrs) cudaFreeAsync(p, s);
+  }
+};
+
+// Dense or causal block mask of `pairs` (b,h) pairs in stream-ordered scratch.
+int full_mask(StreamScratch& ss, int pairs, int nqb, bool causal, int** row_ptr, int** col_idx, int64_t* nnz,
+              const char* what) {
+  const int64_t per = causal ? (int64_t)nqb * (nqb + 1) / 2 : (int64_t)nqb * nqb;
+  *nnz = per * pairs;
+  if (*nnz >= INT32_MAX) return set_error(BSK_ERR_UNSUPPORTED, "%s: %lld mask blocks exceed int32", what, (long long)*nnz);
+  cudaError_t e = cudaSuccess;
+  *row_ptr = static_cast<int*>(ss.get(((size_t)pairs * nqb + 1) * 4, &e));
+  *col_idx = static_cast<int*>(ss.get((size_t)*nnz * 4, &e));
+  if (e != cudaSuccess) return cuda_fail(e, what);
+  const int rows = pairs * nqb;
+  bsk::attn_full_mask_kernel<<<(rows + 255) / 256, 256, 0, ss.s>>>(pairs, nqb, causal ? 1 : 0, *row_ptr, *col_idx);
+  return launch_status(what);
+}
+
+int ref_attention_checks(int B, int H, int S, int D, const char* what) {
+  if (B < 0 || H < 0 || S < 0) return set_error(BSK_ERR_INVALID_ARG, "%s: negative extent", what);
+  if (D != 64 && D != 128) return set_error(BSK_ERR_UNSUPPORTED, "%s: head_dim %d unsupported (64 or 128)", what, D);
+  if (S % 128) return set_error(BSK_ERR_UNSUPPORTED, "%s: S=%d must be a multiple of 128", what, S);
+  return BSK_OK;
+}
+
+}  // namespace
+
+void launch_attention_forward(const void* Q, const void* K, const void* V, void* O, int B, int H, int S, int D,
+                              float scale, bool causal, void* stream) {
+  const char* what = "launch_attention_forward";
+  if (ref_attention_checks(B, H, S, D, what)) return;
+  if (B * H == 0 || S == 0) return;
+  DeviceState* st;
+  if (device_state(&st)) return;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  StreamScratch ss(s);
+  int *rp = nullptr, *ci = nullptr;
+  int64_t nnz = 0;
+  if (full_mask(ss, B * H, S / 128, causal, &rp, &ci, &nnz, what)) return;
+  if (bsattn_launch(true, Q, K, V, O, nullptr, rp, ci, B, H, S, D, 128, scale, causal ? 1 : 0, 0, B * H, stream) ==
+      BSK_OK)
+    t_last_error.clear();
+}
+
+void launch_attention_backward(const void* grad_out, const void* Q, const void* K, const void* V, const void* O,
+                               void* grad_Q, void* grad_K, void* grad_V, int B, int H, int S, int D, float scale,
+                               bool causal, void* stream) {
+  const char* what = "launch_attention_backward";
+  if (ref_attention_checks(B, H, S, D, what)) return;
+  if (B * H == 0 || S == 0) return;
+  DeviceState* st;
+  if (device_state(&st)) return;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  StreamScratch ss(s);
+  const int pairs = B * H, nqb = S / 128;
+  int *rp = nullptr, *ci = nullptr;
+  int64_t nnz = 0;
+  if (full_mask(ss, pairs, nqb, causal, &rp, &ci, &nnz, what)) return;
+  // The signature carries no log-sum-exp: a forward pass recomputes it (its output goes to scratch).
+  cudaError_t e = cudaSuccess;
+  const size_t rows = (size_t)pairs * S;
+  float* lse = static_cast<float*>(ss.get(rows * 4, &e));
+  float* delta = static_cast<float*>(ss.get(rows * 4, &e));
+  void* o_tmp = ss.get(rows * D * 2, &e);
+  int* col_ptr = static_cast<int*>(ss.get(((size_t)pairs * nqb + 1) * 4, &e));
+  int* row_idx = static_cast<int*>(ss.get((size_t)nnz * 4, &e));
+  void* tws = ss.get((size_t)pairs * nqb * 4 + 16, &e);
+  if (e != cudaSuccess) {
+    cuda_fail(e, what);
+    return;
+  }
+  if (bsattn_launch(true, Q, K, V, o_tmp, lse, rp, ci, B, H, S, D, 128, scale, causal ? 1 : 0, 0, pairs, stream))
+    return;
+  if (bsk_bsattn_mask_transpose(rp, ci, pairs, nqb, col_ptr, row_idx, tws, (int64_t)pairs * nqb * 4 + 16, stream))
+    return;
+  if (bsk_bsattn_bwd(1, grad_out, Q, K, V, O, lse, grad_Q, grad_K, grad_V, rp, ci, col_ptr, row_idx, B, H, S, D, 128,
+                     scale, causal ? 1 : 0, delta, stream) == BSK_OK)
+    t_last_error.clear();
+}
+
 int bsk_device_error(uint32_t* out) {
   if (!out) return set_error(BSK_ERR_INVALID_ARG, "device_error: null output");
   DeviceState* st;

@@ -70,3 +70,48 @@ def test_large_sequence_length(no_device_error, cuda_dev):
     gpu_ref = F.scaled_dot_product_attention(Q, K, V)
     ok, m = ref.validate_correctness(out, gpu_ref, rtol=1e-3, atol=2e-3)
     assert ok, m
+
+
+def _stream():
+    import ctypes
+
+    return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+
+
+@pytest.mark.parametrize("causal", [False, True])
+@pytest.mark.parametrize("B,H,S,D", [(1, 8, 512, 64), (1, 4, 512, 128)])
+def test_reference_c_launchers(no_device_error, cuda_dev, B, H, S, D, causal):
+    """launch_attention_forward / launch_attention_backward with the reference's C signatures (fp16, dense or
+    causal): forward vs SDPA under the reference's tolerance; backward vs fp64 autograd (normwise <= 3 x the error
+    of torch's fp16 backward + 2e-3)."""
+    from periodicdent42_b200 import _capi
+
+    Q, K, V = _inputs(B, H, S, D, cuda_dev)
+    scale = 1.0 / (D ** 0.5)
+    O = torch.empty_like(Q)
+    lib = _capi.lib()
+    lib.launch_attention_forward(Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(), B, H, S, D, scale, causal,
+                                 _stream())
+    torch.cuda.synchronize()
+    assert _capi.last_error() == ""
+    want = F.scaled_dot_product_attention(Q.cpu().float(), K.cpu().float(), V.cpu().float(), scale=scale,
+                                          is_causal=causal)
+    ok, m = ref.validate_correctness(O, want, rtol=1e-3, atol=2e-3)
+    assert ok, m
+    dO = torch.randn(B, H, S, D, generator=torch.Generator().manual_seed(2)).half()
+    dOd = dO.to(cuda_dev)
+    dQ, dK, dV = torch.empty_like(Q), torch.empty_like(K), torch.empty_like(V)
+    lib.launch_attention_backward(dOd.data_ptr(), Q.data_ptr(), K.data_ptr(), V.data_ptr(), O.data_ptr(),
+                                  dQ.data_ptr(), dK.data_ptr(), dV.data_ptr(), B, H, S, D, scale, causal, _stream())
+    torch.cuda.synchronize()
+    assert _capi.last_error() == ""
+
+    def grads(dtype):
+        q, k, v = (t.cpu().to(dtype).requires_grad_(True) for t in (Q, K, V))
+        F.scaled_dot_product_attention(q, k, v, scale=scale, is_causal=causal).backward(dO.to(dtype))
+        return q.grad, k.grad, v.grad
+
+    g64, g16 = grads(torch.float64), grads(torch.float16)
+    for got, want64, lp in zip((dQ, dK, dV), g64, g16):
+        err, base = ref.normwise_rel_err(got.cpu(), want64), ref.normwise_rel_err(lp, want64)
+        assert err <= 3 * base + 2e-3, (err, base)
