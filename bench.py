@@ -374,7 +374,7 @@ def bench_attn_bwd(ctx: Ctx, args, res: dict):
     g = torch.Generator(device=ctx.dev).manual_seed(7)
     dO = torch.randn(q.shape, generator=g, device=ctx.dev).to(q.dtype)
     dQ, dK, dV = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    delta = torch.empty(pairs * cfg.S, dtype=torch.float32, device=ctx.dev)
+    delta = torch.empty(2 * pairs * cfg.S, dtype=torch.float32, device=ctx.dev)
     # the (b,h) pairs of this rank: views starting at pair b0 (row lists rebased to that pair)
     sl = slice(b0, b1)
     Bv = lambda t: t.view(pairs, cfg.S, cfg.D)[sl].view(1, b1 - b0, cfg.S, cfg.D)  # noqa: E731
@@ -384,7 +384,7 @@ def bench_attn_bwd(ctx: Ctx, args, res: dict):
     cp_r = (col_ptr[b0 * nqb:b1 * nqb + 1] - base).contiguous()
     ri_r = row_idx[base:int(rp[b1 * nqb])].contiguous()
     lse_r = lse.view(pairs, cfg.S)[sl].reshape(-1)
-    dl_r = delta.view(pairs, cfg.S)[sl].reshape(-1)
+    dl_r = delta[:2 * (b1 - b0) * cfg.S]  # this rank's scratch: Delta and -LSE log2(e) of its pairs
 
     def step():
         _capi.bsattn_bwd(Bv(dO), Bv(q), Bv(k), Bv(v), Bv(O), lse_r, Bv(dQ), Bv(dK), Bv(dV), rp_r, ci_r, cp_r, ri_r,

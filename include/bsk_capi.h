@@ -318,7 +318,7 @@ int bsk_bsattn_mask_transpose(const int32_t* row_ptr, const int32_t* col_idx, in
  *   P = exp(scale * Q K^T - lse) on the mask (the forward's; causal_diag as there).
  * dO, Q, K, V, O, dQ, dK, dV: [B, H, S, D] contiguous; lse [B*H*S] from bsk_bsattn_fwd_ex; row_ptr/col_idx the
  * forward's mask and col_ptr/row_idx its column lists (bsk_bsattn_mask_transpose); delta: device scratch of
- * B*H*S floats. Deterministic: each output row is produced by one CTA in a fixed order (two passes recompute
+ * 2*B*H*S floats (each row's rowsum(dO * O) and its exponent offset -lse * log2(e)). Deterministic: each output row is produced by one CTA in a fixed order (two passes recompute
  * the scores: one per key block for dK/dV, one per query block for dQ). Rows of dK/dV whose key block no query
  * block attends, and rows of dQ with no key blocks, are zero.
  * The reference declares launch_attention_backward

@@ -402,8 +402,10 @@ def bsattn_bwd(dO, Q, K, V, O, lse, dQ, dK, dV, row_ptr, col_idx, col_ptr, row_i
     import torch
 
     B, H, S, D = Q.shape
-    if delta is None:
-        delta = torch.empty(B * H * S, dtype=torch.float32, device=Q.device)
+    if delta is None:  # per row: rowsum(dO * O) and -lse * log2(e)
+        delta = torch.empty(2 * B * H * S, dtype=torch.float32, device=Q.device)
+    elif delta.numel() < 2 * B * H * S:
+        raise ValueError("delta scratch needs 2 * B * H * S floats")
     check(lib().bsk_bsattn_bwd(_attn_dtype(Q), _ptr(dO), _ptr(Q), _ptr(K), _ptr(V), _ptr(O), _ptr(lse), _ptr(dQ),
                                _ptr(dK), _ptr(dV), _ptr(row_ptr), _ptr(col_idx), _ptr(col_ptr), _ptr(row_idx), B, H, S,
                                D, blk, float(scale), int(bool(causal_diag)), _ptr(delta), _stream(stream)),

@@ -29,6 +29,7 @@ struct AttnBwdArgs {
   const void* O;         // [B*H*S, D]   (delta pass)
   const float* lse;      // [B*H*S] natural log
   float* delta;          // [B*H*S] written by the delta pass, read by the others
+  float* nlse2;          // [B*H*S] -LSE * log2(e), written by the delta pass (exponent offset in log2 units)
   void* dQ;              // [B*H*S, D]
   void* dK;
   void* dV;
@@ -44,11 +45,14 @@ struct AttnBwdArgs {
   uint64_t timeout_ns;
 };
 
-// Delta_i = dO_i . O_i in fp32: 8 elements (16 bytes) per thread, D / 8 threads per row, grid-stride.
+// Delta_i = dO_i . O_i in fp32 (8 elements, 16 bytes, per thread; D / 8 threads per row; grid-stride), and the
+// row's exponent offset -LSE_i * log2(e) that the passes below add to scale * log2(e) * S.
 template <bool kF16, int kD>
 __global__ void __launch_bounds__(256) bsattn_bwd_delta_kernel(const uint16_t* __restrict__ dO,
                                                                const uint16_t* __restrict__ O,
-                                                               float* __restrict__ delta, int64_t rows) {
+                                                               const float* __restrict__ lse,
+                                                               float* __restrict__ delta,
+                                                               float* __restrict__ nlse2, int64_t rows) {
   constexpr int kTpr = kD / 8;  // threads per row: 16 (D = 128) or 8 (D = 64), a power of two
   const int64_t total = rows * kTpr;
   for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i - (threadIdx.x & 31) < total;
@@ -76,7 +80,10 @@ __global__ void __launch_bounds__(256) bsattn_bwd_delta_kernel(const uint16_t* _
     }
 #pragma unroll
     for (int o = kTpr / 2; o > 0; o >>= 1) acc += __shfl_xor_sync(0xFFFFFFFFu, acc, o);
-    if (i < total && (i % kTpr) == 0) delta[i / kTpr] = acc;
+    if (i < total && (i % kTpr) == 0) {
+      delta[i / kTpr] = acc;
+      nlse2[i / kTpr] = -lse[i / kTpr] * 1.4426950408889634f;
+    }
   }
 }
 
@@ -164,9 +171,79 @@ __device__ __forceinline__ void zero_row_half(int x, uint16_t* row_out) {
   for (int cc = 0; cc < kD / 16; ++cc) reinterpret_cast<uint4*>(row_out + x * (kD / 2))[cc] = z;
 }
 
+// Packed fp32x2 multiply (FMA pipe, both halves in one instruction) and 2^x of a pair.
+__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t f2_ex2(uint64_t t) {
+  float a, b;
+  f2_unpack(t, a, b);
+  return f2_pack(ex2_approx(a), ex2_approx(b));
+}
+
+// kN columns of a score tile, for one TMEM lane: P = 2^(S * c + off), dS = P * (dP - delta), packed to pairs in
+// place (sv[0..kN/2) = P, dv[0..kN/2) = dS). Per-column offsets come from `col_off` / `col_dlt` (shared
+// memory, kColVec) or per-row scalars; kMask zeroes the elements with `masked(i)` (causal diagonal block).
+template <bool kF16, bool kColVec, bool kMask, int kN, typename MaskFn>
+__device__ __forceinline__ void bwd_half_elementwise(uint32_t (&sv)[kN], uint32_t (&dv)[kN], float c, float row_off,
+                                                     float row_dlt, const float* col_off, const float* col_dlt,
+                                                     MaskFn masked) {
+  const uint64_t c2 = f2_pack(c, c);
+#pragma unroll
+  for (int i = 0; i < kN; i += 4) {
+    float o0, o1, o2, o3, d0, d1, d2, d3;
+    if (kColVec) {
+      const float4 ov = *reinterpret_cast<const float4*>(col_off + i);
+      const float4 dl = *reinterpret_cast<const float4*>(col_dlt + i);
+      o0 = ov.x; o1 = ov.y; o2 = ov.z; o3 = ov.w;
+      d0 = dl.x; d1 = dl.y; d2 = dl.z; d3 = dl.w;
+    } else {
+      o0 = o1 = o2 = o3 = row_off;
+      d0 = d1 = d2 = d3 = row_dlt;
+    }
+    const uint64_t p01 = f2_ex2(f2_fma(f2_pack(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), c2, f2_pack(o0, o1)));
+    const uint64_t p23 =
+        f2_ex2(f2_fma(f2_pack(__uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3])), c2, f2_pack(o2, o3)));
+    float p0, p1, p2, p3;
+    f2_unpack(p01, p0, p1);
+    f2_unpack(p23, p2, p3);
+    if (kMask) {
+      if (masked(i)) p0 = 0.0f;
+      if (masked(i + 1)) p1 = 0.0f;
+      if (masked(i + 2)) p2 = 0.0f;
+      if (masked(i + 3)) p3 = 0.0f;
+    }
+    const uint64_t g01 = f2_mul(f2_pack(p0, p1),
+                                f2_add(f2_pack(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])), f2_pack(-d0, -d1)));
+    const uint64_t g23 = f2_mul(
+        f2_pack(p2, p3), f2_add(f2_pack(__uint_as_float(dv[i + 2]), __uint_as_float(dv[i + 3])), f2_pack(-d2, -d3)));
+    float g0, g1, g2, g3;
+    f2_unpack(g01, g0, g1);
+    f2_unpack(g23, g2, g3);
+    sv[i >> 1] = pack2<kF16>(p0, p1);
+    sv[(i >> 1) + 1] = pack2<kF16>(p2, p3);
+    dv[i >> 1] = pack2<kF16>(g0, g1);
+    dv[(i >> 1) + 1] = pack2<kF16>(g2, g3);
+  }
+}
+
+template <int kD>
+__device__ __forceinline__ void mma_kmajor_n64(uint32_t d, uint32_t A, uint32_t B, uint32_t idesc) {
+#pragma unroll
+  for (int k = 0; k < kD / 16; ++k) {
+    const uint32_t off = (k >> 2) * kAttnChunk + (k & 3) * 32;
+    ptx::mma_f16_ss(d, ptx::smem_desc(A + off, 16, 1024), ptx::smem_desc(B + off, 16, 1024), idesc, k != 0);
+  }
+}
+
 // ------------------------------------------------------------------------------------------------ dQ pass
 // Item = (b,h) pair and query block i; streams the K_j / V_j tiles of row i's key blocks through a ring.
-// TMEM: S [0,128), dP [128,256), dQ accumulator [256, 256 + D), dS (packed pairs) [384, 448).
+// TMEM: S [0,128), dP [128,256), dQ accumulator [256, 256 + D), dS (packed pairs) [384, 448). The key positions of
+// a block are handled in two halves of 64 (warpgroup x takes half x): the MMA thread issues S and dP per half
+// (N = 64), and dQ += dS K for half x as soon as warpgroup x has written it, followed by the next block's half x
+// scores, so the tensor pipe works on one half while the other half's elementwise step runs.
 template <bool kF16, int kD>
 struct BwdDqShape {
   static constexpr int kTile = kAttnBlk * kD * 2;
@@ -184,8 +261,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   constexpr int kTile = Sh::kTile;
   constexpr int kSlots = Sh::kSlots;
   constexpr uint32_t kFmt = kF16 ? 0u : 1u;
-  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 128, kFmt, kFmt, 0, 0);   // S, dP: K = D, both K-major
-  constexpr uint32_t IDESC_DQ = ptx::instr_desc(128, kD, kFmt, kFmt, 0, 1);   // dQ += dS K: K MN-major
+  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 64, kFmt, kFmt, 0, 0);   // S, dP halves: N = 64 keys
+  constexpr uint32_t IDESC_DQ = ptx::instr_desc(128, kD, kFmt, kFmt, 0, 1);  // dQ += dS K: K MN-major
   constexpr uint32_t T_S = 0, T_DP = 128, T_DQ = 256, T_DS = 384;
 
   extern __shared__ uint8_t smem_raw[];
@@ -198,10 +275,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* qd_empty = bars + 1;
   uint64_t* kv_full = bars + 2;
   uint64_t* kv_empty = kv_full + kSlots;
-  uint64_t* sdp_full = kv_empty + kSlots;
-  uint64_t* ds_full = sdp_full + 1;
-  uint64_t* dq_done = ds_full + 1;
-  uint64_t* drain = dq_done + 1;
+  uint64_t* sdp_full = kv_empty + kSlots;  // [2] per half
+  uint64_t* ds_full = sdp_full + 2;        // [2] per half, 4 warp arrivals
+  uint64_t* dq_done = ds_full + 2;
+  uint64_t* dq_empty = dq_done + 1;        // 8 warp arrivals: the accumulator has been read out
+  uint64_t* drain = dq_empty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -214,9 +292,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ptx::mbar_init(ptx::smem_u32(&kv_full[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&kv_empty[s]), 1);
     }
-    ptx::mbar_init(ptx::smem_u32(sdp_full), 1);
-    ptx::mbar_init(ptx::smem_u32(ds_full), 8);
+    for (int x = 0; x < 2; ++x) {
+      ptx::mbar_init(ptx::smem_u32(&sdp_full[x]), 1);
+      ptx::mbar_init(ptx::smem_u32(&ds_full[x]), 4);
+    }
     ptx::mbar_init(ptx::smem_u32(dq_done), 1);
+    ptx::mbar_init(ptx::smem_u32(dq_empty), 8);
     ptx::mbar_init(ptx::smem_u32(drain), 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -301,7 +382,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (one thread)
     if (lane == 0) {
-      uint32_t qd_phase = 0, slot = 0, slot_phase = 0, ds_cnt = 0;
+      uint32_t qd_phase = 0, slot = 0, slot_phase = 0, items_done = 0;
+      uint32_t ds_cnt[2] = {0, 0};
       bool ok = true;
       const uint32_t kv0 = ptx::smem_u32(sKV), q0 = ptx::smem_u32(sQ), do0 = ptx::smem_u32(sdO);
       auto take = [&](uint32_t site) -> uint32_t {
@@ -310,14 +392,21 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
         return s;
       };
-      // D[tmem] = A B^T over K = D: both operands K-major 128-row tiles in 64-column chunks
-      auto mma_kmajor = [&](uint32_t d, uint32_t A, uint32_t B) {
+      // S_x = Q K_x^T and dP_x = dO V_x^T for keys [64x, 64x + 64) of the block
+      auto issue_sdp = [&](int x, uint32_t sk, uint32_t sv) {
+        const uint32_t koff = kv0 + sk * kTile + x * 8192, voff = kv0 + sv * kTile + x * 8192;
+        mma_kmajor_n64<kD>(tmem_base + T_S + 64 * x, q0, koff, IDESC_S);
+        mma_kmajor_n64<kD>(tmem_base + T_DP + 64 * x, do0, voff, IDESC_S);
+        ptx::mma_commit(ptx::smem_u32(&sdp_full[x]));
+      };
+      // dQ += dS_x K_x: K steps over keys [64x + 16k, 64x + 16k + 16), dS_x packed at T_DS + 32x
+      auto issue_dq = [&](int x, uint32_t sk, bool first) {
+        const uint32_t kA = kv0 + sk * kTile;
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k) {
-          const uint32_t off = (k >> 2) * kAttnChunk + (k & 3) * 32;
-          ptx::mma_f16_ss(tmem_base + d, ptx::smem_desc(A + off, 16, 1024), ptx::smem_desc(B + off, 16, 1024),
-                          IDESC_S, k != 0);
-        }
+        for (int k = 0; k < 4; ++k)
+          ptx::mma_f16_ts(tmem_base + T_DQ, tmem_base + T_DS + 32 * x + 8 * k,
+                          ptx::smem_desc(kA + (4 * x + k) * 2048, kAttnChunk, 1024), IDESC_DQ,
+                          (first && k == 0) ? 0u : 1u);
       };
       for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
         int bh, qb, j0, n;
@@ -326,30 +415,45 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ok = wait_bounded(ptx::smem_u32(qd_full), qd_phase, ctl, 10);
         if (!ok) break;
         qd_phase ^= 1;
-        for (int j = 0; j < n && ok; ++j) {
-          const uint32_t sk = take(11);
-          if (sk == 0xFFFFFFFFu) { ok = false; break; }
-          const uint32_t sv = take(12);
-          if (sv == 0xFFFFFFFFu) { ok = false; break; }
-          ptx::tc_fence_after();
-          mma_kmajor(T_S, q0, kv0 + sk * kTile);    // S = Q K^T
-          mma_kmajor(T_DP, do0, kv0 + sv * kTile);  // dP = dO V^T
-          ptx::mma_commit(ptx::smem_u32(&kv_empty[sv]));
-          ptx::mma_commit(ptx::smem_u32(sdp_full));
-          ok = wait_bounded(ptx::smem_u32(ds_full), ds_cnt & 1, ctl, 13);  // dS of block j in TMEM
+        uint32_t sk = take(11), sv = 0xFFFFFFFFu;
+        if (sk != 0xFFFFFFFFu) sv = take(12);
+        if (sv == 0xFFFFFFFFu) { ok = false; break; }
+        ptx::tc_fence_after();
+        issue_sdp(0, sk, sv);
+        issue_sdp(1, sk, sv);
+        if (items_done > 0) {  // the previous item's dQ has been read out of TMEM
+          ok = wait_bounded(ptx::smem_u32(dq_empty), (items_done - 1) & 1, ctl, 16);
           if (!ok) break;
-          ++ds_cnt;
+        }
+        for (int j = 0; j < n && ok; ++j) {
+          ok = wait_bounded(ptx::smem_u32(&ds_full[0]), ds_cnt[0] & 1, ctl, 13);
+          if (!ok) break;
+          ++ds_cnt[0];
           ptx::tc_fence_after();
-          const uint32_t kA = kv0 + sk * kTile;
-#pragma unroll
-          for (int k = 0; k < 8; ++k)  // dQ += dS K: K step k = kv rows [16k, 16k + 16), dS columns [8k, 8k + 8)
-            ptx::mma_f16_ts(tmem_base + T_DQ, tmem_base + T_DS + 8 * k,
-                            ptx::smem_desc(kA + k * 2048, kAttnChunk, 1024), IDESC_DQ, (j == 0 && k == 0) ? 0u : 1u);
+          issue_dq(0, sk, j == 0);
+          uint32_t nk = 0xFFFFFFFFu, nv = 0xFFFFFFFFu;
+          if (j + 1 < n) {
+            nk = take(11);
+            if (nk != 0xFFFFFFFFu) nv = take(12);
+            if (nv == 0xFFFFFFFFu) { ok = false; break; }
+            ptx::tc_fence_after();
+            issue_sdp(0, nk, nv);
+          }
+          ok = wait_bounded(ptx::smem_u32(&ds_full[1]), ds_cnt[1] & 1, ctl, 14);
+          if (!ok) break;
+          ++ds_cnt[1];
+          ptx::tc_fence_after();
+          issue_dq(1, sk, false);
           ptx::mma_commit(ptx::smem_u32(&kv_empty[sk]));
+          ptx::mma_commit(ptx::smem_u32(&kv_empty[sv]));
+          if (j + 1 < n) issue_sdp(1, nk, nv);
+          sk = nk;
+          sv = nv;
         }
         if (!ok) break;
         ptx::mma_commit(ptx::smem_u32(dq_done));
         ptx::mma_commit(ptx::smem_u32(qd_empty));
+        ++items_done;
       }
       ptx::mma_commit(ptx::smem_u32(drain));
       WaitCtl dctl = ctl;
@@ -361,7 +465,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ dS = P (dP - Delta), dQ out
     ptx::setmaxnreg_inc<kAttnRegsHigh>();
-    const int x = (warp - 4) >> 2;  // column half
+    const int x = (warp - 4) >> 2;  // key half
     const int q = warp & 3;
     const int r = 32 * q + lane;    // query row within the block == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
@@ -377,37 +481,33 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         zero_row_half<kD>(x, dq_row);
         continue;
       }
-      const float lse2 = __ldg(&a.lse[grow]) * 1.4426950408889634f;
+      const float off = __ldg(&a.nlse2[grow]);
       const float dlt = __ldg(&a.delta[grow]);
       for (int j = 0; j < n; ++j) {
         const int kb = __ldg(&a.col_idx[j0 + j]);
-        const bool diag = a.causal_diag && kb == qb;
-        ok = warp_wait_bounded(ptx::smem_u32(sdp_full), sdp_cnt & 1, ctl, 20);
+        ok = warp_wait_bounded(ptx::smem_u32(&sdp_full[x]), sdp_cnt & 1, ctl, 20);
         if (!ok) break;
         ++sdp_cnt;
         ptx::tc_fence_after();
         uint32_t sv[64], dv[64];
-        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_S + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_S + 64 * x + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_DP + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
-        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_DP + 64 * x + 32, *reinterpret_cast<uint32_t(*)[32]>(&dv[32]));
+        const uint32_t ts = tmem_base + lane_off + T_S + 64 * x, tp = tmem_base + lane_off + T_DP + 64 * x;
+        ptx::tmem_ld_32x32b_x32(ts, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        ptx::tmem_ld_32x32b_x32(ts + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        ptx::tmem_ld_32x32b_x32(tp, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
+        ptx::tmem_ld_32x32b_x32(tp + 32, *reinterpret_cast<uint32_t(*)[32]>(&dv[32]));
         ptx::tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          const int col = 64 * x + i;
-          float p0 = ex2_approx(fmaf(__uint_as_float(sv[i]), c, -lse2));
-          float p1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), c, -lse2));
-          if (diag && col > r) p0 = 0.0f;
-          if (diag && col + 1 > r) p1 = 0.0f;
-          const float d0 = p0 * (__uint_as_float(dv[i]) - dlt);
-          const float d1 = p1 * (__uint_as_float(dv[i + 1]) - dlt);
-          sv[i >> 1] = pack2<kF16>(d0, d1);
+        if (a.causal_diag && kb == qb) {  // key position 64x + i above query row r
+          bwd_half_elementwise<kF16, false, true, 64>(sv, dv, c, off, dlt, nullptr, nullptr,
+                                                  [&](int i) { return 64 * x + i > r; });
+        } else {
+          bwd_half_elementwise<kF16, false, false, 64>(sv, dv, c, off, dlt, nullptr, nullptr,
+                                                      [](int) { return false; });
         }
-        ptx::tmem_st_32x32b_x32(tmem_base + lane_off + T_DS + 32 * x, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        ptx::tmem_st_32x32b_x32(tmem_base + lane_off + T_DS + 32 * x, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(ds_full));
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&ds_full[x]));
       }
       if (!ok) break;
       ok = warp_wait_bounded<false, 256>(ptx::smem_u32(dq_done), dq_cnt & 1, ctl, 22);
@@ -416,6 +516,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ptx::tc_fence_after();
       write_acc_half<kF16, kD>(tmem_base + lane_off + T_DQ, x, dq_row, a.scale);
       ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(dq_empty));
     }
   }
 
@@ -426,14 +528,15 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 }
 
 // ------------------------------------------------------------------------------------------------ dK/dV pass
-// Item = (b,h) pair and key block j; streams Q_i, dO_i (+ LSE_i, Delta_i) of column j's query blocks.
-// TMEM: S^T [0,128) -> packed P^T in [0,32) and [64,96); dP^T [128,256) -> packed dS^T in [128,160) and
-// [192,224); dV accumulator [256, 256 + D), dK accumulator [256 + D, 256 + 2D).
+// Item = (b,h) pair and key block j; streams Q_i, dO_i (+ -LSE_i log2(e), Delta_i) of column j's query blocks.
+// TMEM: S^T [0,128) -> packed P^T of half x at [64x, 64x + 32); dP^T [128,256) -> packed dS^T of half x at
+// [128 + 64x, ...); dV accumulator [256, 256 + D), dK accumulator [256 + D, 256 + 2D). Query positions are handled
+// in two halves of 64 (warpgroup x takes half x), pipelined like the dQ pass.
 template <bool kF16, int kD>
 struct BwdDkdvShape {
   static constexpr int kTile = kAttnBlk * kD * 2;
   static constexpr int kChunks = kD / 64;
-  static constexpr int kSlotBytes = 2 * kTile + 1024;  // Q, dO, LSE[128], Delta[128]
+  static constexpr int kSlotBytes = 2 * kTile + 1024;  // Q, dO, -LSE*log2(e) [128], Delta [128]
   static constexpr int kSlots = kD == 128 ? 2 : 4;
   static constexpr int kSmemBytes = 1024 + 2 * kTile + kSlots * kSlotBytes + 512;
 };
@@ -448,7 +551,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   constexpr int kSlots = Sh::kSlots;
   constexpr int kSlotBytes = Sh::kSlotBytes;
   constexpr uint32_t kFmt = kF16 ? 0u : 1u;
-  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 128, kFmt, kFmt, 0, 0);   // S^T, dP^T: K = D, K-major
+  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 64, kFmt, kFmt, 0, 0);    // S^T, dP^T halves: N = 64 queries
   constexpr uint32_t IDESC_ACC = ptx::instr_desc(128, kD, kFmt, kFmt, 0, 1);  // dV, dK: B (dO, Q) MN-major
   constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + kD;
 
@@ -456,16 +559,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
   uint8_t* sV = sK + kTile;
-  uint8_t* sQD = sV + kTile;  // [kSlots] x (Q tile, dO tile, LSE, Delta)
+  uint8_t* sQD = sV + kTile;  // [kSlots] x (Q tile, dO tile, -LSE*log2(e), Delta)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sQD + kSlots * kSlotBytes);
   uint64_t* kv_full = bars + 0;
   uint64_t* kv_empty = bars + 1;
   uint64_t* qd_full = bars + 2;
   uint64_t* qd_empty = qd_full + kSlots;
-  uint64_t* sdp_full = qd_empty + kSlots;
-  uint64_t* p_full = sdp_full + 1;
-  uint64_t* acc_done = p_full + 1;
-  uint64_t* drain = acc_done + 1;
+  uint64_t* sdp_full = qd_empty + kSlots;  // [2] per half
+  uint64_t* p_full = sdp_full + 2;         // [2] per half, 4 warp arrivals
+  uint64_t* acc_done = p_full + 2;
+  uint64_t* acc_empty = acc_done + 1;      // 8 warp arrivals: dK / dV read out of TMEM
+  uint64_t* drain = acc_empty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
 
@@ -478,9 +582,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ptx::mbar_init(ptx::smem_u32(&qd_full[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&qd_empty[s]), 1);
     }
-    ptx::mbar_init(ptx::smem_u32(sdp_full), 1);
-    ptx::mbar_init(ptx::smem_u32(p_full), 8);
+    for (int x = 0; x < 2; ++x) {
+      ptx::mbar_init(ptx::smem_u32(&sdp_full[x]), 1);
+      ptx::mbar_init(ptx::smem_u32(&p_full[x]), 4);
+    }
     ptx::mbar_init(ptx::smem_u32(acc_done), 1);
+    ptx::mbar_init(ptx::smem_u32(acc_empty), 8);
     ptx::mbar_init(ptx::smem_u32(drain), 1);
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -550,10 +657,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           const int qrow = bh * a.S + qb * kAttnBlk;
           if (qb < a.nqb) {
             ptx::mbar_arrive_expect_tx(fb, 2 * kTile + 1024);
-            ptx::bulk_load_1d(dst + 2 * kTile, a.lse + qrow, 512, fb);
+            ptx::bulk_load_1d(dst + 2 * kTile, a.nlse2 + qrow, 512, fb);
             ptx::bulk_load_1d(dst + 2 * kTile + 512, a.delta + qrow, 512, fb);
           } else {
-            ptx::mbar_arrive_expect_tx(fb, 2 * kTile);  // zero-filled tiles; LSE / Delta left unread (P = 0)
+            ptx::mbar_arrive_expect_tx(fb, 2 * kTile);  // zero-filled tiles; offsets left unread (P = 0)
           }
 #pragma unroll
           for (int c = 0; c < Sh::kChunks; ++c) {
@@ -576,15 +683,34 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (one thread)
     if (lane == 0) {
-      uint32_t kv_phase = 0, slot = 0, slot_phase = 0, p_cnt = 0;
+      uint32_t kv_phase = 0, slot = 0, slot_phase = 0, items_done = 0;
+      uint32_t p_cnt[2] = {0, 0};
       bool ok = true;
       const uint32_t qd0 = ptx::smem_u32(sQD), k0 = ptx::smem_u32(sK), v0 = ptx::smem_u32(sV);
-      auto mma_kmajor = [&](uint32_t d, uint32_t A, uint32_t B) {
+      auto take = [&](uint32_t site) -> uint32_t {
+        if (!wait_bounded(ptx::smem_u32(&qd_full[slot]), slot_phase, ctl, site)) return 0xFFFFFFFFu;
+        const uint32_t s = slot;
+        if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
+        return s;
+      };
+      // S^T_x = K Q_x^T and dP^T_x = V dO_x^T for query positions [64x, 64x + 64) of the slot's block
+      auto issue_sdp = [&](int x, uint32_t sl) {
+        const uint32_t qA = qd0 + sl * kSlotBytes + x * 8192, dA = qA + kTile;
+        mma_kmajor_n64<kD>(tmem_base + T_S + 64 * x, k0, qA, IDESC_S);
+        mma_kmajor_n64<kD>(tmem_base + T_DP + 64 * x, v0, dA, IDESC_S);
+        ptx::mma_commit(ptx::smem_u32(&sdp_full[x]));
+      };
+      // dV += P^T_x dO_x, dK += dS^T_x Q_x: K steps over query rows [64x + 16k, ...), packed columns 64x + 8k
+      auto issue_acc = [&](int x, uint32_t sl, bool first) {
+        const uint32_t qA = qd0 + sl * kSlotBytes, dA = qA + kTile;
 #pragma unroll
-        for (int k = 0; k < kD / 16; ++k) {
-          const uint32_t off = (k >> 2) * kAttnChunk + (k & 3) * 32;
-          ptx::mma_f16_ss(tmem_base + d, ptx::smem_desc(A + off, 16, 1024), ptx::smem_desc(B + off, 16, 1024),
-                          IDESC_S, k != 0);
+        for (int k = 0; k < 4; ++k) {
+          const uint32_t acc = (first && k == 0) ? 0u : 1u;
+          const uint32_t pc = 64 * x + 8 * k;
+          ptx::mma_f16_ts(tmem_base + T_DV, tmem_base + T_S + pc,
+                          ptx::smem_desc(dA + (4 * x + k) * 2048, kAttnChunk, 1024), IDESC_ACC, acc);
+          ptx::mma_f16_ts(tmem_base + T_DK, tmem_base + T_DP + pc,
+                          ptx::smem_desc(qA + (4 * x + k) * 2048, kAttnChunk, 1024), IDESC_ACC, acc);
         }
       };
       for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
@@ -594,33 +720,41 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ok = wait_bounded(ptx::smem_u32(kv_full), kv_phase, ctl, 10);
         if (!ok) break;
         kv_phase ^= 1;
+        uint32_t cur = take(11);
+        if (cur == 0xFFFFFFFFu) { ok = false; break; }
+        ptx::tc_fence_after();
+        issue_sdp(0, cur);
+        issue_sdp(1, cur);
+        if (items_done > 0) {  // the previous item's dK / dV have been read out of TMEM
+          ok = wait_bounded(ptx::smem_u32(acc_empty), (items_done - 1) & 1, ctl, 16);
+          if (!ok) break;
+        }
         for (int t = 0; t < n && ok; ++t) {
-          ok = wait_bounded(ptx::smem_u32(&qd_full[slot]), slot_phase, ctl, 11);
+          ok = wait_bounded(ptx::smem_u32(&p_full[0]), p_cnt[0] & 1, ctl, 12);
           if (!ok) break;
+          ++p_cnt[0];
           ptx::tc_fence_after();
-          const uint32_t qA = qd0 + slot * kSlotBytes, dA = qA + kTile;
-          mma_kmajor(T_S, k0, qA);   // S^T = K Q^T
-          mma_kmajor(T_DP, v0, dA);  // dP^T = V dO^T
-          ptx::mma_commit(ptx::smem_u32(sdp_full));
-          ok = wait_bounded(ptx::smem_u32(p_full), p_cnt & 1, ctl, 12);  // P^T, dS^T in TMEM
-          if (!ok) break;
-          ++p_cnt;
-          ptx::tc_fence_after();
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {  // K step k = query rows [16k, 16k + 16): packed columns 8k (+32 for k >= 4)
-            const uint32_t acc = (t == 0 && k == 0) ? 0u : 1u;
-            const uint32_t pc = 8 * k + (k >= 4 ? 32 : 0);
-            ptx::mma_f16_ts(tmem_base + T_DV, tmem_base + T_S + pc,
-                            ptx::smem_desc(dA + k * 2048, kAttnChunk, 1024), IDESC_ACC, acc);   // dV += P^T dO
-            ptx::mma_f16_ts(tmem_base + T_DK, tmem_base + T_DP + pc,
-                            ptx::smem_desc(qA + k * 2048, kAttnChunk, 1024), IDESC_ACC, acc);   // dK += dS^T Q
+          issue_acc(0, cur, t == 0);
+          uint32_t nxt = 0xFFFFFFFFu;
+          if (t + 1 < n) {
+            nxt = take(11);
+            if (nxt == 0xFFFFFFFFu) { ok = false; break; }
+            ptx::tc_fence_after();
+            issue_sdp(0, nxt);
           }
-          ptx::mma_commit(ptx::smem_u32(&qd_empty[slot]));
-          if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
+          ok = wait_bounded(ptx::smem_u32(&p_full[1]), p_cnt[1] & 1, ctl, 13);
+          if (!ok) break;
+          ++p_cnt[1];
+          ptx::tc_fence_after();
+          issue_acc(1, cur, false);
+          ptx::mma_commit(ptx::smem_u32(&qd_empty[cur]));
+          if (t + 1 < n) issue_sdp(1, nxt);
+          cur = nxt;
         }
         if (!ok) break;
         ptx::mma_commit(ptx::smem_u32(acc_done));
         ptx::mma_commit(ptx::smem_u32(kv_empty));
+        ++items_done;
       }
       ptx::mma_commit(ptx::smem_u32(drain));
       WaitCtl dctl = ctl;
@@ -632,14 +766,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ P^T, dS^T, dK / dV out
     ptx::setmaxnreg_inc<kAttnRegsHigh>();
-    const int x = (warp - 4) >> 2;  // column half (query positions [64x, 64x + 64))
+    const int x = (warp - 4) >> 2;  // query half (positions [64x, 64x + 64))
     const int q = warp & 3;
     const int r = 32 * q + lane;    // key row within the block == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
     const float c = a.scale_log2;
     uint32_t sdp_cnt = 0, acc_cnt = 0, slot = 0, slot_phase = 0;
     bool ok = true;
-    const uint8_t* qd_base = sQD;
     for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
       int bh, kb, i0, n;
       item_of(item, bh, kb, i0, n);
@@ -654,43 +787,41 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int t = 0; t < n; ++t) {
         const int qb = __ldg(&a.row_idx[i0 + t]);
         const bool valid = qb >= 0 && qb < a.nqb;
-        const bool diag = a.causal_diag && qb == kb;
-        ok = warp_wait_bounded(ptx::smem_u32(&qd_full[slot]), slot_phase, ctl, 19);  // LSE / Delta landed
-        if (ok) ok = warp_wait_bounded(ptx::smem_u32(sdp_full), sdp_cnt & 1, ctl, 20);
+        ok = warp_wait_bounded(ptx::smem_u32(&qd_full[slot]), slot_phase, ctl, 19);  // offsets landed
+        if (ok) ok = warp_wait_bounded(ptx::smem_u32(&sdp_full[x]), sdp_cnt & 1, ctl, 20);
         if (!ok) break;
         ++sdp_cnt;
         ptx::tc_fence_after();
-        const float* lse_s = reinterpret_cast<const float*>(qd_base + slot * kSlotBytes + 2 * kTile);
-        const float* dlt_s = lse_s + 128;
-        uint32_t sv[64], dv[64];
-        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_S + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_S + 64 * x + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_DP + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
-        ptx::tmem_ld_32x32b_x32(tmem_base + lane_off + T_DP + 64 * x + 32, *reinterpret_cast<uint32_t(*)[32]>(&dv[32]));
-        ptx::tmem_wait_ld();
+        const float* off_s = reinterpret_cast<const float*>(sQD + slot * kSlotBytes + 2 * kTile) + 64 * x;
+        const float* dlt_s = off_s + 128;
+        const uint32_t ts = tmem_base + lane_off + T_S + 64 * x, tp = tmem_base + lane_off + T_DP + 64 * x;
+        const bool diag = a.causal_diag && qb == kb;
+        // Two chunks of 32 query positions; chunk cc's packed P^T / dS^T (16 columns each) land at ts / tp + 16cc,
+        // inside the columns [0, 32) this warp has already read, never over chunk 1's unread scores.
+#pragma unroll 1
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t sv[32], dv[32];
+          ptx::tmem_ld_32x32b_x32(ts + 32 * cc, sv);
+          ptx::tmem_ld_32x32b_x32(tp + 32 * cc, dv);
+          ptx::tmem_wait_ld();
+          const int col0 = 64 * x + 32 * cc;  // query position of column 0 of the chunk
+          if (!valid) {
 #pragma unroll
-        for (int i = 0; i < 64; i += 2) {
-          const int col = 64 * x + i;  // query position within the block
-          float p0 = 0.0f, p1 = 0.0f, d0 = 0.0f, d1 = 0.0f;
-          if (valid) {
-            p0 = ex2_approx(fmaf(__uint_as_float(sv[i]), c, -lse_s[col] * 1.4426950408889634f));
-            p1 = ex2_approx(fmaf(__uint_as_float(sv[i + 1]), c, -lse_s[col + 1] * 1.4426950408889634f));
-            if (diag && r > col) p0 = 0.0f;  // key position above the query position
-            if (diag && r > col + 1) p1 = 0.0f;
-            d0 = p0 * (__uint_as_float(dv[i]) - dlt_s[col]);
-            d1 = p1 * (__uint_as_float(dv[i + 1]) - dlt_s[col + 1]);
+            for (int i = 0; i < 16; ++i) sv[i] = dv[i] = 0u;
+          } else if (diag) {  // key row r above query position col0 + i
+            bwd_half_elementwise<kF16, true, true, 32>(sv, dv, c, 0.0f, 0.0f, off_s + 32 * cc, dlt_s + 32 * cc,
+                                                       [&](int i) { return r > col0 + i; });
+          } else {
+            bwd_half_elementwise<kF16, true, false, 32>(sv, dv, c, 0.0f, 0.0f, off_s + 32 * cc, dlt_s + 32 * cc,
+                                                        [](int) { return false; });
           }
-          sv[i >> 1] = pack2<kF16>(p0, p1);
-          dv[i >> 1] = pack2<kF16>(d0, d1);
+          ptx::tmem_st_32x32b_x16(ts + 16 * cc, sv);
+          ptx::tmem_st_32x32b_x16(tp + 16 * cc, dv);
         }
-        // Packed P^T / dS^T of this warpgroup's 64 query columns go to the first 32 of the columns it read itself
-        // ([64x, 64x + 32) of each buffer), so no other warp's pending reads are overwritten.
-        ptx::tmem_st_32x32b_x32(tmem_base + lane_off + T_S + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        ptx::tmem_st_32x32b_x32(tmem_base + lane_off + T_DP + 64 * x, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(p_full));
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&p_full[x]));
         if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
       }
       if (!ok) break;
@@ -701,6 +832,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       write_acc_half<kF16, kD>(tmem_base + lane_off + T_DV, x, dv_row, 1.0f);
       write_acc_half<kF16, kD>(tmem_base + lane_off + T_DK, x, dk_row, a.scale);
       ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(acc_empty));
     }
   }
 

@@ -1544,6 +1544,7 @@ int bsk_bsattn_bwd(int dtype, const void* dO, const void* Q, const void* K, cons
   a.O = O;
   a.lse = lse;
   a.delta = delta;
+  a.nlse2 = delta + rows;
   a.dQ = dQ;
   a.dK = dK;
   a.dV = dV;
@@ -1566,7 +1567,7 @@ int bsk_bsattn_bwd(int dtype, const void* dO, const void* Q, const void* K, cons
   const int dgrid = st->sm_count * 8;
 #define BSK_BWD(F16, DD)                                                                                            \
   do {                                                                                                              \
-    bsattn_bwd_delta_kernel<F16, DD><<<dgrid, 256, 0, s>>>(dO16, O16, delta, (int64_t)rows);                        \
+    bsattn_bwd_delta_kernel<F16, DD><<<dgrid, 256, 0, s>>>(dO16, O16, lse, delta, delta + rows, (int64_t)rows);     \
     bsattn_bwd_dkdv_kernel<F16, DD><<<grid, kAttnThreads, BwdDkdvShape<F16, DD>::kSmemBytes, s>>>(tq, tk, tv, tdo, a); \
     bsattn_bwd_dq_kernel<F16, DD><<<grid, kAttnThreads, BwdDqShape<F16, DD>::kSmemBytes, s>>>(tq, tk, tv, tdo, a);     \
   } while (0)
@@ -1655,7 +1656,7 @@ void launch_attention_backward(const void* grad_out, const void* Q, const void* 
   cudaError_t e = cudaSuccess;
   const size_t rows = (size_t)pairs * S;
   float* lse = static_cast<float*>(ss.get(rows * 4, &e));
-  float* delta = static_cast<float*>(ss.get(rows * 4, &e));
+  float* delta = static_cast<float*>(ss.get(rows * 8, &e));  // Delta and -LSE log2(e)
   void* o_tmp = ss.get(rows * D * 2, &e);
   int* col_ptr = static_cast<int*>(ss.get(((size_t)pairs * nqb + 1) * 4, &e));
   int* row_idx = static_cast<int*>(ss.get((size_t)nnz * 4, &e));
