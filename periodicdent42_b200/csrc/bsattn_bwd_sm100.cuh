@@ -23,6 +23,7 @@
 namespace bsk {
 
 constexpr uint32_t kKidBsAttnBwd = 7;
+constexpr uint32_t kBwdSuspendNs = 2000;  // suspend hint of the compute and MMA waits (woken at completion)
 
 struct AttnBwdArgs {
   const void* dO;        // [B*H*S, D]
@@ -335,7 +336,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = true;
       const uint32_t kv0 = ptx::smem_u32(sKV);
       auto push = [&](const CUtensorMap* m, int row) -> bool {
-        if (!wait_bounded<false, 512>(ptx::smem_u32(&kv_empty[slot]), slot_phase ^ 1, ctl, 2)) return false;
+        if (!wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&kv_empty[slot]), slot_phase ^ 1, ctl, 2)) return false;
         const uint32_t fb = ptx::smem_u32(&kv_full[slot]);
         ptx::mbar_arrive_expect_tx(fb, kTile);
 #pragma unroll
@@ -348,7 +349,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         int bh, qb, j0, n;
         item_of(item, bh, qb, j0, n);
         if (n == 0) continue;
-        ok = wait_bounded<false, 512>(ptx::smem_u32(qd_empty), qd_phase ^ 1, ctl, 1);
+        ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(qd_empty), qd_phase ^ 1, ctl, 1);
         if (!ok) break;
         const uint32_t qf = ptx::smem_u32(qd_full);
         ptx::mbar_arrive_expect_tx(qf, 2 * kTile);
@@ -387,7 +388,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = true;
       const uint32_t kv0 = ptx::smem_u32(sKV), q0 = ptx::smem_u32(sQ), do0 = ptx::smem_u32(sdO);
       auto take = [&](uint32_t site) -> uint32_t {
-        if (!wait_bounded(ptx::smem_u32(&kv_full[slot]), slot_phase, ctl, site)) return 0xFFFFFFFFu;
+        if (!wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&kv_full[slot]), slot_phase, ctl, site)) return 0xFFFFFFFFu;
         const uint32_t s = slot;
         if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
         return s;
@@ -426,7 +427,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (!ok) break;
         }
         for (int j = 0; j < n && ok; ++j) {
-          ok = wait_bounded(ptx::smem_u32(&ds_full[0]), ds_cnt[0] & 1, ctl, 13);
+          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&ds_full[0]), ds_cnt[0] & 1, ctl, 13);
           if (!ok) break;
           ++ds_cnt[0];
           ptx::tc_fence_after();
@@ -439,7 +440,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             ptx::tc_fence_after();
             issue_sdp(0, nk, nv);
           }
-          ok = wait_bounded(ptx::smem_u32(&ds_full[1]), ds_cnt[1] & 1, ctl, 14);
+          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&ds_full[1]), ds_cnt[1] & 1, ctl, 14);
           if (!ok) break;
           ++ds_cnt[1];
           ptx::tc_fence_after();
@@ -485,7 +486,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const float dlt = __ldg(&a.delta[grow]);
       for (int j = 0; j < n; ++j) {
         const int kb = __ldg(&a.col_idx[j0 + j]);
-        ok = warp_wait_bounded(ptx::smem_u32(&sdp_full[x]), sdp_cnt & 1, ctl, 20);
+        ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&sdp_full[x]), sdp_cnt & 1, ctl, 20);
         if (!ok) break;
         ++sdp_cnt;
         ptx::tc_fence_after();
@@ -510,7 +511,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&ds_full[x]));
       }
       if (!ok) break;
-      ok = warp_wait_bounded<false, 256>(ptx::smem_u32(dq_done), dq_cnt & 1, ctl, 22);
+      ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(dq_done), dq_cnt & 1, ctl, 22);
       if (!ok) break;
       ++dq_cnt;
       ptx::tc_fence_after();
@@ -636,7 +637,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         int bh, kb, i0, n;
         item_of(item, bh, kb, i0, n);
         if (n == 0) continue;
-        ok = wait_bounded<false, 512>(ptx::smem_u32(kv_empty), kv_phase ^ 1, ctl, 1);
+        ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(kv_empty), kv_phase ^ 1, ctl, 1);
         if (!ok) break;
         const uint32_t kf = ptx::smem_u32(kv_full);
         ptx::mbar_arrive_expect_tx(kf, 2 * kTile);
@@ -650,7 +651,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         kv_phase ^= 1;
         for (int t = 0; t < n && ok; ++t) {
           const int qb = qblock(i0 + t);
-          ok = wait_bounded<false, 512>(ptx::smem_u32(&qd_empty[slot]), slot_phase ^ 1, ctl, 2);
+          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&qd_empty[slot]), slot_phase ^ 1, ctl, 2);
           if (!ok) break;
           const uint32_t fb = ptx::smem_u32(&qd_full[slot]);
           const uint32_t dst = qd0 + slot * kSlotBytes;
@@ -688,7 +689,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       bool ok = true;
       const uint32_t qd0 = ptx::smem_u32(sQD), k0 = ptx::smem_u32(sK), v0 = ptx::smem_u32(sV);
       auto take = [&](uint32_t site) -> uint32_t {
-        if (!wait_bounded(ptx::smem_u32(&qd_full[slot]), slot_phase, ctl, site)) return 0xFFFFFFFFu;
+        if (!wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&qd_full[slot]), slot_phase, ctl, site)) return 0xFFFFFFFFu;
         const uint32_t s = slot;
         if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
         return s;
@@ -730,7 +731,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (!ok) break;
         }
         for (int t = 0; t < n && ok; ++t) {
-          ok = wait_bounded(ptx::smem_u32(&p_full[0]), p_cnt[0] & 1, ctl, 12);
+          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&p_full[0]), p_cnt[0] & 1, ctl, 12);
           if (!ok) break;
           ++p_cnt[0];
           ptx::tc_fence_after();
@@ -742,7 +743,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             ptx::tc_fence_after();
             issue_sdp(0, nxt);
           }
-          ok = wait_bounded(ptx::smem_u32(&p_full[1]), p_cnt[1] & 1, ctl, 13);
+          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&p_full[1]), p_cnt[1] & 1, ctl, 13);
           if (!ok) break;
           ++p_cnt[1];
           ptx::tc_fence_after();
@@ -787,8 +788,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       for (int t = 0; t < n; ++t) {
         const int qb = __ldg(&a.row_idx[i0 + t]);
         const bool valid = qb >= 0 && qb < a.nqb;
-        ok = warp_wait_bounded(ptx::smem_u32(&qd_full[slot]), slot_phase, ctl, 19);  // offsets landed
-        if (ok) ok = warp_wait_bounded(ptx::smem_u32(&sdp_full[x]), sdp_cnt & 1, ctl, 20);
+        ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&qd_full[slot]), slot_phase, ctl, 19);  // offsets
+        if (ok) ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&sdp_full[x]), sdp_cnt & 1, ctl, 20);
         if (!ok) break;
         ++sdp_cnt;
         ptx::tc_fence_after();
@@ -825,7 +826,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
       }
       if (!ok) break;
-      ok = warp_wait_bounded<false, 256>(ptx::smem_u32(acc_done), acc_cnt & 1, ctl, 22);
+      ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(acc_done), acc_cnt & 1, ctl, 22);
       if (!ok) break;
       ++acc_cnt;
       ptx::tc_fence_after();

@@ -74,6 +74,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the thread may sleep inside the instruction until the phase completes or
+// about kSuspendNs have passed, instead of returning at once (no issue slots spent re-polling).
+template <uint32_t kSuspendNs>
+__device__ __forceinline__ bool mbar_try_wait_hint(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "n"(kSuspendNs)
+      : "memory");
+  return ok != 0;
+}
+
 // ---------------------------------------------------------------- proxies / fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -443,6 +458,31 @@ __device__ __forceinline__ bool wait_bounded(uint32_t bar, uint32_t parity, cons
       sleep_ns = sleep_ns * 2 > kMaxSleepNs ? kMaxSleepNs : sleep_ns * 2;
     }
   }
+}
+
+// Bounded wait whose polls suspend in hardware (mbar_try_wait_hint) between checks of the abort flag and the
+// time limit: for roles that share an SM sub-partition with warps doing arithmetic.
+template <uint32_t kSuspendNs>
+__device__ __forceinline__ bool wait_bounded_hint(uint32_t bar, uint32_t parity, const WaitCtl& c, uint32_t site) {
+  if (ptx::mbar_try_wait_hint<kSuspendNs>(bar, parity)) return true;
+  const uint64_t t0 = ptx::globaltimer_ns();
+  while (true) {
+    if (ptx::mbar_try_wait_hint<kSuspendNs>(bar, parity)) return true;
+    if (*c.abort) return false;
+    if (ptx::globaltimer_ns() - t0 > c.timeout_ns) {
+      record_error(c, kErrWaitTimeout, site);
+      return false;
+    }
+  }
+}
+
+template <uint32_t kSuspendNs>
+__device__ __forceinline__ bool warp_wait_bounded_hint(uint32_t bar, uint32_t parity, const WaitCtl& c,
+                                                       uint32_t site) {
+  int ok = 1;
+  if (ptx::lane_id() == 0) ok = wait_bounded_hint<kSuspendNs>(bar, parity, c, site) ? 1 : 0;
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  return ok != 0;
 }
 
 // Warp-collective bounded wait: lane 0 waits, the result is broadcast to the warp.
