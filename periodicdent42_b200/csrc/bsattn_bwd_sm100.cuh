@@ -15,7 +15,9 @@
 //
 // CTA layout (both passes, 384 threads): warp 0 producer (one thread, TMA), warp 1 MMA issuer (one thread),
 // warps 2-3 idle, warps 4-11 two warpgroups of elementwise work; warpgroup x takes columns [64x, 64x + 64) of
-// the 128 x 128 score tiles (each warp its 32-lane quarter of TMEM), and half of D for the output.
+// the 128 x 128 score tiles (each warp its 32-lane quarter of TMEM), and half of D for the output. P is kept in
+// fp32 registers between the P step and the dS step; the tensor-core operands P^T / dS^T are rounded to the
+// input type.
 #pragma once
 
 #include "bsattn_sm100.cuh"
@@ -184,54 +186,8 @@ __device__ __forceinline__ uint64_t f2_ex2(uint64_t t) {
   return f2_pack(ex2_approx(a), ex2_approx(b));
 }
 
-// kN columns of a score tile, for one TMEM lane: P = 2^(S * c + off), dS = P * (dP - delta), packed to pairs in
-// place (sv[0..kN/2) = P, dv[0..kN/2) = dS). Per-column offsets come from `col_off` / `col_dlt` (shared
-// memory, kColVec) or per-row scalars; kMask zeroes the elements with `masked(i)` (causal diagonal block).
-template <bool kF16, bool kColVec, bool kMask, int kN, typename MaskFn>
-__device__ __forceinline__ void bwd_half_elementwise(uint32_t (&sv)[kN], uint32_t (&dv)[kN], float c, float row_off,
-                                                     float row_dlt, const float* col_off, const float* col_dlt,
-                                                     MaskFn masked) {
-  const uint64_t c2 = f2_pack(c, c);
-#pragma unroll
-  for (int i = 0; i < kN; i += 4) {
-    float o0, o1, o2, o3, d0, d1, d2, d3;
-    if (kColVec) {
-      const float4 ov = *reinterpret_cast<const float4*>(col_off + i);
-      const float4 dl = *reinterpret_cast<const float4*>(col_dlt + i);
-      o0 = ov.x; o1 = ov.y; o2 = ov.z; o3 = ov.w;
-      d0 = dl.x; d1 = dl.y; d2 = dl.z; d3 = dl.w;
-    } else {
-      o0 = o1 = o2 = o3 = row_off;
-      d0 = d1 = d2 = d3 = row_dlt;
-    }
-    const uint64_t p01 = f2_ex2(f2_fma(f2_pack(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), c2, f2_pack(o0, o1)));
-    const uint64_t p23 =
-        f2_ex2(f2_fma(f2_pack(__uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3])), c2, f2_pack(o2, o3)));
-    float p0, p1, p2, p3;
-    f2_unpack(p01, p0, p1);
-    f2_unpack(p23, p2, p3);
-    if (kMask) {
-      if (masked(i)) p0 = 0.0f;
-      if (masked(i + 1)) p1 = 0.0f;
-      if (masked(i + 2)) p2 = 0.0f;
-      if (masked(i + 3)) p3 = 0.0f;
-    }
-    const uint64_t g01 = f2_mul(f2_pack(p0, p1),
-                                f2_add(f2_pack(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])), f2_pack(-d0, -d1)));
-    const uint64_t g23 = f2_mul(
-        f2_pack(p2, p3), f2_add(f2_pack(__uint_as_float(dv[i + 2]), __uint_as_float(dv[i + 3])), f2_pack(-d2, -d3)));
-    float g0, g1, g2, g3;
-    f2_unpack(g01, g0, g1);
-    f2_unpack(g23, g2, g3);
-    sv[i >> 1] = pack2<kF16>(p0, p1);
-    sv[(i >> 1) + 1] = pack2<kF16>(p2, p3);
-    dv[i >> 1] = pack2<kF16>(g0, g1);
-    dv[(i >> 1) + 1] = pack2<kF16>(g2, g3);
-  }
-}
-
 template <int kD>
-__device__ __forceinline__ void mma_kmajor_n64(uint32_t d, uint32_t A, uint32_t B, uint32_t idesc) {
+__device__ __forceinline__ void mma_kmajor(uint32_t d, uint32_t A, uint32_t B, uint32_t idesc) {
 #pragma unroll
   for (int k = 0; k < kD / 16; ++k) {
     const uint32_t off = (k >> 2) * kAttnChunk + (k & 3) * 32;
@@ -241,10 +197,10 @@ __device__ __forceinline__ void mma_kmajor_n64(uint32_t d, uint32_t A, uint32_t 
 
 // ------------------------------------------------------------------------------------------------ dQ pass
 // Item = (b,h) pair and query block i; streams the K_j / V_j tiles of row i's key blocks through a ring.
-// TMEM: S [0,128), dP [128,256), dQ accumulator [256, 256 + D), dS (packed pairs) [384, 448). The key positions of
-// a block are handled in two halves of 64 (warpgroup x takes half x): the MMA thread issues S and dP per half
-// (N = 64), and dQ += dS K for half x as soon as warpgroup x has written it, followed by the next block's half x
-// scores, so the tensor pipe works on one half while the other half's elementwise step runs.
+// TMEM: S [0,128), dP [128,256), dQ accumulator [256, 256 + D), dS (packed pairs) [384, 448). Warpgroup x takes
+// key positions [64x, 64x + 64). Order per block j: S(j), dP(j); once S(j) sits in registers the next block's S is
+// issued; once dS(j) is in TMEM, dQ += dS(j) K_j and the next block's dP -- so the warps compute P while dP runs
+// and the scores of block j + 1 while they finish block j.
 template <bool kF16, int kD>
 struct BwdDqShape {
   static constexpr int kTile = kAttnBlk * kD * 2;
@@ -262,7 +218,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   constexpr int kTile = Sh::kTile;
   constexpr int kSlots = Sh::kSlots;
   constexpr uint32_t kFmt = kF16 ? 0u : 1u;
-  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 64, kFmt, kFmt, 0, 0);   // S, dP halves: N = 64 keys
+  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 128, kFmt, kFmt, 0, 0);  // S, dP: K = D, both K-major
   constexpr uint32_t IDESC_DQ = ptx::instr_desc(128, kD, kFmt, kFmt, 0, 1);  // dQ += dS K: K MN-major
   constexpr uint32_t T_S = 0, T_DP = 128, T_DQ = 256, T_DS = 384;
 
@@ -276,9 +232,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* qd_empty = bars + 1;
   uint64_t* kv_full = bars + 2;
   uint64_t* kv_empty = kv_full + kSlots;
-  uint64_t* sdp_full = kv_empty + kSlots;  // [2] per half
-  uint64_t* ds_full = sdp_full + 2;        // [2] per half, 4 warp arrivals
-  uint64_t* dq_done = ds_full + 2;
+  uint64_t* s_full = kv_empty + kSlots;   // S of the current block in TMEM
+  uint64_t* dp_full = s_full + 1;         // dP of the current block in TMEM
+  uint64_t* s_free = dp_full + 1;         // 8 warp arrivals: S has been read into registers
+  uint64_t* ds_full = s_free + 1;         // 8 warp arrivals: dS written (packed) to TMEM
+  uint64_t* dq_done = ds_full + 1;
   uint64_t* dq_empty = dq_done + 1;        // 8 warp arrivals: the accumulator has been read out
   uint64_t* drain = dq_empty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
@@ -293,10 +251,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ptx::mbar_init(ptx::smem_u32(&kv_full[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&kv_empty[s]), 1);
     }
-    for (int x = 0; x < 2; ++x) {
-      ptx::mbar_init(ptx::smem_u32(&sdp_full[x]), 1);
-      ptx::mbar_init(ptx::smem_u32(&ds_full[x]), 4);
-    }
+    ptx::mbar_init(ptx::smem_u32(s_full), 1);
+    ptx::mbar_init(ptx::smem_u32(dp_full), 1);
+    ptx::mbar_init(ptx::smem_u32(s_free), 8);
+    ptx::mbar_init(ptx::smem_u32(ds_full), 8);
     ptx::mbar_init(ptx::smem_u32(dq_done), 1);
     ptx::mbar_init(ptx::smem_u32(dq_empty), 8);
     ptx::mbar_init(ptx::smem_u32(drain), 1);
@@ -383,8 +341,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (one thread)
     if (lane == 0) {
-      uint32_t qd_phase = 0, slot = 0, slot_phase = 0, items_done = 0;
-      uint32_t ds_cnt[2] = {0, 0};
+      uint32_t qd_phase = 0, slot = 0, slot_phase = 0, items_done = 0, sf_cnt = 0, ds_cnt = 0;
       bool ok = true;
       const uint32_t kv0 = ptx::smem_u32(sKV), q0 = ptx::smem_u32(sQ), do0 = ptx::smem_u32(sdO);
       auto take = [&](uint32_t site) -> uint32_t {
@@ -393,61 +350,60 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
         return s;
       };
-      // S_x = Q K_x^T and dP_x = dO V_x^T for keys [64x, 64x + 64) of the block
-      auto issue_sdp = [&](int x, uint32_t sk, uint32_t sv) {
-        const uint32_t koff = kv0 + sk * kTile + x * 8192, voff = kv0 + sv * kTile + x * 8192;
-        mma_kmajor_n64<kD>(tmem_base + T_S + 64 * x, q0, koff, IDESC_S);
-        mma_kmajor_n64<kD>(tmem_base + T_DP + 64 * x, do0, voff, IDESC_S);
-        ptx::mma_commit(ptx::smem_u32(&sdp_full[x]));
+      auto issue_s = [&](uint32_t sk) {  // S = Q K^T
+        mma_kmajor<kD>(tmem_base + T_S, q0, kv0 + sk * kTile, IDESC_S);
+        ptx::mma_commit(ptx::smem_u32(s_full));
       };
-      // dQ += dS_x K_x: K steps over keys [64x + 16k, 64x + 16k + 16), dS_x packed at T_DS + 32x
-      auto issue_dq = [&](int x, uint32_t sk, bool first) {
+      auto issue_dp = [&](uint32_t sv) {  // dP = dO V^T
+        mma_kmajor<kD>(tmem_base + T_DP, do0, kv0 + sv * kTile, IDESC_S);
+        ptx::mma_commit(ptx::smem_u32(dp_full));
+      };
+      auto issue_dq = [&](uint32_t sk, bool first) {  // dQ += dS K: K step k = keys [16k, 16k + 16), dS columns 8k
         const uint32_t kA = kv0 + sk * kTile;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          ptx::mma_f16_ts(tmem_base + T_DQ, tmem_base + T_DS + 32 * x + 8 * k,
-                          ptx::smem_desc(kA + (4 * x + k) * 2048, kAttnChunk, 1024), IDESC_DQ,
-                          (first && k == 0) ? 0u : 1u);
+        for (int k = 0; k < 8; ++k)
+          ptx::mma_f16_ts(tmem_base + T_DQ, tmem_base + T_DS + 8 * k,
+                          ptx::smem_desc(kA + k * 2048, kAttnChunk, 1024), IDESC_DQ, (first && k == 0) ? 0u : 1u);
       };
+      // Per block j: S(j), dP(j) | S read -> S(j+1) | dS(j) written -> dQ(j), dP(j+1): the scores of the next block
+      // are computed while the warps work on this one.
       for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
         int bh, qb, j0, n;
         item_of(item, bh, qb, j0, n);
         if (n == 0) continue;
-        ok = wait_bounded(ptx::smem_u32(qd_full), qd_phase, ctl, 10);
+        ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(qd_full), qd_phase, ctl, 10);
         if (!ok) break;
         qd_phase ^= 1;
         uint32_t sk = take(11), sv = 0xFFFFFFFFu;
         if (sk != 0xFFFFFFFFu) sv = take(12);
         if (sv == 0xFFFFFFFFu) { ok = false; break; }
         ptx::tc_fence_after();
-        issue_sdp(0, sk, sv);
-        issue_sdp(1, sk, sv);
+        issue_s(sk);
+        issue_dp(sv);
         if (items_done > 0) {  // the previous item's dQ has been read out of TMEM
-          ok = wait_bounded(ptx::smem_u32(dq_empty), (items_done - 1) & 1, ctl, 16);
+          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(dq_empty), (items_done - 1) & 1, ctl, 16);
           if (!ok) break;
         }
         for (int j = 0; j < n && ok; ++j) {
-          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&ds_full[0]), ds_cnt[0] & 1, ctl, 13);
+          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(s_free), sf_cnt & 1, ctl, 13);
           if (!ok) break;
-          ++ds_cnt[0];
-          ptx::tc_fence_after();
-          issue_dq(0, sk, j == 0);
+          ++sf_cnt;
           uint32_t nk = 0xFFFFFFFFu, nv = 0xFFFFFFFFu;
           if (j + 1 < n) {
             nk = take(11);
             if (nk != 0xFFFFFFFFu) nv = take(12);
             if (nv == 0xFFFFFFFFu) { ok = false; break; }
             ptx::tc_fence_after();
-            issue_sdp(0, nk, nv);
+            issue_s(nk);
           }
-          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&ds_full[1]), ds_cnt[1] & 1, ctl, 14);
+          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(ds_full), ds_cnt & 1, ctl, 14);
           if (!ok) break;
-          ++ds_cnt[1];
+          ++ds_cnt;
           ptx::tc_fence_after();
-          issue_dq(1, sk, false);
+          issue_dq(sk, j == 0);
           ptx::mma_commit(ptx::smem_u32(&kv_empty[sk]));
           ptx::mma_commit(ptx::smem_u32(&kv_empty[sv]));
-          if (j + 1 < n) issue_sdp(1, nk, nv);
+          if (j + 1 < n) issue_dp(nv);
           sk = nk;
           sv = nv;
         }
@@ -466,12 +422,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ dS = P (dP - Delta), dQ out
     ptx::setmaxnreg_inc<kAttnRegsHigh>();
-    const int x = (warp - 4) >> 2;  // key half
+    const int x = (warp - 4) >> 2;  // key half: positions [64x, 64x + 64)
     const int q = warp & 3;
     const int r = 32 * q + lane;    // query row within the block == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
-    const float c = a.scale_log2;
-    uint32_t sdp_cnt = 0, dq_cnt = 0;
+    const uint64_t c2 = f2_pack(a.scale_log2, a.scale_log2);
+    uint32_t s_cnt = 0, dp_cnt = 0, dq_cnt = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
       int bh, qb, j0, n;
@@ -483,32 +439,56 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         continue;
       }
       const float off = __ldg(&a.nlse2[grow]);
-      const float dlt = __ldg(&a.delta[grow]);
+      const float ndlt = -__ldg(&a.delta[grow]);
+      const uint64_t off2 = f2_pack(off, off), ndlt2 = f2_pack(ndlt, ndlt);
       for (int j = 0; j < n; ++j) {
         const int kb = __ldg(&a.col_idx[j0 + j]);
-        ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&sdp_full[x]), sdp_cnt & 1, ctl, 20);
+        ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(s_full), s_cnt & 1, ctl, 20);
         if (!ok) break;
-        ++sdp_cnt;
+        ++s_cnt;
         ptx::tc_fence_after();
-        uint32_t sv[64], dv[64];
+        uint32_t pv[64];  // S, then P (fp32) of this warp's 64 keys
         const uint32_t ts = tmem_base + lane_off + T_S + 64 * x, tp = tmem_base + lane_off + T_DP + 64 * x;
-        ptx::tmem_ld_32x32b_x32(ts, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        ptx::tmem_ld_32x32b_x32(ts + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        ptx::tmem_ld_32x32b_x32(tp, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
-        ptx::tmem_ld_32x32b_x32(tp + 32, *reinterpret_cast<uint32_t(*)[32]>(&dv[32]));
+        ptx::tmem_ld_32x32b_x32(ts, *reinterpret_cast<uint32_t(*)[32]>(&pv[0]));
+        ptx::tmem_ld_32x32b_x32(ts + 32, *reinterpret_cast<uint32_t(*)[32]>(&pv[32]));
         ptx::tmem_wait_ld();
-        if (a.causal_diag && kb == qb) {  // key position 64x + i above query row r
-          bwd_half_elementwise<kF16, false, true, 64>(sv, dv, c, off, dlt, nullptr, nullptr,
-                                                  [&](int i) { return 64 * x + i > r; });
-        } else {
-          bwd_half_elementwise<kF16, false, false, 64>(sv, dv, c, off, dlt, nullptr, nullptr,
-                                                      [](int) { return false; });
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(s_free));  // the next block's S may overwrite it
+        const bool diag = a.causal_diag && kb == qb;
+#pragma unroll
+        for (int i = 0; i < 64; i += 2) {
+          float p0, p1;
+          f2_unpack(f2_ex2(f2_fma(f2_pack(__uint_as_float(pv[i]), __uint_as_float(pv[i + 1])), c2, off2)), p0, p1);
+          if (diag && 64 * x + i > r) p0 = 0.0f;      // key position above the query row
+          if (diag && 64 * x + i + 1 > r) p1 = 0.0f;
+          pv[i] = __float_as_uint(p0);
+          pv[i + 1] = __float_as_uint(p1);
         }
-        ptx::tmem_st_32x32b_x32(tmem_base + lane_off + T_DS + 32 * x, *reinterpret_cast<uint32_t(*)[32]>(&dv[0]));
+        ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(dp_full), dp_cnt & 1, ctl, 21);
+        if (!ok) break;
+        ++dp_cnt;
+        ptx::tc_fence_after();
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t dv[32];
+          ptx::tmem_ld_32x32b_x32(tp + 32 * cc, dv);
+          ptx::tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            float g0, g1;
+            f2_unpack(f2_mul(f2_pack(__uint_as_float(pv[32 * cc + i]), __uint_as_float(pv[32 * cc + i + 1])),
+                             f2_add(f2_pack(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])), ndlt2)),
+                      g0, g1);
+            pk[i >> 1] = pack2<kF16>(g0, g1);
+          }
+          ptx::tmem_st_32x32b_x16(tmem_base + lane_off + T_DS + 32 * x + 16 * cc, pk);
+        }
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&ds_full[x]));
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(ds_full));
       }
       if (!ok) break;
       ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(dq_done), dq_cnt & 1, ctl, 22);
@@ -530,9 +510,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 
 // ------------------------------------------------------------------------------------------------ dK/dV pass
 // Item = (b,h) pair and key block j; streams Q_i, dO_i (+ -LSE_i log2(e), Delta_i) of column j's query blocks.
-// TMEM: S^T [0,128) -> packed P^T of half x at [64x, 64x + 32); dP^T [128,256) -> packed dS^T of half x at
-// [128 + 64x, ...); dV accumulator [256, 256 + D), dK accumulator [256 + D, 256 + 2D). Query positions are handled
-// in two halves of 64 (warpgroup x takes half x), pipelined like the dQ pass.
+// TMEM: S^T [0,128) -> packed P^T of warpgroup x's query positions [64x, 64x + 64) at [64x, 64x + 32); dP^T
+// [128,256) -> packed dS^T likewise at [128 + 64x, ...); dV accumulator [256, 256 + D), dK [256 + D, 256 + 2D).
+// Order per block t: S^T(t), dP^T(t); P^T written -> dV(t), S^T(t+1); dS^T written -> dK(t), dP^T(t+1).
 template <bool kF16, int kD>
 struct BwdDkdvShape {
   static constexpr int kTile = kAttnBlk * kD * 2;
@@ -552,7 +532,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   constexpr int kSlots = Sh::kSlots;
   constexpr int kSlotBytes = Sh::kSlotBytes;
   constexpr uint32_t kFmt = kF16 ? 0u : 1u;
-  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 64, kFmt, kFmt, 0, 0);    // S^T, dP^T halves: N = 64 queries
+  constexpr uint32_t IDESC_S = ptx::instr_desc(128, 128, kFmt, kFmt, 0, 0);   // S^T, dP^T: K = D, both K-major
   constexpr uint32_t IDESC_ACC = ptx::instr_desc(128, kD, kFmt, kFmt, 0, 1);  // dV, dK: B (dO, Q) MN-major
   constexpr uint32_t T_S = 0, T_DP = 128, T_DV = 256, T_DK = 256 + kD;
 
@@ -566,9 +546,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* kv_empty = bars + 1;
   uint64_t* qd_full = bars + 2;
   uint64_t* qd_empty = qd_full + kSlots;
-  uint64_t* sdp_full = qd_empty + kSlots;  // [2] per half
-  uint64_t* p_full = sdp_full + 2;         // [2] per half, 4 warp arrivals
-  uint64_t* acc_done = p_full + 2;
+  uint64_t* s_full = qd_empty + kSlots;   // S^T of the current block in TMEM
+  uint64_t* dp_full = s_full + 1;         // dP^T of the current block in TMEM
+  uint64_t* p_full = dp_full + 1;         // 8 warp arrivals: P^T written (packed) to TMEM
+  uint64_t* ds_full = p_full + 1;         // 8 warp arrivals: dS^T written (packed) to TMEM
+  uint64_t* acc_done = ds_full + 1;
   uint64_t* acc_empty = acc_done + 1;      // 8 warp arrivals: dK / dV read out of TMEM
   uint64_t* drain = acc_empty + 1;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
@@ -583,10 +565,10 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ptx::mbar_init(ptx::smem_u32(&qd_full[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&qd_empty[s]), 1);
     }
-    for (int x = 0; x < 2; ++x) {
-      ptx::mbar_init(ptx::smem_u32(&sdp_full[x]), 1);
-      ptx::mbar_init(ptx::smem_u32(&p_full[x]), 4);
-    }
+    ptx::mbar_init(ptx::smem_u32(s_full), 1);
+    ptx::mbar_init(ptx::smem_u32(dp_full), 1);
+    ptx::mbar_init(ptx::smem_u32(p_full), 8);
+    ptx::mbar_init(ptx::smem_u32(ds_full), 8);
     ptx::mbar_init(ptx::smem_u32(acc_done), 1);
     ptx::mbar_init(ptx::smem_u32(acc_empty), 8);
     ptx::mbar_init(ptx::smem_u32(drain), 1);
@@ -684,8 +666,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer (one thread)
     if (lane == 0) {
-      uint32_t kv_phase = 0, slot = 0, slot_phase = 0, items_done = 0;
-      uint32_t p_cnt[2] = {0, 0};
+      uint32_t kv_phase = 0, slot = 0, slot_phase = 0, items_done = 0, p_cnt = 0, ds_cnt = 0;
       bool ok = true;
       const uint32_t qd0 = ptx::smem_u32(sQD), k0 = ptx::smem_u32(sK), v0 = ptx::smem_u32(sV);
       auto take = [&](uint32_t site) -> uint32_t {
@@ -694,62 +675,68 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
         return s;
       };
-      // S^T_x = K Q_x^T and dP^T_x = V dO_x^T for query positions [64x, 64x + 64) of the slot's block
-      auto issue_sdp = [&](int x, uint32_t sl) {
-        const uint32_t qA = qd0 + sl * kSlotBytes + x * 8192, dA = qA + kTile;
-        mma_kmajor_n64<kD>(tmem_base + T_S + 64 * x, k0, qA, IDESC_S);
-        mma_kmajor_n64<kD>(tmem_base + T_DP + 64 * x, v0, dA, IDESC_S);
-        ptx::mma_commit(ptx::smem_u32(&sdp_full[x]));
+      auto issue_s = [&](uint32_t sl) {  // S^T = K Q^T
+        mma_kmajor<kD>(tmem_base + T_S, k0, qd0 + sl * kSlotBytes, IDESC_S);
+        ptx::mma_commit(ptx::smem_u32(s_full));
       };
-      // dV += P^T_x dO_x, dK += dS^T_x Q_x: K steps over query rows [64x + 16k, ...), packed columns 64x + 8k
-      auto issue_acc = [&](int x, uint32_t sl, bool first) {
-        const uint32_t qA = qd0 + sl * kSlotBytes, dA = qA + kTile;
+      auto issue_dp = [&](uint32_t sl) {  // dP^T = V dO^T
+        mma_kmajor<kD>(tmem_base + T_DP, v0, qd0 + sl * kSlotBytes + kTile, IDESC_S);
+        ptx::mma_commit(ptx::smem_u32(dp_full));
+      };
+      // K step k = query rows [16k, 16k + 16): packed columns 8k of half 0, 64 + 8(k - 4) of half 1
+      auto pcol = [](int k) -> uint32_t { return 8 * k + (k >= 4 ? 32 : 0); };
+      auto issue_dv = [&](uint32_t sl, bool first) {  // dV += P^T dO
+        const uint32_t dA = qd0 + sl * kSlotBytes + kTile;
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t acc = (first && k == 0) ? 0u : 1u;
-          const uint32_t pc = 64 * x + 8 * k;
-          ptx::mma_f16_ts(tmem_base + T_DV, tmem_base + T_S + pc,
-                          ptx::smem_desc(dA + (4 * x + k) * 2048, kAttnChunk, 1024), IDESC_ACC, acc);
-          ptx::mma_f16_ts(tmem_base + T_DK, tmem_base + T_DP + pc,
-                          ptx::smem_desc(qA + (4 * x + k) * 2048, kAttnChunk, 1024), IDESC_ACC, acc);
-        }
+        for (int k = 0; k < 8; ++k)
+          ptx::mma_f16_ts(tmem_base + T_DV, tmem_base + T_S + pcol(k), ptx::smem_desc(dA + k * 2048, kAttnChunk, 1024),
+                          IDESC_ACC, (first && k == 0) ? 0u : 1u);
       };
+      auto issue_dk = [&](uint32_t sl, bool first) {  // dK += dS^T Q
+        const uint32_t qA = qd0 + sl * kSlotBytes;
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          ptx::mma_f16_ts(tmem_base + T_DK, tmem_base + T_DP + pcol(k), ptx::smem_desc(qA + k * 2048, kAttnChunk, 1024),
+                          IDESC_ACC, (first && k == 0) ? 0u : 1u);
+      };
+      // Per block t: S^T(t), dP^T(t) | P^T written -> dV(t), S^T(t+1) | dS^T written -> dK(t), dP^T(t+1): the
+      // warps compute P^T while dP^T runs and dS^T while dV and the next S^T run.
       for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
         int bh, kb, i0, n;
         item_of(item, bh, kb, i0, n);
         if (n == 0) continue;
-        ok = wait_bounded(ptx::smem_u32(kv_full), kv_phase, ctl, 10);
+        ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(kv_full), kv_phase, ctl, 10);
         if (!ok) break;
         kv_phase ^= 1;
         uint32_t cur = take(11);
         if (cur == 0xFFFFFFFFu) { ok = false; break; }
         ptx::tc_fence_after();
-        issue_sdp(0, cur);
-        issue_sdp(1, cur);
+        issue_s(cur);
+        issue_dp(cur);
         if (items_done > 0) {  // the previous item's dK / dV have been read out of TMEM
-          ok = wait_bounded(ptx::smem_u32(acc_empty), (items_done - 1) & 1, ctl, 16);
+          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(acc_empty), (items_done - 1) & 1, ctl, 16);
           if (!ok) break;
         }
         for (int t = 0; t < n && ok; ++t) {
-          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&p_full[0]), p_cnt[0] & 1, ctl, 12);
+          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(p_full), p_cnt & 1, ctl, 12);
           if (!ok) break;
-          ++p_cnt[0];
+          ++p_cnt;
           ptx::tc_fence_after();
-          issue_acc(0, cur, t == 0);
+          issue_dv(cur, t == 0);
           uint32_t nxt = 0xFFFFFFFFu;
           if (t + 1 < n) {
             nxt = take(11);
             if (nxt == 0xFFFFFFFFu) { ok = false; break; }
             ptx::tc_fence_after();
-            issue_sdp(0, nxt);
+            issue_s(nxt);
           }
-          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&p_full[1]), p_cnt[1] & 1, ctl, 13);
+          ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(ds_full), ds_cnt & 1, ctl, 13);
           if (!ok) break;
-          ++p_cnt[1];
+          ++ds_cnt;
           ptx::tc_fence_after();
-          issue_acc(1, cur, false);
+          issue_dk(cur, t == 0);
           ptx::mma_commit(ptx::smem_u32(&qd_empty[cur]));
-          if (t + 1 < n) issue_sdp(1, nxt);
+          if (t + 1 < n) issue_dp(nxt);
           cur = nxt;
         }
         if (!ok) break;
@@ -771,8 +758,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int q = warp & 3;
     const int r = 32 * q + lane;    // key row within the block == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
-    const float c = a.scale_log2;
-    uint32_t sdp_cnt = 0, acc_cnt = 0, slot = 0, slot_phase = 0;
+    const uint64_t c2 = f2_pack(a.scale_log2, a.scale_log2);
+    uint32_t s_cnt = 0, dp_cnt = 0, acc_cnt = 0, slot = 0, slot_phase = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
       int bh, kb, i0, n;
@@ -789,40 +776,83 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const int qb = __ldg(&a.row_idx[i0 + t]);
         const bool valid = qb >= 0 && qb < a.nqb;
         ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&qd_full[slot]), slot_phase, ctl, 19);  // offsets
-        if (ok) ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(&sdp_full[x]), sdp_cnt & 1, ctl, 20);
+        if (ok) ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(s_full), s_cnt & 1, ctl, 20);
         if (!ok) break;
-        ++sdp_cnt;
+        ++s_cnt;
         ptx::tc_fence_after();
         const float* off_s = reinterpret_cast<const float*>(sQD + slot * kSlotBytes + 2 * kTile) + 64 * x;
         const float* dlt_s = off_s + 128;
         const uint32_t ts = tmem_base + lane_off + T_S + 64 * x, tp = tmem_base + lane_off + T_DP + 64 * x;
         const bool diag = a.causal_diag && qb == kb;
-        // Two chunks of 32 query positions; chunk cc's packed P^T / dS^T (16 columns each) land at ts / tp + 16cc,
-        // inside the columns [0, 32) this warp has already read, never over chunk 1's unread scores.
-#pragma unroll 1
-        for (int cc = 0; cc < 2; ++cc) {
-          uint32_t sv[32], dv[32];
-          ptx::tmem_ld_32x32b_x32(ts + 32 * cc, sv);
-          ptx::tmem_ld_32x32b_x32(tp + 32 * cc, dv);
-          ptx::tmem_wait_ld();
-          const int col0 = 64 * x + 32 * cc;  // query position of column 0 of the chunk
-          if (!valid) {
+        float pf[64];  // P^T (fp32) of this warp's 64 query positions, kept for dS^T
+        // Two chunks of 32 positions; chunk cc's packed values (16 columns) land at ts + 16cc, inside the columns
+        // [0, 32) this warp has already read, never over chunk 1's unread scores.
 #pragma unroll
-            for (int i = 0; i < 16; ++i) sv[i] = dv[i] = 0u;
-          } else if (diag) {  // key row r above query position col0 + i
-            bwd_half_elementwise<kF16, true, true, 32>(sv, dv, c, 0.0f, 0.0f, off_s + 32 * cc, dlt_s + 32 * cc,
-                                                       [&](int i) { return r > col0 + i; });
-          } else {
-            bwd_half_elementwise<kF16, true, false, 32>(sv, dv, c, 0.0f, 0.0f, off_s + 32 * cc, dlt_s + 32 * cc,
-                                                        [](int) { return false; });
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t sv[32];
+          ptx::tmem_ld_32x32b_x32(ts + 32 * cc, sv);
+          ptx::tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const float4 o = *reinterpret_cast<const float4*>(off_s + 32 * cc + i);
+            float p0, p1, p2, p3;
+            f2_unpack(f2_ex2(f2_fma(f2_pack(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), c2, f2_pack(o.x, o.y))),
+                      p0, p1);
+            f2_unpack(f2_ex2(f2_fma(f2_pack(__uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3])), c2,
+                                    f2_pack(o.z, o.w))),
+                      p2, p3);
+            const int col = 64 * x + 32 * cc + i;  // query position
+            if (!valid) p0 = p1 = p2 = p3 = 0.0f;
+            if (diag) {  // key row r above the query position
+              if (r > col) p0 = 0.0f;
+              if (r > col + 1) p1 = 0.0f;
+              if (r > col + 2) p2 = 0.0f;
+              if (r > col + 3) p3 = 0.0f;
+            }
+            pf[32 * cc + i] = p0;
+            pf[32 * cc + i + 1] = p1;
+            pf[32 * cc + i + 2] = p2;
+            pf[32 * cc + i + 3] = p3;
+            pk[i >> 1] = pack2<kF16>(p0, p1);
+            pk[(i >> 1) + 1] = pack2<kF16>(p2, p3);
           }
-          ptx::tmem_st_32x32b_x16(ts + 16 * cc, sv);
-          ptx::tmem_st_32x32b_x16(tp + 16 * cc, dv);
+          ptx::tmem_st_32x32b_x16(ts + 16 * cc, pk);
         }
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&p_full[x]));
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(p_full));
+        ok = warp_wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(dp_full), dp_cnt & 1, ctl, 21);
+        if (!ok) break;
+        ++dp_cnt;
+        ptx::tc_fence_after();
+#pragma unroll
+        for (int cc = 0; cc < 2; ++cc) {
+          uint32_t dv[32];
+          ptx::tmem_ld_32x32b_x32(tp + 32 * cc, dv);
+          ptx::tmem_wait_ld();
+          uint32_t pk[16];
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            const float4 d = *reinterpret_cast<const float4*>(dlt_s + 32 * cc + i);
+            float g0, g1, g2, g3;
+            f2_unpack(f2_mul(f2_pack(pf[32 * cc + i], pf[32 * cc + i + 1]),
+                             f2_add(f2_pack(__uint_as_float(dv[i]), __uint_as_float(dv[i + 1])), f2_pack(-d.x, -d.y))),
+                      g0, g1);
+            f2_unpack(f2_mul(f2_pack(pf[32 * cc + i + 2], pf[32 * cc + i + 3]),
+                             f2_add(f2_pack(__uint_as_float(dv[i + 2]), __uint_as_float(dv[i + 3])),
+                                    f2_pack(-d.z, -d.w))),
+                      g2, g3);
+            pk[i >> 1] = pack2<kF16>(g0, g1);
+            pk[(i >> 1) + 1] = pack2<kF16>(g2, g3);
+          }
+          ptx::tmem_st_32x32b_x16(tp + 16 * cc, pk);
+        }
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(ds_full));
         if (++slot == kSlots) { slot = 0; slot_phase ^= 1; }
       }
       if (!ok) break;
