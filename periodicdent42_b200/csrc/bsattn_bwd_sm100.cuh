@@ -126,7 +126,65 @@ __global__ void bsattn_mask_transpose_kernel(const int* __restrict__ row_ptr, co
   }
 }
 
-// Block mask of dense (every key block) or causal (key blocks 0..i of query block i) attention for `pairs`
+// Column lists, one CTA per (b,h) pair (nqb <= kTransposeSmemMaxBlocks): the pair's block mask as an nqb x nqb bit
+// map in shared memory (set from the row lists by the threads of each row), per-column counts, a CTA scan into
+// col_ptr, and each column's thread writes its query blocks in ascending order. Same output as the kernel above.
+constexpr int kTransposeSmemMaxBlocks = 512;  // bit map of 512 x 512 bits = 32 KB
+
+__global__ void __launch_bounds__(256) bsattn_mask_transpose_smem_kernel(const int* __restrict__ row_ptr,
+                                                                         const int* __restrict__ col_idx, int pairs,
+                                                                         int nqb, int* __restrict__ col_ptr,
+                                                                         int* __restrict__ row_idx,
+                                                                         int* __restrict__ bad) {
+  extern __shared__ uint32_t bits[];  // [nqb][words per row]
+  __shared__ int warp_sum[8];
+  const int wpr = (nqb + 31) / 32;
+  for (int p = blockIdx.x; p < pairs; p += gridDim.x) {
+    for (int w = threadIdx.x; w < nqb * wpr; w += blockDim.x) bits[w] = 0u;
+    __syncthreads();
+    for (int i = threadIdx.x; i < nqb; i += blockDim.x)
+      for (int e = row_ptr[p * nqb + i]; e < row_ptr[p * nqb + i + 1]; ++e) {
+        const int kb = col_idx[e];
+        if (kb < 0 || kb >= nqb) {
+          *bad = 1;
+          continue;
+        }
+        atomicOr(&bits[i * wpr + (kb >> 5)], 1u << (kb & 31));
+      }
+    __syncthreads();
+    // scan of the column counts, nqb columns in chunks of blockDim, running carry in `base`
+    int base = row_ptr[p * nqb];
+    for (int j0 = 0; j0 < nqb; j0 += blockDim.x) {
+      const int j = j0 + threadIdx.x;
+      int cnt = 0;
+      if (j < nqb)
+        for (int i = 0; i < nqb; ++i) cnt += (bits[i * wpr + (j >> 5)] >> (j & 31)) & 1u;
+      int incl = cnt;
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+        if ((threadIdx.x & 31) >= o) incl += v;
+      }
+      if ((threadIdx.x & 31) == 31) warp_sum[threadIdx.x >> 5] = incl;
+      __syncthreads();
+      int before = base;
+      for (int w = 0; w < (threadIdx.x >> 5); ++w) before += warp_sum[w];
+      int pos = before + incl - cnt;
+      if (j < nqb) {
+        col_ptr[p * nqb + j] = pos;
+        for (int i = 0; i < nqb; ++i)
+          if ((bits[i * wpr + (j >> 5)] >> (j & 31)) & 1u) row_idx[pos++] = i;
+      }
+      int total = 0;
+      for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) total += warp_sum[w];
+      __syncthreads();
+      base += total;
+    }
+    if (p == pairs - 1 && threadIdx.x == 0) col_ptr[pairs * nqb] = base;
+    __syncthreads();
+  }
+}
+
+// Block mask of dense (every key block) or causal// Block mask of dense (every key block) or causal (key blocks 0..i of query block i) attention for `pairs`
 // (b,h) pairs: one thread per block-row writes its row pointer and column list.
 __global__ void attn_full_mask_kernel(int pairs, int nqb, int causal, int* __restrict__ row_ptr,
                                       int* __restrict__ col_idx) {

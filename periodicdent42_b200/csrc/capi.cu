@@ -1505,8 +1505,14 @@ int bsk_bsattn_mask_transpose(const int32_t* row_ptr, const int32_t* col_idx, in
   int* bad = reinterpret_cast<int*>(static_cast<char*>(workspace) + (int64_t)pairs * nqb * 4);
   cudaError_t e = cudaMemsetAsync(bad, 0, sizeof(int), s);
   if (e != cudaSuccess) return cuda_fail(e, "bsattn_mask_transpose");
-  const int threads = 128, grid = (pairs + threads - 1) / threads;
-  bsattn_mask_transpose_kernel<<<grid, threads, 0, s>>>(row_ptr, col_idx, pairs, nqb, col_ptr, row_idx, cursor, bad);
+  if (nqb <= kTransposeSmemMaxBlocks) {
+    const int smem = nqb * ((nqb + 31) / 32) * 4;
+    const int grid = pairs < st->sm_count * 4 ? pairs : st->sm_count * 4;
+    bsattn_mask_transpose_smem_kernel<<<grid, 256, smem, s>>>(row_ptr, col_idx, pairs, nqb, col_ptr, row_idx, bad);
+  } else {
+    const int threads = 128, grid = (pairs + threads - 1) / threads;
+    bsattn_mask_transpose_kernel<<<grid, threads, 0, s>>>(row_ptr, col_idx, pairs, nqb, col_ptr, row_idx, cursor, bad);
+  }
   return launch_status("bsattn_mask_transpose");
 }
 

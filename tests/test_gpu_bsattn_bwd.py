@@ -130,3 +130,28 @@ def test_autograd_and_determinism(no_device_error, cuda_dev):
     _, gq64, gk64, gv64 = _grads(q, k, v, dO.cpu(), mask, 1.0 / math.sqrt(128), torch.float64)
     for got, want in zip(grads[0], (gq64, gk64, gv64)):
         assert ref.normwise_rel_err(got.cpu(), want) <= 2e-2
+
+
+@pytest.mark.parametrize("pairs,nqb,density", [(5, 40, 0.3), (2, 600, 0.02)])
+def test_mask_transpose_random_masks(cuda_dev, pairs, nqb, density):
+    """Random block masks through both transpose paths (shared-memory bit map for nqb <= 512, the serial kernel
+    above): ascending query blocks per key block-column, col_ptr in row_ptr's numbering."""
+    g = torch.Generator().manual_seed(nqb)
+    rps, cis, base = [0], [], 0
+    for p in range(pairs):
+        m = torch.rand(nqb, nqb, generator=g) < density
+        crow, col = wl.mask_to_bsr(m)
+        rps.extend((crow[1:] + base).tolist())
+        cis.extend(col.tolist())
+        base += int(crow[-1])
+    rp, ci = torch.tensor(rps, dtype=torch.int32), torch.tensor(cis, dtype=torch.int32)
+    col_ptr, row_idx = _capi.bsattn_mask_transpose(rp.to(cuda_dev), ci.to(cuda_dev), pairs, nqb)
+    col_ptr, row_idx = col_ptr.cpu().tolist(), row_idx.cpu().tolist()
+    for p in range(pairs):
+        cols = [[] for _ in range(nqb)]
+        for i in range(nqb):
+            for kb in cis[rps[p * nqb + i]:rps[p * nqb + i + 1]]:
+                cols[kb].append(i)
+        for j in range(nqb):
+            assert row_idx[col_ptr[p * nqb + j]:col_ptr[p * nqb + j + 1]] == cols[j], (p, j)
+    assert col_ptr[-1] == rps[-1]
