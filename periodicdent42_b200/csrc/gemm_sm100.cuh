@@ -112,17 +112,19 @@ __device__ __forceinline__ bool bsrbsr_pair(const GemmArgs& a, int j, int jc, in
   return p0 >= 0 || p1 >= 0;
 }
 
-// Warp-collective: how many of A's blocks [j0, j1) contribute to the tile starting at block column jc (32 blocks
-// examined per round, one per lane). Same answer on every lane and in every role of the CTA.
-__device__ __forceinline__ int bsrbsr_count(const GemmArgs& a, int j0, int j1, int jc) {
+// Warp-collective: how many of A's blocks [j0, j1) meet B block (kb, jc) (*c0) and (kb, jc + 1) (*c1), i.e. how
+// many MMAs each 128-column half of the tile receives. Same answer on every lane and in every role of the CTA.
+__device__ __forceinline__ void bsrbsr_half_counts(const GemmArgs& a, int j0, int j1, int jc, int* c0, int* c1) {
   const int lane = threadIdx.x & 31;
-  int n = 0;
+  int n0 = 0, n1 = 0;
   for (int jb = j0; jb < j1; jb += 32) {
-    int p0, p1;
-    const bool on = jb + lane < j1 && bsrbsr_pair(a, jb + lane, jc, p0, p1);
-    n += __popc(__ballot_sync(0xFFFFFFFFu, on));
+    int p0 = -1, p1 = -1;
+    if (jb + lane < j1) bsrbsr_pair(a, jb + lane, jc, p0, p1);
+    n0 += __popc(__ballot_sync(0xFFFFFFFFu, p0 >= 0));
+    n1 += __popc(__ballot_sync(0xFFFFFFFFu, p1 >= 0));
   }
-  return n;
+  *c0 = n0;
+  *c1 = n1;
 }
 
 __device__ __forceinline__ void st_global_v4(float* p, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -260,14 +262,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               if (!ok) break;
               if (lane == 0) {
                 const uint32_t fb = ptx::smem_u32(&full[stage]);
-                ptx::mbar_arrive_expect_tx(fb, STAGE_TX);
+                ptx::mbar_arrive_expect_tx(fb, kGemmAStage + (q0 >= 0 ? kGemmBStage / 2 : 0) +
+                                                   (q1 >= 0 ? kGemmBStage / 2 : 0));
                 ptx::tma_load_2d(ptx::smem_u32(sA + stage * kGemmAStage), &tmA, fb, s * BK, (jb + jj) * 128);
-                // B: K rows [s*BK, +BK) of blocks (kb, jc) -> columns [0,128) and (kb, jc+1) -> [128,256) of the
-                // tile; a missing block is read at row b_nnzb*128 (past the end), i.e. as zeros
+                // B: K rows [s*BK, +BK) of block (kb, jc) -> columns [0,128) and of (kb, jc+1) -> [128,256) of the
+                // tile; only the blocks that exist are loaded (the MMA warp skips the other half)
                 const uint32_t bdst = ptx::smem_u32(sB + stage * kGemmBStage);
 #pragma unroll
                 for (int q = 0; q < 4; ++q)
-                  ptx::tma_load_2d(bdst + q * (BK * 128), &tmB, fb, (q & 1) * 64, (q < 2 ? r0 : r1) + s * BK);
+                  if ((q < 2 ? q0 : q1) >= 0)
+                    ptx::tma_load_2d(bdst + q * (BK * 128), &tmB, fb, (q & 1) * 64, (q < 2 ? r0 : r1) + s * BK);
               }
               ++issued;
               if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
@@ -331,37 +335,62 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint64_t adesc0 = ptx::smem_desc(ptx::smem_u32(sA), 16, 1024);
     const uint64_t bdesc0 = ptx::smem_desc(ptx::smem_u32(sB), BK * 128, 1024);
     constexpr uint32_t B_KSTEP = (MMA_K * 128) >> 4;
+    constexpr uint32_t IDESC_HALF = ptx::instr_desc(kGemmBM, 128, 0, 0, 0, 1);  // one B block: N = 128
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int mt, nt;
       gemm_tile_coords(tile, a, mt, nt);
       int j0, j1;
       bsr_row_range(a, a.row_begin + mt, j0, j1);
-      const int nk = bsrbsr_count(a, j0, j1, nt * kGemmBN / 128) * BSR_STEPS;
+      const int jc = nt * kGemmBN / 128;
       if (lane == 0) {
         ok = wait_bounded(tempty0 + acc * 8, acc_phase ^ 1, ctl, 3);
-        if (ok) {
-          ptx::tc_fence_after();
-          const uint32_t d_tmem = tmem_base + acc * kGemmBN;
-          for (int kb = 0; kb < nk; ++kb) {
-            ok = wait_bounded(full0 + stage * 8, phase, ctl, 4);
-            if (!ok) break;
-            ptx::tc_fence_after();
-            const uint64_t ad = adesc0 + ((stage * kGemmAStage) >> 4);
-            const uint64_t bd = bdesc0 + ((stage * kGemmBStage) >> 4);
-#pragma unroll
-            for (int k = 0; k < K_STEPS; ++k) ptx::mma_f16_ss(d_tmem, ad + k * 2, bd + k * B_KSTEP, IDESC, (kb | k) != 0);
-            ptx::mma_commit(empty0 + stage * 8);
-            if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
-          }
-          if (ok) {
-            ptx::mma_commit(tfull0 + acc * 8);
-            acc ^= 1;
-            if (acc == 0) acc_phase ^= 1;
-          }
-        }
+        if (ok) ptx::tc_fence_after();
       }
       ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
       if (!ok) break;
+      const uint32_t d_tmem = tmem_base + acc * kGemmBN;
+      bool init0 = false, init1 = false;  // lane 0: the tile's half has received its first (overwriting) MMA
+      // Blocks in the producer's order: ascending within each group of 32; per block, an N = 128 MMA for each
+      // B block that exists (column half 0 <- (kb, jc), half 1 <- (kb, jc + 1)).
+      for (int jb = j0; jb < j1 && ok; jb += 32) {
+        int p0 = -1, p1 = -1;
+        if (jb + lane < j1) bsrbsr_pair(a, jb + lane, jc, p0, p1);
+        const unsigned h0 = __ballot_sync(0xFFFFFFFFu, p0 >= 0), h1 = __ballot_sync(0xFFFFFFFFu, p1 >= 0);
+        if (lane == 0) {
+          unsigned live = h0 | h1;
+          while (live && ok) {
+            const int jj = __ffs(live) - 1;
+            live &= live - 1;
+            const bool has0 = (h0 >> jj) & 1u, has1 = (h1 >> jj) & 1u;
+            for (int s = 0; s < BSR_STEPS && ok; ++s) {
+              ok = wait_bounded(full0 + stage * 8, phase, ctl, 4);
+              if (!ok) break;
+              ptx::tc_fence_after();
+              const uint64_t ad = adesc0 + ((stage * kGemmAStage) >> 4);
+              const uint64_t bd = bdesc0 + ((stage * kGemmBStage) >> 4);
+#pragma unroll
+              for (int k = 0; k < K_STEPS; ++k) {
+                if (has0) ptx::mma_f16_ss(d_tmem, ad + k * 2, bd + k * B_KSTEP, IDESC_HALF, (init0 || k) ? 1u : 0u);
+                if (has1)
+                  ptx::mma_f16_ss(d_tmem + 128, ad + k * 2, bd + ((2 * BK * 128) >> 4) + k * B_KSTEP, IDESC_HALF,
+                                  (init1 || k) ? 1u : 0u);
+              }
+              init0 = init0 || has0;
+              init1 = init1 || has1;
+              ptx::mma_commit(empty0 + stage * 8);
+              if (++stage == kGemmStages) { stage = 0; phase ^= 1; }
+            }
+          }
+        }
+        ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
+      }
+      if (!ok) break;
+      if (lane == 0) {
+        ptx::mma_commit(tfull0 + acc * 8);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      __syncwarp();
     }
     if (lane == 0) {  // all MMAs this thread issued complete before TMEM is released
       ptx::mma_commit(ptx::smem_u32(drain));
@@ -437,7 +466,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int mt, nt;
       gemm_tile_coords(tile, a, mt, nt);
-      int m0, nk = 1;
+      int m0, nk = 1, nk1 = 1;  // nk1: MMAs into the second 128-column half (BSR x BSR), else unused
       if constexpr (kML == Mainloop::Dense) {
         m0 = mt * kGemmBM;
       } else {
@@ -446,9 +475,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int j0, j1;
         bsr_row_range(a, r, j0, j1);
         if constexpr (kML == Mainloop::BsrBsr)
-          nk = bsrbsr_count(a, j0, j1, nt * kGemmBN / 128);
+          bsrbsr_half_counts(a, j0, j1, nt * kGemmBN / 128, &nk, &nk1);
         else
-          nk = j1 - j0;
+          nk = nk1 = j1 - j0;
       }
       const int n0 = nt * kGemmBN;
       if (!warp_wait_bounded(ptx::smem_u32(&tfull[acc]), acc_phase, ctl, 6)) break;
@@ -460,7 +489,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       for (int c = 0; c < kGemmBN; c += 32) {
         uint32_t r[32];
         __syncwarp();
-        if (nk > 0) {
+        if ((c < 128 ? nk : nk1) > 0) {  // a half no MMA wrote holds stale values: it is zero
           ptx::tmem_ld_32x32b_x32(t_row + c, r);
           ptx::tmem_wait_ld();
         } else {
