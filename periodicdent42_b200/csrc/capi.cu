@@ -16,6 +16,7 @@
 #include "bsk_capi.h"
 #include "gemm_sm100.cuh"
 #include "gemm_pair_sm100.cuh"
+#include "bsr_pair_sm100.cuh"
 #include "bsattn_sm100.cuh"
 #include "bsr_convert.cuh"
 #include "bsattn_bwd_sm100.cuh"
@@ -50,6 +51,7 @@ struct DeviceState {
   std::string init_error;
   int sm_count = 0;
   int pair_clusters = 0;       // co-resident 2-CTA clusters of the pair GEMM kernels (all share one footprint)
+  int bsr_pair_clusters = 0;   // co-resident 2-CTA clusters of the pair BSR SpMM kernel (0: not used)
   uint32_t* err_word = nullptr;
 };
 DeviceState g_devices[kMaxDevices];
@@ -156,6 +158,7 @@ void init_device(DeviceState& st, int dev) {
       allow_smem(gemm_pair_sm100_kernel<2, Epi::F32PeerRows, 1>, kPairSmemBytes),
       allow_smem(gemm_pair_sm100_kernel<2, Epi::F32PeerRows, 2>, kPairWideSmemBytes),
       allow_smem(gemm_pair_sm100_kernel<1, Epi::BF16Scaled, 2>, kPairWideSmemBytes),
+      allow_smem(spmm_bsr_pair_sm100_kernel, kBsrPairSmemBytes),
   };
   for (cudaError_t x : errs) {
     if (x != cudaSuccess) {
@@ -172,6 +175,7 @@ void init_device(DeviceState& st, int dev) {
     st.pair_clusters = c[0];
     for (int i = 1; i < 4; ++i) st.pair_clusters = c[i] < st.pair_clusters ? c[i] : st.pair_clusters;
   }
+  st.bsr_pair_clusters = max_clusters(spmm_bsr_pair_sm100_kernel, kPairThreads, kBsrPairSmemBytes);
   if (st.pair_clusters <= 0) {
     st.status = BSK_ERR_CUDA;
     st.init_error = "cudaOccupancyMaxActiveClusters reports no co-resident CTA pair";
@@ -936,22 +940,29 @@ int bsk_spmm_bsr_f16f32(const int32_t* row_ptr, const int32_t* col_idx, const vo
                                       (size_t)(row_end - row_begin) * bs_r, s);
     return e == cudaSuccess ? BSK_OK : cuda_fail(e, "spmm_bsr: zero fill");
   }
+  // Tile kind: 0 = one CTA per 128 x 256 output tile; 1 = a CTA pair per 128 x 512 tile computed transposed
+  // (the sparse block is the shared operand). BSK_SPMM_TILE=single|pair overrides, then a registered shape
+  // configuration, then the built-in choice: the pair kernel from 512 output columns up.
+  int kind = -1, group = 0;
+  find_config(BSK_OP_SPMM_BSR, M, N, K, &kind, &group);
+  if (const char* v = getenv("BSK_SPMM_TILE")) {
+    if (strcmp(v, "single") == 0) kind = 0;
+    if (strcmp(v, "pair") == 0) kind = 1;
+  }
+  if (kind < 0 || kind > 1) kind = N >= kBsrPairTileN ? 1 : 0;
+  if (st->bsr_pair_clusters <= 0) kind = 0;
   CUtensorMap ta, tb;
-  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, vals, 128, (uint64_t)nnzb * 128, 256, 64, 128,
-                        "A values"))
+  if (int rc = make_map(&ta, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, vals, 128, (uint64_t)nnzb * 128, 256, 64,
+                        kind ? 64 : 128, "A values"))
     return rc;
   if (int rc = make_map(&tb, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, B, N, K, ldb * 2, 64, 64, "B")) return rc;
   GemmArgs a{};
   a.M = M;
   a.N = N;
   a.num_m_tiles = row_end - row_begin;
-  a.num_n_tiles = (N + kGemmBN - 1) / kGemmBN;
+  a.num_n_tiles = (N + (kind ? kBsrPairTileN : kGemmBN) - 1) / (kind ? kBsrPairTileN : kGemmBN);
   a.num_k_blocks = 0;
-  {
-    int kind_unused, group;
-    launch_config(BSK_OP_SPMM_BSR, M, N, K, false, &kind_unused, &group);
-    a.group_m = resolve_group(group, a.num_m_tiles, 0, 0);
-  }
+  a.group_m = resolve_group(group, a.num_m_tiles, 0, 0);
   a.k_splits = 1;
   a.kb_per_split = a.num_k_blocks;
   a.out = C;
@@ -965,6 +976,11 @@ int bsk_spmm_bsr_f16f32(const int32_t* row_ptr, const int32_t* col_idx, const vo
   a.err = st->err_word;
   a.timeout_ns = t_timeout_ns;
   const int tiles = a.num_m_tiles * a.num_n_tiles;
+  if (kind == 1) {
+    const int clusters = tiles < st->bsr_pair_clusters ? tiles : st->bsr_pair_clusters;
+    spmm_bsr_pair_sm100_kernel<<<2 * clusters, kPairThreads, kBsrPairSmemBytes, s>>>(ta, tb, a);
+    return launch_status("spmm_bsr pair launch");
+  }
   const int grid = tiles < st->sm_count ? tiles : st->sm_count;
   gemm_sm100_kernel<2, Mainloop::Bsr, Epi::F32><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
   return launch_status("spmm_bsr launch");

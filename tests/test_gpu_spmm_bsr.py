@@ -1,5 +1,6 @@
 """BSR x dense SpMM through the C ABI vs the reference's torch path (torch.sparse.mm on fp32 BSR) and the
-fp64 block restatement. Tolerance: normwise relative error <= 1e-3; index handling exact."""
+fp64 block restatement. Tolerance: normwise relative error <= 1e-3; index handling exact. Every case runs on both
+kernels: the one-CTA 128 x 256 tile and the CTA-pair 128 x 512 transposed tile (BSK_SPMM_TILE)."""
 import pytest
 import torch
 
@@ -9,6 +10,12 @@ from periodicdent42_b200 import workloads as wl
 
 pytestmark = pytest.mark.gpu
 TOL = 1e-3
+
+
+@pytest.fixture(autouse=True, params=["single", "pair"])
+def tile(request, monkeypatch):
+    monkeypatch.setenv("BSK_SPMM_TILE", request.param)
+    return request.param
 
 
 def _case(Mb, Kb, N, per_row, seed, empty_rows=()):
@@ -40,7 +47,7 @@ def _run(crow, col, vals, B, M, row_begin=0, row_end=None, C=None):
 
 
 @pytest.mark.parametrize("Mb,Kb,N,per_row", [(2, 2, 256, 1), (4, 8, 512, 3), (3, 5, 200, 5), (8, 8, 1024, 8),
-                                             (16, 16, 520, 4)])
+                                             (16, 16, 520, 4), (5, 12, 1544, 6), (3, 4, 24, 2)])
 def test_bsr_shapes(no_device_error, Mb, Kb, N, per_row):
     crow, col, vals, B = _case(Mb, Kb, N, per_row, Mb * 100 + N)
     M, K = Mb * 128, Kb * 128
