@@ -99,8 +99,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
       const uint32_t s0 = ptx::smem_u32(smem);
       const uint32_t full0 = ptx::smem_u32(full), empty0 = ptx::smem_u32(empty);
       const uint32_t full0_leader = ptx::mapa_shared(full0, 0);
-      const uint64_t pol_a = (BSK_BSR_PAIR_HINTS & 2) ? ptx::l2_policy_evict_last() : 0;
-      const uint64_t pol_b = (BSK_BSR_PAIR_HINTS & 4) ? ptx::l2_policy_evict_last() : 0;
+      const uint64_t pol_a = (BSK_BSR_PAIR_HINTS & 2) ? ptx::policy_evict_last() : 0;
+      const uint64_t pol_b = (BSK_BSR_PAIR_HINTS & 4) ? ptx::policy_evict_last() : 0;
       for (int unit = pair; unit < num_units && ok; unit += npairs) {
         int mt, nt;
         gemm_tile_coords(unit, a, mt, nt);

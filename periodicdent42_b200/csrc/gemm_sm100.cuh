@@ -68,6 +68,19 @@ struct GemmArgs {
 };
 
 __device__ __forceinline__ void gemm_tile_coords(int tile, const GemmArgs& a, int& mt, int& nt) {
+#if BSK_RASTER_NMAJOR
+  if (a.row_ptr == nullptr) {
+    const int gn_ = a.group_m < a.num_n_tiles ? a.group_m : a.num_n_tiles;
+    const int per = gn_ * a.num_m_tiles;
+    const int gg = tile / per;
+    const int fn = gg * gn_;
+    const int gnn = min(a.num_n_tiles - fn, gn_);
+    const int tt = tile - gg * per;
+    nt = fn + tt % gnn;
+    mt = tt / gnn;
+    return;
+  }
+#endif
   const int per_group = a.group_m * a.num_n_tiles;
   const int g = tile / per_group;
   const int first_m = g * a.group_m;

@@ -356,7 +356,7 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
-// The same load with an L2 eviction-priority policy (from l2_policy_evict_last / _first) attached.
+// The same load with an L2 eviction-priority policy (from policy_evict_last / _first) attached.
 __device__ __forceinline__ void tma_load_2d_pair_hint(uint32_t dst, const CUtensorMap* m, uint32_t cluster_bar,
                                                       int32_t x, int32_t y, uint64_t policy) {
   asm volatile(
@@ -364,19 +364,6 @@ __device__ __forceinline__ void tma_load_2d_pair_hint(uint32_t dst, const CUtens
       " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(cluster_bar), "r"(x), "r"(y), "l"(policy)
       : "memory");
-}
-
-// L2 cache policies for the whole accessed range (fraction 1.0): keep the lines longer than normal
-// (evict_last) or give them up first (evict_first).
-__device__ __forceinline__ uint64_t l2_policy_evict_last() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-  return p;
-}
-__device__ __forceinline__ uint64_t l2_policy_evict_first() {
-  uint64_t p;
-  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-  return p;
 }
 
 // TMEM management for a CTA pair: one warp of EACH CTA of the pair executes these together.
