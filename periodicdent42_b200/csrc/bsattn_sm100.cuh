@@ -299,6 +299,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       uint32_t p_uses[2] = {0, 0};
       bool ok = true;
       const uint32_t sQa = ptx::smem_u32(sQ), kv0 = ptx::smem_u32(sKV);
+      const uint64_t qdesc0 = ptx::smem_desc(sQa, 16, 1024);              // Q, K: K-major
+      const uint64_t kvdesc_k0 = ptx::smem_desc(kv0, 16, 1024);
+      const uint64_t kvdesc_v0 = ptx::smem_desc(kv0, kAttnChunk, 1024);   // V: MN-major, 64-column slabs
       auto take_slot = [&](uint32_t site) -> uint32_t {
         if (!wait_bounded(ptx::smem_u32(&kv_full[slot]), slot_phase, ctl, site)) return 0xFFFFFFFFu;
         return slot;
@@ -311,12 +314,12 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t sl = take_slot(11);
         if (sl == 0xFFFFFFFFu) return false;
         ptx::tc_fence_after();
-        const uint32_t kA = kv0 + sl * kAttnTile, qA = sQa + x * kAttnTile;
+        // Descriptors differ from the ring's base descriptor only in the start address: add (bytes >> 4).
+        const uint64_t qd = qdesc0 + ((x * kAttnTile) >> 4), kd = kvdesc_k0 + ((sl * kAttnTile) >> 4);
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) {  // K = D in steps of 16: 4 steps per 64-column chunk
-          const uint32_t off = (k >> 2) * kAttnChunk + (k & 3) * 32;
-          ptx::mma_f16_ss(tmem_base + x * 128, ptx::smem_desc(qA + off, 16, 1024), ptx::smem_desc(kA + off, 16, 1024),
-                          IDESC_S, k != 0);
+          const uint32_t off = ((k >> 2) * kAttnChunk + (k & 3) * 32) >> 4;
+          ptx::mma_f16_ss(tmem_base + x * 128, qd + off, kd + off, IDESC_S, k != 0);
         }
         release_slot(sl);
         ptx::mma_commit(ptx::smem_u32(&s_full[x]));
@@ -328,11 +331,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const uint32_t sl = take_slot(13);
         if (sl == 0xFFFFFFFFu) return false;
         ptx::tc_fence_after();
-        const uint32_t vA = kv0 + sl * kAttnTile;
+        const uint64_t vd = kvdesc_v0 + ((sl * kAttnTile) >> 4);
 #pragma unroll
         for (int k = 0; k < 8; ++k)  // K step k: P columns [8k, 8k+8) hold kv positions [16k, 16k+16)
-          ptx::mma_f16_ts(tmem_base + 256 + x * 128, tmem_base + x * 128 + 8 * k,
-                          ptx::smem_desc(vA + k * 2048, kAttnChunk, 1024), IDESC_PV, (first && k == 0) ? 0u : 1u);
+          ptx::mma_f16_ts(tmem_base + 256 + x * 128, tmem_base + x * 128 + 8 * k, vd + ((k * 2048) >> 4), IDESC_PV,
+                          (first && k == 0) ? 0u : 1u);
         release_slot(sl);
         if (last) ptx::mma_commit(ptx::smem_u32(&o_done[x]));
         return true;
