@@ -49,7 +49,7 @@ def parse_args():
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     p.add_argument("--ops", default="dense,fp8,bsr,attn,attn_bwd,convert,bsr_bsr",
-                   help="comma list; dense is the headline")
+                   help="comma list; dense is the headline; opt-in: autotune, cublas (same-box library yardstick)")
     p.add_argument("--dense-mode", choices=["nshard", "splitk", "splitk_nccl"], default="nshard",
                    help="nshard: N-sharded, no communication; splitk: K split across ranks, reduce-scatter fused "
                         "into the GEMM (peer-memory epilogue); splitk_nccl: K split + NCCL reduce_scatter")
@@ -176,7 +176,9 @@ class Clocks:
                     reasons.add(n)
         sm = [self._f(r[2]) for _, r in rows]
         return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm), "sm_max_mhz": max(self._f(r[3]) for _, r in rows),
-                "power_w_max": max(self._f(r[4]) for _, r in rows), "samples": len(rows), "reasons": sorted(reasons)}
+                "power_w_max": max(self._f(r[4]) for _, r in rows),
+                "power_w_median": statistics.median(self._f(r[4]) for _, r in rows), "samples": len(rows),
+                "reasons": sorted(reasons)}
 
     def stop(self, headline="dense"):
         if self.proc is None:
@@ -229,6 +231,25 @@ def time_region(ctx: Ctx, fn, steps: int, warmup: int, name: str = ""):
 
 
 # ----------------------------------------------------------------------------------------- dense GEMM
+def bench_cublas_dense(ctx: Ctx, args, res: dict):
+    """Same-box yardstick, opt-in (`--ops dense,cublas`): the library GEMM (cuBLAS through torch.matmul, fp16 in,
+    fp16 out) on the dense workload's shape and inputs. Not the product path. Its timed region gets its own clock
+    and power record, so a gap to the dense line splits into work per SM clock and clock (power) effects."""
+    cfg = dense_cfg(args)
+    A, Bt = wl.dense_inputs(cfg, ctx.dev)
+    n0, n1 = sharding.dense_nshard(cfg.N, ctx.world, ctx.rank)
+    Bt_r = Bt[n0:n1]
+    C = torch.empty(cfg.M, n1 - n0, dtype=torch.float16, device=ctx.dev)
+
+    def step():
+        torch.matmul(A, Bt_r.t(), out=C)
+    ms = time_region(ctx, step, args.steps, args.warmup, "cublas_dense")
+    res["cublas_dense"] = {"ms": ms, "tflops": cfg.flops / (ms * 1e-3) / 1e12,
+                           "what": "torch.matmul fp16 x fp16 -> fp16 (cuBLAS), same shape and inputs, same steps"}
+    del A, Bt, Bt_r, C
+    torch.cuda.empty_cache()
+
+
 def dense_cfg(args) -> wl.DenseCfg:
     if args.shape:
         M, N, K = (int(x) for x in args.shape.split(","))
@@ -622,7 +643,7 @@ def main():
         for op in ops:
             {"dense": bench_dense, "fp8": bench_fp8, "bsr": bench_bsr, "attn": bench_attn,
              "convert": bench_convert, "bsr_bsr": bench_bsr_bsr, "autotune": bench_autotune,
-             "attn_bwd": bench_attn_bwd}[op](ctx, args, res)
+             "attn_bwd": bench_attn_bwd, "cublas": bench_cublas_dense}[op](ctx, args, res)
     finally:
         clk = clocks.stop() if clocks else None
     err_word = _capi.device_error()
@@ -683,6 +704,17 @@ def main():
                                     "scaling": r["scaling"]}
         if res.get("autotune"):
             opsum["autotune_dense"] = res["autotune"]
+        if "cublas_dense" in res:  # work per SM clock of both timed regions (median SM clock of each region)
+            r = dict(res["cublas_dense"])
+            regions = (clk or {}).get("per_region", {})
+            sm_count = torch.cuda.get_device_properties(ctx.dev).multi_processor_count
+            for name, tf in (("cublas_dense", r["tflops"]), ("dense", d["tflops"] if d else None)):
+                reg = regions.get(name)
+                if reg and tf:
+                    r[f"{name}_sm_mhz"] = reg["sm_mhz"]
+                    r[f"{name}_power_w_median"] = reg["power_w_median"]
+                    r[f"{name}_flop_per_clk_per_sm"] = tf / ctx.world * 1e12 / (reg["sm_mhz"] * 1e6 * sm_count)
+            opsum["cublas_dense"] = r
         line["ops"] = opsum
         line["device_error_word"] = err_word
         print(json.dumps(line), flush=True)
