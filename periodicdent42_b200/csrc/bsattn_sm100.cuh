@@ -302,42 +302,57 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       const uint64_t qdesc0 = ptx::smem_desc(sQa, 16, 1024);              // Q, K: K-major
       const uint64_t kvdesc_k0 = ptx::smem_desc(kv0, 16, 1024);
       const uint64_t kvdesc_v0 = ptx::smem_desc(kv0, kAttnChunk, 1024);   // V: MN-major, 64-column slabs
-      auto take_slot = [&](uint32_t site) -> uint32_t {
-        if (!wait_bounded(ptx::smem_u32(&kv_full[slot]), slot_phase, ctl, site)) return 0xFFFFFFFFu;
-        return slot;
-      };
-      auto release_slot = [&](uint32_t sl) {
-        ptx::mma_commit(ptx::smem_u32(&kv_empty[sl]));
+      auto advance = [&]() {
         if (++slot == kAttnKVSlots) { slot = 0; slot_phase ^= 1; }
       };
-      auto issue_s = [&](int x) -> bool {  // S_x = Q_x K^T (after PV_x of the previous block, in issue order)
-        const uint32_t sl = take_slot(11);
-        if (sl == 0xFFFFFFFFu) return false;
-        ptx::tc_fence_after();
-        // Descriptors differ from the ring's base descriptor only in the start address: add (bytes >> 4).
+      // A shared-memory access (an mbarrier poll included) issued after tcgen05.mma waits until the queued MMAs
+      // have been handed to the tensor pipe, so the pipe runs dry during every poll that follows an MMA group.
+      // The barrier waits of a block are therefore made back to back, before its MMAs: PV_x(j) and S_x(j+1)
+      // go out as one group of 16 behind one burst of waits (P_x(j), V_x(j), K_x(j+1)).
+      auto s_mmas = [&](int x, uint32_t sl) {  // S_x = Q_x K^T from ring slot sl
         const uint64_t qd = qdesc0 + ((x * kAttnTile) >> 4), kd = kvdesc_k0 + ((sl * kAttnTile) >> 4);
 #pragma unroll
         for (int k = 0; k < kD / 16; ++k) {  // K = D in steps of 16: 4 steps per 64-column chunk
           const uint32_t off = ((k >> 2) * kAttnChunk + (k & 3) * 32) >> 4;
           ptx::mma_f16_ss(tmem_base + x * 128, qd + off, kd + off, IDESC_S, k != 0);
         }
-        release_slot(sl);
+      };
+      auto issue_s = [&](int x) -> bool {  // S_x(0) of a row
+        const uint32_t sk = slot;
+        if (!wait_bounded(ptx::smem_u32(&kv_full[sk]), slot_phase, ctl, 11)) return false;
+        advance();
+        ptx::tc_fence_after();
+        s_mmas(x, sk);
+        ptx::mma_commit(ptx::smem_u32(&kv_empty[sk]));
         ptx::mma_commit(ptx::smem_u32(&s_full[x]));
         return true;
       };
-      auto issue_pv = [&](int x, bool first, bool last) -> bool {  // O_x += P_x (TMEM) V
+      // O_x += P_x(j) V_x(j) (P from TMEM), then (next) S_x(j+1), which may overwrite the P columns: in issue order.
+      auto issue_pv_s = [&](int x, bool first, bool last, bool next) -> bool {
         if (!wait_bounded(ptx::smem_u32(&p_full[x]), p_uses[x] & 1, ctl, 12)) return false;
         ++p_uses[x];
-        const uint32_t sl = take_slot(13);
-        if (sl == 0xFFFFFFFFu) return false;
+        const uint32_t sv = slot;
+        if (!wait_bounded(ptx::smem_u32(&kv_full[sv]), slot_phase, ctl, 13)) return false;
+        advance();
+        uint32_t sk = 0;
+        if (next) {
+          sk = slot;
+          if (!wait_bounded(ptx::smem_u32(&kv_full[sk]), slot_phase, ctl, 11)) return false;
+          advance();
+        }
         ptx::tc_fence_after();
-        const uint64_t vd = kvdesc_v0 + ((sl * kAttnTile) >> 4);
+        const uint64_t vd = kvdesc_v0 + ((sv * kAttnTile) >> 4);
 #pragma unroll
         for (int k = 0; k < 8; ++k)  // K step k: P columns [8k, 8k+8) hold kv positions [16k, 16k+16)
           ptx::mma_f16_ts(tmem_base + 256 + x * 128, tmem_base + x * 128 + 8 * k, vd + ((k * 2048) >> 4), IDESC_PV,
                           (first && k == 0) ? 0u : 1u);
-        release_slot(sl);
+        ptx::mma_commit(ptx::smem_u32(&kv_empty[sv]));
         if (last) ptx::mma_commit(ptx::smem_u32(&o_done[x]));
+        if (next) {
+          s_mmas(x, sk);
+          ptx::mma_commit(ptx::smem_u32(&kv_empty[sk]));
+          ptx::mma_commit(ptx::smem_u32(&s_full[x]));
+        }
         return true;
       };
       for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
@@ -348,14 +363,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ok = wait_bounded(ptx::smem_u32(q_full), q_phase, ctl, 14);
         if (!ok) break;
         q_phase ^= 1;
+        // Ring order (the producer's): K_A(0), K_B(0), then per j: V_A(j), K_A(j+1), V_B(j), K_B(j+1).
         if (A.n > 0) ok = ok && issue_s(0);
         if (B.n > 0) ok = ok && issue_s(1);
         const int n = max(A.n, B.n);
         for (int j = 0; j < n && ok; ++j) {
-          if (j < A.n) ok = ok && issue_pv(0, j == 0, j + 1 == A.n);
-          if (j + 1 < A.n) ok = ok && issue_s(0);
-          if (j < B.n) ok = ok && issue_pv(1, j == 0, j + 1 == B.n);
-          if (j + 1 < B.n) ok = ok && issue_s(1);
+          if (j < A.n) ok = ok && issue_pv_s(0, j == 0, j + 1 == A.n, j + 1 < A.n);
+          if (j < B.n) ok = ok && issue_pv_s(1, j == 0, j + 1 == B.n, j + 1 < B.n);
         }
         if (ok) ptx::mma_commit(ptx::smem_u32(q_empty));
       }
