@@ -776,18 +776,18 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           if (!ok) break;
         }
         for (int t = 0; t < n && ok; ++t) {
+          // The next slot is taken in the same burst of waits as P^T (a poll after queued MMAs drains the pipe).
           ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(p_full), p_cnt & 1, ctl, 12);
           if (!ok) break;
           ++p_cnt;
-          ptx::tc_fence_after();
-          issue_dv(cur, t == 0);
           uint32_t nxt = 0xFFFFFFFFu;
           if (t + 1 < n) {
             nxt = take(11);
             if (nxt == 0xFFFFFFFFu) { ok = false; break; }
-            ptx::tc_fence_after();
-            issue_s(nxt);
           }
+          ptx::tc_fence_after();
+          issue_dv(cur, t == 0);
+          if (t + 1 < n) issue_s(nxt);
           ok = wait_bounded_hint<kBwdSuspendNs>(ptx::smem_u32(ds_full), ds_cnt & 1, ctl, 13);
           if (!ok) break;
           ++ds_cnt;
