@@ -32,6 +32,11 @@ constexpr int kAttnBlk = 128;
 constexpr int kAttnThreads = 384;
 constexpr int kAttnChunk = kAttnBlk * 64 * 2;  // 16 KB: 128 rows x 64 columns (one 128-B swizzle atom wide)
 constexpr int kAttnKVSlots = 5;
+// Eighths of the exponentials computed on the FMA pipe (ex2_poly2) instead of the MUFU.
+#ifndef BSK_ATTN_POLY_EIGHTHS
+#define BSK_ATTN_POLY_EIGHTHS 2
+#endif
+constexpr int kAttnPolyEighths = BSK_ATTN_POLY_EIGHTHS;
 
 // Head dimension D (64 or 128) and element type (fp16 or bf16) of one instantiation.
 template <bool kF16, int kD>
@@ -451,7 +456,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         for (int i = 0; i < 128; i += 2) {
           float t0, t1, e0, e1;
           f2_unpack(f2_fma(f2_pack(v[i], v[i + 1]), c2, nm2), t0, t1);
-          if ((i & 7) == 6) {
+          if (((i >> 1) & 7) >= 8 - kAttnPolyEighths) {
             ex2_poly2(t0, t1, e0, e1);
           } else {
             e0 = ex2_approx(t0);
