@@ -139,7 +139,7 @@ void init_device(DeviceState& st, int dev) {
       allow_smem(gemm_sm100_kernel<2, Mainloop::Dense, Epi::F32>, kGemmSmemBytes),
       allow_smem(gemm_sm100_kernel<1, Mainloop::Dense, Epi::BF16Scaled>, kGemmSmemBytes),
       allow_smem(gemm_sm100_kernel<2, Mainloop::Bsr, Epi::F32>, kGemmSmemBytes),
-      allow_smem(gemm_sm100_kernel<2, Mainloop::BsrBsr, Epi::F32>, kGemmSmemBytes),
+      allow_smem(gemm_sm100_kernel<2, Mainloop::BsrBsr, Epi::F32>, kGemmBsrBsrSmemBytes),
       allow_smem(bsattn_sm100_kernel<false, 128>, AttnShape<false, 128>::kSmemBytes),
       allow_smem(bsattn_sm100_kernel<false, 64>, AttnShape<false, 64>::kSmemBytes),
       allow_smem(bsattn_sm100_kernel<true, 128>, AttnShape<true, 128>::kSmemBytes),
@@ -1045,11 +1045,19 @@ int bsk_spmm_bsr_bsr_f16f32(const int32_t* a_row_ptr, const int32_t* a_col_idx, 
   a.b_row_ptr = b_row_ptr;
   a.b_col_idx = b_col_idx;
   a.b_nnzb = b_nnzb;
+  // B's block map staged in shared memory when it fits (map entries and kb_count + 1 row pointers); the
+  // environment variable BSK_BSRBSR_TABLE=0 keeps the binary searches in global memory.
+  {
+    const int nbc = N / 128;
+    const char* v = getenv("BSK_BSRBSR_TABLE");
+    const bool off = v && strcmp(v, "0") == 0;
+    a.b_nbc = (!off && a.kb_count + 1 <= 256 && (int64_t)a.kb_count * nbc <= kBsrTableMax) ? nbc : 0;
+  }
   a.err = st->err_word;
   a.timeout_ns = t_timeout_ns;
   const int tiles = a.num_m_tiles * a.num_n_tiles;
   const int grid = tiles < st->sm_count ? tiles : st->sm_count;
-  gemm_sm100_kernel<2, Mainloop::BsrBsr, Epi::F32><<<grid, kGemmThreads, kGemmSmemBytes, s>>>(ta, tb, a);
+  gemm_sm100_kernel<2, Mainloop::BsrBsr, Epi::F32><<<grid, kGemmThreads, kGemmBsrBsrSmemBytes, s>>>(ta, tb, a);
   return launch_status("spmm_bsr_bsr launch");
 }
 

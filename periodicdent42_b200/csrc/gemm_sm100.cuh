@@ -28,6 +28,10 @@ constexpr int kGemmAStage = kGemmBM * kGemmRowBytes;  // 16 KB
 constexpr int kGemmBStage = kGemmBN * kGemmRowBytes;  // 32 KB
 constexpr int kGemmTmemCols = 512;
 constexpr int kGemmSmemBytes = 1024 /*align slack*/ + kGemmStages * (kGemmAStage + kGemmBStage) + 256;
+// BSR x BSR: B's block map (block-row x block-column -> stored block, -1 absent) staged in shared memory after the
+// barriers, up to this many entries; larger maps fall back to a binary search per lookup.
+constexpr int kBsrTableMax = 8192;
+constexpr int kGemmBsrBsrSmemBytes = kGemmSmemBytes + kBsrTableMax * 4 + 1024;  // + staged row pointers
 
 enum class Mainloop : int { Dense = 0, Bsr = 1, BsrBsr = 2 };
 // F32PeerRows: fp32 partial rows stored into their owner rank's receive slot (split-K reduce-scatter).
@@ -63,6 +67,8 @@ struct GemmArgs {
   const int* b_row_ptr;        // BSR x BSR only: B's block-row pointer (K/128 + 1 entries, int32)
   const int* b_col_idx;        // BSR x BSR only: B's block columns, ascending within each block-row
   int b_nnzb;                  // BSR x BSR only: B's stored blocks (a load at block b_nnzb reads zero fill)
+  int b_nbc;                   // BSR x BSR only: B's block columns when its block map is staged in shared
+                               // memory (kb_count * b_nbc <= kBsrTableMax), else 0 (binary search in global)
   uint32_t* err;
   uint64_t timeout_ns;
 };
@@ -100,9 +106,10 @@ __device__ __forceinline__ bool bsr_row_range(const GemmArgs& a, int r, int& j0,
   return j0 == p0 && j1 == p1;
 }
 
-// Position of B block (kb, jc) in B's BSR arrays, or -1: binary search of the ascending block-row kb (row
-// pointers clamped to [0, b_nnzb]).
-__device__ __forceinline__ int bsr_b_find(const GemmArgs& a, int kb, int jc) {
+// Position of B block (kb, jc) in B's BSR arrays, or -1: from the shared-memory block map when it is staged,
+// else a binary search of the ascending block-row kb (row pointers clamped to [0, b_nnzb]).
+__device__ __forceinline__ int bsr_b_find(const GemmArgs& a, const int* tab, int kb, int jc) {
+  if (tab) return jc < a.b_nbc ? tab[kb * a.b_nbc + jc] : -1;
   int lo = min(max(__ldg(&a.b_row_ptr[kb]), 0), a.b_nnzb);
   int hi = min(max(__ldg(&a.b_row_ptr[kb + 1]), lo), a.b_nnzb);
   const int end = hi;
@@ -116,23 +123,24 @@ __device__ __forceinline__ int bsr_b_find(const GemmArgs& a, int kb, int jc) {
 // BSR x BSR: for A's stored block j (block column kb = col_idx[j]) and the output tile whose first block column
 // is jc, the B blocks (kb, jc) and (kb, jc + 1). Returns false when neither exists or kb is out of range (the
 // A block then contributes nothing to the tile).
-__device__ __forceinline__ bool bsrbsr_pair(const GemmArgs& a, int j, int jc, int& p0, int& p1) {
+__device__ __forceinline__ bool bsrbsr_pair(const GemmArgs& a, const int* tab, int j, int jc, int& p0, int& p1) {
   const int kb = __ldg(&a.col_idx[j]);
   p0 = p1 = -1;
   if (kb < 0 || kb >= a.kb_count) return false;
-  p0 = bsr_b_find(a, kb, jc);
-  p1 = bsr_b_find(a, kb, jc + 1);
+  p0 = bsr_b_find(a, tab, kb, jc);
+  p1 = bsr_b_find(a, tab, kb, jc + 1);
   return p0 >= 0 || p1 >= 0;
 }
 
 // Warp-collective: how many of A's blocks [j0, j1) meet B block (kb, jc) (*c0) and (kb, jc + 1) (*c1), i.e. how
 // many MMAs each 128-column half of the tile receives. Same answer on every lane and in every role of the CTA.
-__device__ __forceinline__ void bsrbsr_half_counts(const GemmArgs& a, int j0, int j1, int jc, int* c0, int* c1) {
+__device__ __forceinline__ void bsrbsr_half_counts(const GemmArgs& a, const int* tab, int j0, int j1, int jc, int* c0,
+                                                   int* c1) {
   const int lane = threadIdx.x & 31;
   int n0 = 0, n1 = 0;
   for (int jb = j0; jb < j1; jb += 32) {
     int p0 = -1, p1 = -1;
-    if (jb + lane < j1) bsrbsr_pair(a, jb + lane, jc, p0, p1);
+    if (jb + lane < j1) bsrbsr_pair(a, tab, jb + lane, jc, p0, p1);
     n0 += __popc(__ballot_sync(0xFFFFFFFFu, p0 >= 0));
     n1 += __popc(__ballot_sync(0xFFFFFFFFu, p1 >= 0));
   }
@@ -218,6 +226,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     ptx::tmem_alloc(ptx::smem_u32(tmem_holder), kGemmTmemCols);
     ptx::tmem_relinquish();
   }
+  // BSR x BSR: stage B's block map in shared memory (all threads; one global read per stored block).
+  const int* btab = nullptr;
+  if constexpr (kML == Mainloop::BsrBsr) {
+    if (a.b_nbc > 0) {
+      int* tab = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(bars) + 256);
+      int* rp = tab + kBsrTableMax;  // B row pointers, clamped to [0, b_nnzb]
+      const int entries = a.kb_count * a.b_nbc;
+      for (int i = threadIdx.x; i < entries; i += blockDim.x) tab[i] = -1;
+      for (int i = threadIdx.x; i <= a.kb_count; i += blockDim.x) rp[i] = min(max(__ldg(&a.b_row_ptr[i]), 0), a.b_nnzb);
+      __syncthreads();
+      for (int p = threadIdx.x; p < a.b_nnzb; p += blockDim.x) {
+        int lo = 0, hi = a.kb_count;  // block-row of stored block p: the last kb with rp[kb] <= p
+        while (lo < hi) {
+          const int mid = (lo + hi + 1) >> 1;
+          if (rp[mid] <= p) lo = mid; else hi = mid - 1;
+        }
+        const int col = __ldg(&a.b_col_idx[p]);
+        if (lo < a.kb_count && p < rp[lo + 1] && col >= 0 && col < a.b_nbc) tab[lo * a.b_nbc + col] = p;
+      }
+      btab = tab;
+    }
+  }
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -259,7 +289,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           int p0 = -1, p1 = -1;
           bool on = false;
           if (jb + lane < j1) {
-            on = bsrbsr_pair(a, jb + lane, jc, p0, p1);
+            on = bsrbsr_pair(a, btab, jb + lane, jc, p0, p1);
             const int kb = __ldg(&a.col_idx[jb + lane]);
             if (kb < 0 || kb >= a.kb_count) atomicCAS(a.err, 0u, kErrBounds | (KID << 8) | (8u << 16));
           }
@@ -367,7 +397,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       // B block that exists (column half 0 <- (kb, jc), half 1 <- (kb, jc + 1)).
       for (int jb = j0; jb < j1 && ok; jb += 32) {
         int p0 = -1, p1 = -1;
-        if (jb + lane < j1) bsrbsr_pair(a, jb + lane, jc, p0, p1);
+        if (jb + lane < j1) bsrbsr_pair(a, btab, jb + lane, jc, p0, p1);
         const unsigned h0 = __ballot_sync(0xFFFFFFFFu, p0 >= 0), h1 = __ballot_sync(0xFFFFFFFFu, p1 >= 0);
         if (lane == 0) {
           unsigned live = h0 | h1;
@@ -488,7 +518,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         int j0, j1;
         bsr_row_range(a, r, j0, j1);
         if constexpr (kML == Mainloop::BsrBsr)
-          bsrbsr_half_counts(a, j0, j1, nt * kGemmBN / 128, &nk, &nk1);
+          bsrbsr_half_counts(a, btab, j0, j1, nt * kGemmBN / 128, &nk, &nk1);
         else
           nk = nk1 = j1 - j0;
       }

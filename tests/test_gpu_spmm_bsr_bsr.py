@@ -1,6 +1,7 @@
 """BSR x BSR SpMM (sparse B) through the C ABI, the reference-signature launcher and the public sparse_mm, against
 the fp64 recompute of the dense operands (the oracle: A.to_dense() @ B.to_dense()).
-Tolerance: normwise relative error <= 1e-3 against fp64 (the fp16 bar of the BSR path)."""
+Tolerance: normwise relative error <= 1e-3 against fp64 (the fp16 bar of the BSR path). Every case runs with B's
+block map staged in shared memory and with the binary searches in global memory (BSK_BSRBSR_TABLE)."""
 import ctypes
 
 import pytest
@@ -15,6 +16,12 @@ pytestmark = pytest.mark.gpu
 TOL = 1e-3
 
 
+@pytest.fixture(autouse=True, params=["table", "search"])
+def b_lookup(request, monkeypatch):
+    monkeypatch.setenv("BSK_BSRBSR_TABLE", "1" if request.param == "table" else "0")
+    return request.param
+
+
 def _bsr(Mb, Kb, per_row, seed, dev):
     g = torch.Generator().manual_seed(seed)
     crow, col = wl.bsr_pattern(Mb, Kb, per_row, g)
@@ -27,7 +34,7 @@ def _dense(crow, col, vals, M, K):
 
 
 @pytest.mark.parametrize("Mb,Kb,Nb,a_per,b_per", [(4, 6, 4, 2, 1), (8, 8, 8, 3, 2), (6, 4, 3, 4, 1), (16, 16, 12, 5, 3),
-                                                  (3, 5, 2, 5, 2)])
+                                                  (3, 5, 2, 5, 2), (2, 300, 2, 4, 1)])
 def test_bsr_bsr_matches_dense_oracle(no_device_error, cuda_dev, Mb, Kb, Nb, a_per, b_per):
     M, K, N = Mb * 128, Kb * 128, Nb * 128
     arp, aci, av = _bsr(Mb, Kb, a_per, Mb * 7 + Kb, cuda_dev)
