@@ -26,6 +26,23 @@ namespace bsk {
 
 constexpr uint32_t kKidBsAttnBwd = 7;
 constexpr uint32_t kBwdSuspendNs = 2000;  // suspend hint of the compute and MMA waits (woken at completion)
+// Eighths of the exponentials of P computed on the FMA pipe (ex2_poly2) instead of the MUFU, in both passes.
+#ifndef BSK_BWD_POLY_EIGHTHS
+#define BSK_BWD_POLY_EIGHTHS 2
+#endif
+constexpr int kBwdPolyEighths = BSK_BWD_POLY_EIGHTHS;
+
+// exp2 of a packed pair on the MUFU, or on the FMA pipe when `poly` (a compile-time choice after unrolling).
+__device__ __forceinline__ uint64_t f2_ex2_split(uint64_t t, bool poly) {
+  float a, b;
+  f2_unpack(t, a, b);
+  if (poly) {
+    float ya, yb;
+    ex2_poly2(a, b, ya, yb);
+    return f2_pack(ya, yb);
+  }
+  return f2_pack(ex2_approx(a), ex2_approx(b));
+}
 
 struct AttnBwdArgs {
   const void* dO;        // [B*H*S, D]
@@ -237,11 +254,6 @@ __device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
   uint64_t r;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
   return r;
-}
-__device__ __forceinline__ uint64_t f2_ex2(uint64_t t) {
-  float a, b;
-  f2_unpack(t, a, b);
-  return f2_pack(ex2_approx(a), ex2_approx(b));
 }
 
 template <int kD>
@@ -517,7 +529,9 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
 #pragma unroll
         for (int i = 0; i < 64; i += 2) {
           float p0, p1;
-          f2_unpack(f2_ex2(f2_fma(f2_pack(__uint_as_float(pv[i]), __uint_as_float(pv[i + 1])), c2, off2)), p0, p1);
+          f2_unpack(f2_ex2_split(f2_fma(f2_pack(__uint_as_float(pv[i]), __uint_as_float(pv[i + 1])), c2, off2),
+                                 ((i >> 1) & 7) >= 8 - kBwdPolyEighths),
+                    p0, p1);
           if (diag && 64 * x + i > r) p0 = 0.0f;      // key position above the query row
           if (diag && 64 * x + i + 1 > r) p1 = 0.0f;
           pv[i] = __float_as_uint(p0);
@@ -855,10 +869,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int i = 0; i < 32; i += 4) {
             const float4 o = *reinterpret_cast<const float4*>(off_s + 32 * cc + i);
             float p0, p1, p2, p3;
-            f2_unpack(f2_ex2(f2_fma(f2_pack(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), c2, f2_pack(o.x, o.y))),
+            f2_unpack(f2_ex2_split(f2_fma(f2_pack(__uint_as_float(sv[i]), __uint_as_float(sv[i + 1])), c2,
+                                          f2_pack(o.x, o.y)),
+                                   ((i >> 1) & 7) >= 8 - kBwdPolyEighths),
                       p0, p1);
-            f2_unpack(f2_ex2(f2_fma(f2_pack(__uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3])), c2,
-                                    f2_pack(o.z, o.w))),
+            f2_unpack(f2_ex2_split(f2_fma(f2_pack(__uint_as_float(sv[i + 2]), __uint_as_float(sv[i + 3])), c2,
+                                          f2_pack(o.z, o.w)),
+                                   (((i >> 1) + 1) & 7) >= 8 - kBwdPolyEighths),
                       p2, p3);
             const int col = 64 * x + 32 * cc + i;  // query position
             if (!valid) p0 = p1 = p2 = p3 = 0.0f;
