@@ -57,7 +57,8 @@ def parse_args():
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--e2e-steps", type=int, default=3)
-    p.add_argument("--tune-cache-out", action="store_true", help="write the autotune op's results as a cache file")
+    p.add_argument("--tune-cache-out", default=None, metavar="PATH",
+                   help="write the autotune op's results as a cache file at PATH")
     p.add_argument("--e2e-k-chunk", type=int, default=0, help="K per streamed chunk of the e2e GEMM (0 = auto)")
     p.add_argument("--op-steps", type=int, default=20, help="timed steps of the fp8 / bsr / attn measurements")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
@@ -432,8 +433,7 @@ def bench_autotune(ctx: Ctx, args, res: dict):
 
     out = []
     if ctx.rank == 0:
-        cache = at.AutotuneCache(os.path.join(os.path.dirname(os.path.abspath(__file__)), "gpurun_out",
-                                              "autotune_bench.json")) if args.tune_cache_out else None
+        cache = at.AutotuneCache(args.tune_cache_out) if args.tune_cache_out else None
         for (M, N, K) in TUNE_SHAPES:
             e = at.tune_gemm(M, N, K, warmup=3, runs=10, rounds=2, cache=cache, save=cache is not None)
             fl = 2.0 * M * N * K
