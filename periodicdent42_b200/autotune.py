@@ -24,6 +24,7 @@ from . import _capi
 
 OPS = {"gemm_f16f32": 1, "gemm_e4m3_bf16": 2, "spmm_bsr": 3, "spmm_bsr_bsr": 4}
 TILES = {-1: "policy", 0: "single_128x256", 1: "pair_256x256", 2: "pair_256x512"}
+SPMM_TILES = {-1: "policy", 0: "single_128x256", 1: "pair_128x512_transposed"}  # BSR x dense SpMM
 GROUPS = (0, 1, 2, 4, 8, 16, 32, 64)
 
 
@@ -51,9 +52,15 @@ def parse_shape_key(key: str) -> tuple[str, int, int, int]:
 
 
 def candidates(op: str, M: int, N: int, K: int) -> list[tuple[int, int]]:
-    """(tile, group_m) variants to time: every tile kind of a dense GEMM (the policy's own choice first) times
-    the rasterisation groups that differ for this many M tiles; SpMMs only vary the group."""
-    tiles = [-1, 0, 1, 2] if op in ("gemm_f16f32", "gemm_e4m3_bf16") else [-1]
+    """(tile, group_m) variants to time: every tile kind (the policy's own choice first) times the rasterisation
+    groups that differ for this many M tiles. Dense GEMMs: single 128x256, pair 256x256, pair 256x512; BSR x dense
+    SpMM: single 128x256, CTA-pair 128x512 (at least 512 output columns); BSR x BSR: the group only."""
+    if op in ("gemm_f16f32", "gemm_e4m3_bf16"):
+        tiles = [-1, 0, 1, 2]
+    elif op == "spmm_bsr":
+        tiles = [-1, 0, 1] if N >= 512 else [-1]
+    else:
+        tiles = [-1]
     out = []
     for t in tiles:
         rows = 128 if t == 0 or (t == -1 and M <= 128) or op.startswith("spmm") else 256
@@ -168,7 +175,7 @@ def tune(op: str, M: int, N: int, K: int, run: Callable[[], None], variants: Opt
     default_ms = best.get((-1, 0))
     best_ms, tile, group = min(results)
     register(op, M, N, K, tile, group)
-    entry = {"tile": tile, "tile_name": TILES[tile], "group_m": group, "ms": best_ms, "default_ms": default_ms,
+    entry = {"tile": tile, "tile_name": (SPMM_TILES if op == "spmm_bsr" else TILES)[tile], "group_m": group, "ms": best_ms, "default_ms": default_ms,
              "variants": len(results), "warmup": warmup, "runs": runs, "rounds": rounds}
     if cache is None and save:
         cache = AutotuneCache()
@@ -190,7 +197,7 @@ def tune_gemm(M: int, N: int, K: int, device=None, **kw) -> dict:
 
 
 def tune_spmm_bsr(row_ptr, col_idx, vals, B, M: int, **kw) -> dict:
-    """Tunes the BSR SpMM (rasterisation group) on the caller's operands (int32 indices, fp16 values)."""
+    """Tunes the BSR SpMM (tile kind and rasterisation group) on the caller's operands (int32 indices, fp16 values)."""
     K, N = B.shape
     C = torch.empty(M, N, device=B.device)
     return tune("spmm_bsr", M, N, K, lambda: _capi.spmm_bsr_f16f32(row_ptr, col_idx, vals, B, C, M), **kw)

@@ -40,7 +40,9 @@ def test_candidates():
     assert len(set(c)) == len(c)
     small = at.candidates("gemm_f16f32", 256, 256, 64)  # one or two M tiles: few distinct groups
     assert len(small) < len(c)
-    assert {t for t, _ in at.candidates("spmm_bsr", 8192, 8192, 8192)} == {-1}
+    assert {t for t, _ in at.candidates("spmm_bsr", 8192, 8192, 8192)} == {-1, 0, 1}
+    assert {t for t, _ in at.candidates("spmm_bsr", 8192, 256, 8192)} == {-1}
+    assert {t for t, _ in at.candidates("spmm_bsr_bsr", 8192, 8192, 8192)} == {-1}
 
 
 def test_shape_keys_round_trip():
