@@ -134,7 +134,9 @@ int64_t bsk_gemm_splitk_workspace_bytes(int M, int N, int K, int splits);
  * permitted or is owned by another allocator. It allocates nothing: the split partials go to a static device
  * array of 32 MiB built into this library (every GPU that loads the library holds it until exit).
  *   - splits * M * round_up(N, 4) * 4 bytes must fit in 32 MiB, else BSK_ERR_INVALID_ARG with a message
- *     (e.g. 1024 x 1024 with up to 8 splits).
+ *     (e.g. 1024 x 1024 with up to 8 splits). Automatic splits (splits <= 0) always fit: the plan keeps
+ *     (256 x 256 tiles) x splits at or below the co-resident CTA pairs (74 on a B200), i.e. at most
+ *     74 x 256 KiB = 18.5 MiB of partials; only an explicit `splits` can exceed the array.
  *   - The first call on each device looks up the array's device address (cudaGetSymbolAddress); make that
  *     first call on a device before any stream capture.
  *   - All calls share the array: calls that overlap on the GPU (other streams, other threads) race on it.
@@ -372,6 +374,13 @@ int bsk_set_wait_timeout_ns(uint64_t ns);
  * device-side failure detection).
  */
 int bsk_selftest_wait_timeout(uint64_t timeout_ns, void* stream);
+
+/*
+ * Accuracy self-test of the attention softmax's two exponential routes: y[i] = 2^x[i] for n device floats,
+ * by the FMA-pipe polynomial (fma_pipe = 1; a quarter of the softmax's exponentials take it) or by the MUFU
+ * instruction (fma_pipe = 0). Asynchronous on `stream`. No reference counterpart.
+ */
+int bsk_selftest_exp2(const float* x, float* y, int n, int fma_pipe, void* stream);
 
 #ifdef __cplusplus
 }

@@ -86,6 +86,7 @@ SIGNATURES = {
     "bsk_device_error": (_i32, [ctypes.POINTER(ctypes.c_uint32)]),
     "bsk_set_wait_timeout_ns": (_i32, [_u64]),
     "bsk_selftest_wait_timeout": (_i32, [_u64, _vp]),
+    "bsk_selftest_exp2": (_i32, [_vp, _vp, _i32, _i32, _vp]),
 }
 
 
@@ -426,6 +427,12 @@ def set_wait_timeout_ns(ns: int) -> None:
 def selftest_wait_timeout(ns: int, stream=None) -> int:
     """Returns the status code of the failure-detection probe (BSK_ERR_DEVICE_TIMEOUT is the expected one)."""
     return lib().bsk_selftest_wait_timeout(int(ns), _stream(stream))
+
+
+def selftest_exp2(x, y, fma_pipe: bool, stream=None) -> None:
+    """y = 2^x elementwise (fp32 device tensors) by the softmax's FMA-pipe polynomial or its MUFU route."""
+    check(lib().bsk_selftest_exp2(_ptr(x), _ptr(y), x.numel(), int(bool(fma_pipe)), _stream(stream)),
+          "bsk_selftest_exp2")
 
 
 def bsr_validate_host(row_ptr, col_idx, Kb: int) -> None:

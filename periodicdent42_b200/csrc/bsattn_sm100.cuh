@@ -541,4 +541,23 @@ __global__ void wait_probe_kernel(uint32_t* err, uint64_t timeout_ns) {
   warp_wait_bounded(ptx::smem_u32(&bar), 0, c, 1);
 }
 
+// y[i] = 2^x[i] by the softmax's exponential routes, for the accuracy self-test: fma_pipe = 1 takes the
+// FMA-pipe polynomial (ex2_poly2, on the pairs (x[2j], x[2j+1]) exactly as the softmax feeds it), 0 the
+// MUFU instruction (ex2.approx.ftz). Grid-stride over pairs; an odd tail element is paired with itself.
+__global__ void exp2_probe_kernel(const float* __restrict__ x, float* __restrict__ y, int n, int fma_pipe) {
+  const int pairs = (n + 1) / 2;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < pairs; j += gridDim.x * blockDim.x) {
+    const int i0 = 2 * j, i1 = (2 * j + 1 < n) ? 2 * j + 1 : 2 * j;
+    float y0, y1;
+    if (fma_pipe) {
+      ex2_poly2(x[i0], x[i1], y0, y1);
+    } else {
+      y0 = ex2_approx(x[i0]);
+      y1 = ex2_approx(x[i1]);
+    }
+    y[i0] = y0;
+    if (i1 != i0) y[i1] = y1;
+  }
+}
+
 }  // namespace bsk

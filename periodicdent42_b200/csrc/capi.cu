@@ -1741,4 +1741,18 @@ int bsk_selftest_wait_timeout(uint64_t timeout_ns, void* stream) {
   return set_error(BSK_ERR_CUDA, "selftest: the probe kernel did not report a timeout (word=0x%08x)", word);
 }
 
+int bsk_selftest_exp2(const float* x, float* y, int n, int fma_pipe, void* stream) {
+  if (n < 0) return set_error(BSK_ERR_INVALID_ARG, "selftest_exp2: negative length");
+  if (fma_pipe != 0 && fma_pipe != 1) return set_error(BSK_ERR_INVALID_ARG, "selftest_exp2: fma_pipe must be 0 or 1");
+  if (n > 0 && (!x || !y)) return set_error(BSK_ERR_INVALID_ARG, "selftest_exp2: null pointer");
+  DeviceState* st;
+  if (int rc = device_state(&st)) return rc;
+  if (n == 0) return BSK_OK;
+  const int pairs = (n + 1) / 2;
+  const int blocks_needed = (pairs + 255) / 256;
+  const int grid = blocks_needed < 4 * st->sm_count ? blocks_needed : 4 * st->sm_count;
+  bsk::exp2_probe_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(x, y, n, fma_pipe);
+  return launch_status("selftest_exp2 launch");
+}
+
 }  // extern "C"

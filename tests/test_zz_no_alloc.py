@@ -16,8 +16,9 @@ TOL = 1e-3  # normwise relative error vs fp64, the fp16 GEMM bar of the other GE
 
 def test_static_scratch_splitk_matches_workspace_entry_point_twice(cuda_dev):
     assert _capi.device_error() == 0
-    # two calls in a row with different shapes and split counts; the second reads none of the first's partials
-    for seed, (M, N, K, splits) in enumerate([(1024, 1024, 4096, 4), (512, 768, 8192, 8)]):
+    # calls in a row with different shapes and split counts; none reads an earlier call's partials. The last one
+    # lets the library choose the splits (one 256 x 256 output tile and a long K: 32 splits, 8 MiB of partials).
+    for seed, (M, N, K, splits) in enumerate([(1024, 1024, 4096, 4), (512, 768, 8192, 8), (256, 256, 65536, 0)]):
         g = torch.Generator().manual_seed(100 + seed)
         A = torch.randn(M, K, generator=g).half()
         Bt = torch.randn(N, K, generator=g).half()
