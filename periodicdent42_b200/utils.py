@@ -82,3 +82,49 @@ def get_optimal_block_size(matrix_shape: Tuple[int, int]) -> int:
     """Block size for BSR input on B200 (utils.py:147-172 picked 8/16/32 by size for WMMA kernels): the
     tcgen05 kernel's M tile is 128, so 128x128 blocks avoid any re-blocking."""
     return 128
+
+
+# BSR SpMM throughput per device at each device's validation workload, in TFLOPS of stored-block FLOPs, with torch's
+# sparse path (torch.sparse.mm) and CUTLASS timed on the same device where a figure exists:
+#   device: (this operator, torch.sparse.mm, CUTLASS or None, SMs, concurrent output tiles per SM, tile rows x cols,
+#            where the figures come from)
+# B200 is this build, measured; L4 / A100 / H100 keep the figures the reference's estimator is built on
+# (BlackwellSparseK/python/utils.py:195-212: its L4 measurement and its projections from it).
+_SPMM_DEVICES = {
+    "B200": (1015.0, 3.93, None, 148, 0.5, (128, 512),
+             "this build measured on B200 (8192^3, 128x128 blocks, 16 of 64 per block-row; torch.sparse.mm on the "
+             "same matrix in CSR fp16)"),
+    "H100": (580.0, 9.6, 330.0, 132, 1.0, (256, 128), "the reference's projection from its L4 measurement"),
+    "A100": (312.0, 5.2, 180.0, 108, 1.0, (256, 128), "the reference's projection from its L4 measurement"),
+    "L4": (52.1, 0.87, 30.0, 58, 1.0, (256, 128), "the reference's L4 measurement (8192^2, 78 % sparse)"),
+}
+
+
+def _wave_efficiency(M: int, N: int, sms: int, per_sm: float, tile) -> float:
+    """Fraction of the GPU's tile slots the persistent kernel keeps busy over a shape's output tiles."""
+    tiles = -(-max(M, 1) // tile[0]) * -(-max(N, 1) // tile[1])
+    slots = max(1, int(sms * per_sm))
+    return tiles / (-(-tiles // slots) * slots)
+
+
+def estimate_speedup(matrix_shape: Tuple[int, int], sparsity: float, device: str = "B200") -> dict:
+    """Estimated BSR SpMM throughput for an M x N output on `device`, with the reference's result keys
+    (utils.py:172-236). The estimate scales the device's measured throughput at its validation workload by how well
+    the shape's output tiles fill the GPU (a shape with few tiles leaves SMs idle in its last wave) relative to
+    that workload; ``tflops`` counts the FLOPs of the stored blocks (what the kernel executes), so to first order
+    it does not depend on ``sparsity``. Unknown devices raise ``ValueError`` as in the reference."""
+    if device not in _SPMM_DEVICES:
+        raise ValueError(f"Unknown device: {device}")
+    ours, torch_tf, cutlass_tf, sms, per_sm, tile, basis = _SPMM_DEVICES[device]
+    M, N = matrix_shape
+    f = _wave_efficiency(M, N, sms, per_sm, tile) / _wave_efficiency(8192, 8192, sms, per_sm, tile)
+    tflops = ours * f
+    return {
+        "device": device,
+        "matrix_shape": matrix_shape,
+        "sparsity": sparsity,
+        "tflops": tflops,
+        "speedup_vs_pytorch": tflops / torch_tf,
+        "speedup_vs_cutlass": (tflops / cutlass_tf) if cutlass_tf else None,
+        "note": f"Scaled by output-tile occupancy from {basis}",
+    }
