@@ -120,77 +120,113 @@ def load_traffic():
 
 
 class Clocks:
-    """nvidia-smi sampler (100 ms) running across the run; each timed region records its host-time window and
-    the summary is taken over the samples inside the headline window (falling back to all samples under
-    load when the window holds fewer than 3)."""
+    """SM clock, power and clock-event reasons of the GPUs in use, sampled every ~10 ms from a thread through NVML
+    (queries only; falls back to `nvidia-smi -lms 100` when NVML cannot be loaded). Each timed region records its
+    host-time window; summaries are taken over the samples inside a window, so even a ~50 ms region (the 8-GPU
+    headline) gets a handful of samples. The headline summary falls back to all samples under load only when its
+    window holds fewer than 3."""
     QUERY = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = (("hw_slowdown", 0x8), ("hw_thermal_slowdown", 0x40), ("sw_thermal_slowdown", 0x20),
+               ("sw_power_cap", 0x4))
 
-    def __init__(self, gpu_indices):
-        self.idx = set(gpu_indices)
-        self.proc = None
+    def __init__(self, gpu_indices, period_s: float = 0.01):
+        self.idx = sorted(set(gpu_indices))
+        self.period = period_s
         self.windows = {}
-        self.path = os.path.join("/tmp", f"bsk_clocks_{os.getpid()}.csv")
+        self.rows = []  # (time, gpu, sm_mhz, max_mhz, power_w, {reason: bool})
+        self.source = None
+        self._stop = None
+        self._thread = None
+        self._proc = None
+        self._path = os.path.join("/tmp", f"bsk_clocks_{os.getpid()}.csv")
 
     def start(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                                          "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            import pynvml
+
+            pynvml.nvmlInit()
+            handles = [(i, pynvml.nvmlDeviceGetHandleByIndex(i)) for i in self.idx]
+            maxes = {i: pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM) for i, h in handles}
+        except Exception:  # noqa: BLE001 - no NVML: the nvidia-smi sampler instead
+            self._start_smi()
+            return
+        import threading
+
+        self.source = "nvml"
+        self._stop = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                for i, h in handles:
+                    try:
+                        t = time.time()
+                        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    except Exception:  # noqa: BLE001
+                        continue
+                    self.rows.append((t, i, float(sm), float(maxes[i]), pw,
+                                      {n: bool(rs & b) for n, b in self.REASONS}))
+                self._stop.wait(self.period)
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
+
+    def _start_smi(self):
+        try:
+            self._proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                                           "-lms", "100"], stdout=open(self._path, "w"), stderr=subprocess.DEVNULL)
+            self.source = "nvidia-smi"
         except OSError:
-            self.proc = None
+            self._proc = None
+
+    def _read_smi(self):
+        import datetime as _dt
+
+        def f(x):
+            try:
+                return float(x)
+            except ValueError:
+                return float("nan")
+        with open(self._path) as fh:
+            for line in fh:
+                p = [x.strip() for x in line.split(",")]
+                if len(p) < 10:
+                    continue
+                try:
+                    gpu = int(p[1])
+                    ts = _dt.datetime.strptime(p[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                except ValueError:
+                    continue
+                if gpu in self.idx:
+                    self.rows.append((ts, gpu, f(p[2]), f(p[3]), f(p[4]),
+                                      {n: v.lower().startswith("active") for (n, _), v in zip(self.REASONS, p[6:10])}))
+        os.unlink(self._path)
 
     def mark(self, name, t0, t1):
         self.windows[name] = (t0, t1)
 
     @staticmethod
-    def _f(x):
-        try:
-            return float(x)
-        except ValueError:
-            return float("nan")
-
-    def _rows(self):
-        import datetime as _dt
-
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                p = [x.strip() for x in line.split(",")]
-                if len(p) < 10:
-                    continue
-                try:
-                    if int(p[1]) not in self.idx:
-                        continue
-                    ts = _dt.datetime.strptime(p[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
-                except ValueError:
-                    continue
-                rows.append((ts, p))
-        return rows
-
-    def summary(self, rows):
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for _, r in rows:
-            for n, v in zip(names, r[6:10]):
-                if v.lower().startswith("active"):
-                    reasons.add(n)
-        sm = [self._f(r[2]) for _, r in rows]
-        return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm), "sm_max_mhz": max(self._f(r[3]) for _, r in rows),
-                "power_w_max": max(self._f(r[4]) for _, r in rows),
-                "power_w_median": statistics.median(self._f(r[4]) for _, r in rows), "samples": len(rows),
-                "reasons": sorted(reasons)}
+    def summary(rows):
+        reasons = sorted({n for r in rows for n, on in r[5].items() if on})
+        sm = [r[2] for r in rows]
+        return {"sm_mhz": statistics.median(sm), "sm_min_mhz": min(sm), "sm_max_mhz": max(r[3] for r in rows),
+                "power_w_max": max(r[4] for r in rows), "power_w_median": statistics.median(r[4] for r in rows),
+                "samples": len(rows), "reasons": reasons}
 
     def stop(self, headline="dense"):
-        if self.proc is None:
-            return None
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        rows = self._rows()
-        os.unlink(self.path)
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=5)
+        elif self._proc is not None:
+            self._proc.terminate()
+            try:
+                self._proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self._proc.kill()
+            self._read_smi()
+        rows = self.rows
         if not rows:
             return None
         out = {}
@@ -200,10 +236,11 @@ class Clocks:
                 out[name] = self.summary(win)
         head = out.get(headline)
         if head is None or head["samples"] < 3:
-            load = [x for x in rows if self._f(x[1][4]) > 200.0] or rows
+            load = [x for x in rows if x[4] > 200.0] or rows
             head = dict(self.summary(load), window="all samples under load")
         else:
             head = dict(head, window=f"{headline} timed region")
+        head["source"] = self.source
         head["per_region"] = out
         return head
 
@@ -353,7 +390,9 @@ def bench_fp8(ctx: Ctx, args, res: dict):
     # 0.5 GB inputs: flush L2 between steps by rotating through 4 input copies is not needed at
     # 268 MB per operand (> 126 MB L2); each step re-reads both operands from HBM.
     ms = time_region(ctx, step, args.op_steps, args.warmup, "fp8")
-    res["fp8"] = {"ms": ms, "tflops": cfg.flops / (ms * 1e-3) / 1e12, "flops": cfg.flops, "launches_per_step": 1}
+    res["fp8"] = {"ms": ms, "tflops": cfg.flops / (ms * 1e-3) / 1e12, "flops": cfg.flops, "launches_per_step": 1,
+                  # per rank: e4m3 A and this rank's B^T rows once, bf16 D columns once
+                  "algorithmic_bytes": (cfg.M + (n1 - n0)) * cfg.K + cfg.M * (n1 - n0) * 2}
     del Aq, Bqt, D
     torch.cuda.empty_cache()
 
@@ -371,7 +410,11 @@ def bench_bsr(ctx: Ctx, args, res: dict):
     def step():
         _capi.spmm_bsr_f16f32(rp32, ci32, vals, B, C, cfg.M, r0, r1, stream=ctx.stream)
     ms = time_region(ctx, step, args.op_steps, args.warmup, "bsr")
+    blocks_r = int(crow[r1].item() - crow[r0].item())
     res["bsr"] = {"ms": ms, "tflops": cfg.flops / (ms * 1e-3) / 1e12, "flops": cfg.flops, "launches_per_step": 1,
+                  # per rank: its stored blocks, the dense B, its C rows
+                  "algorithmic_bytes": blocks_r * cfg.block * cfg.block * 2 + cfg.K * cfg.N * 2
+                  + (r1 - r0) * cfg.block * cfg.N * 4,
                   "nnzb": int(crow[-1].item()), "block_rows": [r0, r1], "Mb": Mb}
     del crow, col, vals, B, C
     torch.cuda.empty_cache()
@@ -415,6 +458,8 @@ def bench_attn_bwd(ctx: Ctx, args, res: dict):
     nnz = int(rp[-1])
     flops = 2.5 * 4 * 128 ** 2 * cfg.D * nnz
     res["attn_bwd"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "flops": flops, "launches_per_step": 3,
+                       # per rank: read Q, K, V, O, dO and the LSE, write dQ, dK, dV (its pairs)
+                       "algorithmic_bytes": (b1 - b0) * cfg.S * (8 * cfg.D * 2 + 4),
                        "nnz_blocks": nnz, "executed_gemm_ratio": 7 / 5}
     del q, k, v, O, dO, dQ, dK, dV
     torch.cuda.empty_cache()
@@ -469,6 +514,8 @@ def bench_bsr_bsr(ctx: Ctx, args, res: dict):
         _capi.spmm_bsr_bsr_f16f32(rp, ci, vals, brp, bci, bvals, C, cfg.M, cfg.N, cfg.K, r0, r1, stream=ctx.stream)
     ms = time_region(ctx, step, args.op_steps, args.warmup, "bsr_bsr")
     res["bsr_bsr"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "flops": flops, "launches_per_step": 1,
+                      "algorithmic_bytes": int(crow[r1] - crow[r0]) * 128 * 128 * 2 + int(bcrow[-1]) * 128 * 128 * 2
+                      + (r1 - r0) * 128 * cfg.N * 4,
                       "block_pairs": pairs, "nnzb": int(crow[-1].item()), "b_nnzb": int(bcrow[-1])}
     del crow, col, vals, bvals, C
     torch.cuda.empty_cache()
@@ -562,6 +609,8 @@ def bench_attn(ctx: Ctx, args, res: dict):
     ms = time_region(ctx, step, args.op_steps, args.warmup, "attn")
     flops = wl.attn_flops(rp, cfg.block, cfg.D)
     res["attn"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "flops": flops, "launches_per_step": 1,
+                   # per rank: read Q, K, V and write O of its (b,h) pairs
+                   "algorithmic_bytes": (b1 - b0) * cfg.S * cfg.D * 2 * 4,
                    "nnz_blocks": int(rp[-1].item()), "pairs": [b0, b1]}
     del q, k, v, O
     torch.cuda.empty_cache()
@@ -586,6 +635,76 @@ def cpu_dense_sample(cfg: wl.DenseCfg, k_slice: int, seconds: float, threads: in
         if el >= seconds or reps >= 50:
             break
     return flops * reps / el / 1e12, reps, torch.get_num_threads()
+
+
+def _cpu_loop(fn, seconds: float, max_reps: int = 1000):
+    """Runs fn until `seconds` of wall time (at least once); returns (elapsed s, reps)."""
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        fn()
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= seconds or reps >= max_reps:
+            return el, reps
+
+
+def cpu_op_samples(seconds: float) -> dict:
+    """The reference's CPU torch path of the FP8, BSR and attention operators on bounded samples of their benchmark
+    workloads, all host threads, each reported per FLOP of the same kind the GPU line counts (TFLOPS):
+      fp8   torch._scaled_mm (e4m3 x e4m3, per-tensor scales, bf16 out) on a 256 x 256 output tile of the workload
+            with a K = 2048 slice (the CPU kernel runs at well under 1 GFLOP/s, so the sample is small)
+      bsr   torch.sparse.mm on the fp32-upcast BSR matrix (fp16 BSR is not implemented on the CPU) for the first
+            block-rows of the workload against the whole dense B; nonzero-block FLOPs
+      attn  the block-sparse attention of the workload's first (b,h) pairs, fp32 (masked-SDPA semantics over the
+            nonzero key blocks), nonzero-block FLOPs"""
+    from oracle import reference_path as ref
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    cores = torch.get_num_threads()
+    out = {}
+    # FP8
+    g = torch.Generator().manual_seed(wl.FP8.seed)
+    ks = 2048
+    Aq, sa = wl.quantize_e4m3(torch.randn(256, ks, generator=g))
+    Bq, sb = wl.quantize_e4m3(torch.randn(256, ks, generator=g))
+    el, reps = _cpu_loop(lambda: ref.fp8_ref(Aq, Bq, sa, sb), seconds / 3)
+    out["fp8"] = {"value": 2.0 * 256 * 256 * ks * reps / el / 1e12, "unit": UNIT, "cores": cores, "kind": "port",
+                  "sample": f"{reps} x torch._scaled_mm 256x256x{ks} (e4m3, per-tensor scales, bf16 out)"}
+    # BSR
+    cfg = wl.BSR
+    crow, col, vals, B = wl.bsr_inputs(cfg, "cpu")
+    rows = 4
+    nz = int(crow[rows])
+    Bf = B.float()
+    Ab = torch.sparse_bsr_tensor(crow[:rows + 1], col[:nz], vals[:nz].float(), size=(rows * cfg.block, cfg.K))
+    el, reps = _cpu_loop(lambda: torch.sparse.mm(Ab, Bf), seconds / 3)
+    out["bsr"] = {"value": 2.0 * nz * cfg.block * cfg.block * cfg.N * reps / el / 1e12, "unit": UNIT,
+                  "cores": cores, "kind": "port",
+                  "sample": f"{reps} x torch.sparse.mm(fp32 BSR, fp32 B) on {rows} of {cfg.M // cfg.block} block-rows "
+                            f"({nz} blocks) x the full 8192x8192 B"}
+    del B, Bf, vals
+    # attention
+    acfg = wl.ATTN
+    nqb = acfg.S // acfg.block
+    g = torch.Generator().manual_seed(acfg.seed)
+    rp, ci = wl.attn_mask_bsr(acfg, n_pairs=2)
+    q, k, v = (torch.randn(acfg.S, acfg.D, generator=g).to(torch.bfloat16) for _ in range(3))
+    scale = 1.0 / math.sqrt(acfg.D)
+    state = {"pairs": 0, "blocks": 0}
+
+    def one_pair():
+        p = state["pairs"] % 2
+        r0, r1 = p * nqb, (p + 1) * nqb
+        ref.attn_blocksparse(q, k, v, rp[r0:r1 + 1], ci[int(rp[r0]):int(rp[r1])], scale, True)
+        state["pairs"] += 1
+        state["blocks"] += int(rp[r1] - rp[r0])
+    el, reps = _cpu_loop(one_pair, seconds / 3)
+    out["attn"] = {"value": 4.0 * acfg.block * acfg.block * acfg.D * state["blocks"] / el / 1e12, "unit": UNIT,
+                   "cores": cores, "kind": "port",
+                   "sample": f"{reps} (b,h) pairs of S={acfg.S}, D={acfg.D}, {state['blocks']} nonzero blocks, "
+                             "fp32 block-sparse restatement of masked SDPA"}
+    return out
 
 
 def run_reference(args):
@@ -620,6 +739,36 @@ def run_reference(args):
     return 0
 
 
+# ----------------------------------------------------------------------------------------- roofline
+def per_clock(tflops_per_gpu: float, region: dict, sm_count: int, mult: int) -> dict:
+    """Work per SM clock of a timed region (median SM clock of its samples): FLOP / clk / SM and its fraction of
+    the dense tensor peak per clock (8192 for fp16/bf16, 16384 for e4m3)."""
+    fpc = tflops_per_gpu * 1e12 / (region["sm_mhz"] * 1e6 * sm_count)
+    return {"sm_mhz": region["sm_mhz"], "samples": region["samples"], "reasons": region["reasons"],
+            "flop_per_clk_per_sm": fpc, "frac_of_clock_peak": fpc / (8192 * mult)}
+
+
+def op_roofline(name: str, r: dict, region, peaks: dict, peak_src: str, world: int, sm_count: int, traffic) -> dict:
+    """Tensor-core roofline of one operator's timed region. The denominator follows the region's own clock record:
+    the measured cuBLAS burst peak when the region ran without the power cap, the sustained (power-capped) one when
+    `sw_power_cap` was active in it; FP8 counts twice the bf16 figure."""
+    mult = 2 if name == "fp8" else 1
+    per_gpu = r["tflops"] / world
+    capped = bool(region) and "sw_power_cap" in region["reasons"]
+    base = peaks["bf16_tflops_sustained"] if capped else peaks["bf16_tflops"]
+    peak = base * mult
+    out = {"bound": "tensor", "achieved": per_gpu, "peak": peak, "unit": "TFLOP/s", "frac": per_gpu / peak,
+           "peak_kind": ("2 x " if mult == 2 else "") + f"{peak_src} bf16 "
+                        + ("sustained (sw_power_cap active in this region)" if capped
+                           else "burst (no power cap in this region)"),
+           "algorithmic_bytes": r.get("algorithmic_bytes"),
+           "traffic": traffic["bytes_per_launch"] if traffic and world == 1 else None,
+           "traffic_source": traffic["source"] if traffic and world == 1 else None}
+    if region:
+        out.update(per_clock(per_gpu, region, sm_count, mult))
+    return out
+
+
 # ----------------------------------------------------------------------------------------- main
 def main():
     args = parse_args()
@@ -648,10 +797,14 @@ def main():
         clk = clocks.stop() if clocks else None
     err_word = _capi.device_error()
     cpu = None
-    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline and "dense" in res:
-        tf, reps, cores = cpu_dense_sample(dense_cfg(args), min(4096, dense_cfg(args).K), args.cpu_seconds)
-        cpu = {"value": tf, "unit": UNIT, "cores": cores, "kind": "port",
-               "sample": f"{reps} x torch.matmul(fp32) on the 8192x8192x4096 K-slice of the headline shape"}
+    cpu_ops = {}
+    if ctx.rank == 0 and ctx.world == 1 and not args.no_cpu_baseline:
+        if "dense" in res:
+            tf, reps, cores = cpu_dense_sample(dense_cfg(args), min(4096, dense_cfg(args).K), args.cpu_seconds)
+            cpu = {"value": tf, "unit": UNIT, "cores": cores, "kind": "port",
+                   "sample": f"{reps} x torch.matmul(fp32) on the 8192x8192x4096 K-slice of the headline shape"}
+        if any(o in res for o in ("fp8", "bsr", "attn")):
+            cpu_ops = cpu_op_samples(args.cpu_seconds)
     if ctx.rank == 0:
         d = res.get("dense")
         traffic = load_traffic()
@@ -682,14 +835,18 @@ def main():
         line["cpu_baseline"] = cpu
         line["clocks"] = clk
         opsum = {}
+        regions = (clk or {}).get("per_region", {})
+        sm_count = torch.cuda.get_device_properties(ctx.dev).multi_processor_count
+        if d and regions.get("dense"):
+            line["per_clock"] = per_clock(d["tflops"] / ctx.world, regions["dense"], sm_count, 1)
         for name in ("fp8", "bsr", "attn", "attn_bwd", "bsr_bsr"):
             if name in res:
                 r = res[name]
-                pk = peak_t * (2 if name == "fp8" else 1)
                 opsum[name] = {"tflops": r["tflops"], "ms": r["ms"],
-                               "frac_of_peak": r["tflops"] / ctx.world / pk,
-                               "peak": pk, "peak_basis": ("2 x " if name == "fp8" else "") + "measured bf16 sustained"}
-                for kk in ("nnzb", "nnz_blocks", "block_pairs", "b_nnzb"):
+                               "roofline": op_roofline(name, r, regions.get(name), peaks, peak_src, ctx.world,
+                                                       sm_count, traffic.get(name)),
+                               "cpu_baseline": cpu_ops.get(name)}
+                for kk in ("nnzb", "nnz_blocks", "block_pairs", "b_nnzb", "algorithmic_bytes"):
                     if kk in r:
                         opsum[name][kk] = r[kk]
         if "convert" in res:

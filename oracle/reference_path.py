@@ -142,10 +142,18 @@ def attn_blocksparse_fp64(q, k, v, row_ptr, col_idx, scale: float, causal_diag: 
     rows (row_ptr rebased so row_ptr[0] is this pair's first entry). Gathers only the nonzero key blocks
     of each query block-row and applies an exact two-pass softmax. Empty rows give zeros.
     ``pair_rows`` restricts the computation to a subset of query block-rows (list of ints)."""
+    return attn_blocksparse(q, k, v, row_ptr, col_idx, scale, causal_diag, block, pair_rows, torch.float64)
+
+
+def attn_blocksparse(q, k, v, row_ptr, col_idx, scale: float, causal_diag: bool, block: int = 128,
+                     pair_rows=None, dtype=torch.float32) -> torch.Tensor:
+    """Block-sparse attention of one (b,h) pair in `dtype` (the fp64 oracle above, or the fp32 CPU restatement
+    of the reference's masked-SDPA path that the benchmark times as its CPU baseline: the same result as
+    F.scaled_dot_product_attention with the dense block mask, computed over the nonzero key blocks only)."""
     S, D = q.shape
     nqb = S // block
-    qd, kd, vd = q.double(), k.double(), v.double()
-    out = torch.zeros(S, D, dtype=torch.float64)
+    qd, kd, vd = q.to(dtype), k.to(dtype), v.to(dtype)
+    out = torch.zeros(S, D, dtype=dtype)
     rp = row_ptr.tolist()
     ci = col_idx.tolist()
     base = rp[0]
