@@ -1,8 +1,8 @@
 """Build recipe for the oracle's native parts -- TEST INFRASTRUCTURE ONLY.
 
   oracle/liboracle_bsr.so   the plain-C restatement (bsr_oracle.c), built with gcc everywhere
-  oracle/_ref/libbsr_ref.so the reference's own cpu_bsr (build_ref.sh), built only where the
-                            reference checkout exists (REF_ROOT, default /root/reference)
+  oracle/_ref/libbsr_ref.so the reference's own cpu_bsr (build_ref.sh), built only when the location of a
+                            reference checkout is given (argument `ref_root` or REF_ROOT) and holds the source
 """
 from __future__ import annotations
 
@@ -21,12 +21,15 @@ def build_oracle(force: bool = False) -> str:
     return ORACLE_LIB
 
 
-def build_ref(force: bool = False) -> str | None:
-    ref_root = os.environ.get("REF_ROOT", "/root/reference")
-    if not os.path.isdir(os.path.join(ref_root, "BlackwellSparseK", "src")):
+def build_ref(force: bool = False, ref_root: str | None = None) -> str | None:
+    """Builds oracle/_ref from the reference checkout at `ref_root` (default: $REF_ROOT); without one, returns the
+    library built earlier, if any."""
+    ref_root = ref_root or os.environ.get("REF_ROOT")
+    if not ref_root or not os.path.isdir(os.path.join(ref_root, "BlackwellSparseK", "src")):
         return REF_LIB if os.path.exists(REF_LIB) else None
     if force or not os.path.exists(REF_LIB):
-        subprocess.run(["sh", os.path.join(HERE, "build_ref.sh")], check=True, stdout=subprocess.DEVNULL)
+        subprocess.run(["sh", os.path.join(HERE, "build_ref.sh")], check=True, stdout=subprocess.DEVNULL,
+                       env={**os.environ, "REF_ROOT": ref_root})
     return REF_LIB
 
 

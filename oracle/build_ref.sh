@@ -1,10 +1,10 @@
 #!/bin/sh
 # Compiles the reference's CPU BSR checker (cpu_bsr, BlackwellSparseK/src/bsr_reference.cu) from its
 # source in the reference checkout into oracle/_ref/libbsr_ref.so -- TEST INFRASTRUCTURE ONLY.
-# Only this container has the reference checkout; the built library travels with the working tree.
+# REF_ROOT names the directory that holds the reference checkout (BlackwellSparseK/ inside it); required.
 set -e
 HERE=$(cd "$(dirname "$0")" && pwd)
-REF_ROOT=${REF_ROOT:-/root/reference}
+[ -n "$REF_ROOT" ] || { echo "set REF_ROOT to the reference checkout" >&2; exit 2; }
 SRC="$REF_ROOT/BlackwellSparseK/src/bsr_reference.cu"
 [ -f "$SRC" ] || { echo "reference source not found: $SRC" >&2; exit 2; }
 mkdir -p "$HERE/_ref"

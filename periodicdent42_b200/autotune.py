@@ -58,7 +58,9 @@ def candidates(op: str, M: int, N: int, K: int) -> list[tuple[int, int]]:
     if op in ("gemm_f16f32", "gemm_e4m3_bf16"):
         tiles = [-1, 0, 1, 2]
     elif op == "spmm_bsr":
-        tiles = [-1, 0, 1] if N >= 512 else [-1]
+        # BSK_SPMM_TILE forces one tile kind over any registered configuration, so tile variants would all time
+        # the same kernel and the cache would record an arbitrary winner: tune the group only
+        tiles = [-1, 0, 1] if N >= 512 and not os.environ.get("BSK_SPMM_TILE") else [-1]
     else:
         tiles = [-1]
     out = []

@@ -73,7 +73,8 @@ class SplitKReduceScatterGemm:
             out = torch.empty(self.rows, N, dtype=torch.float32, device=A.device)
         k0, k1 = sharding.dense_ksplit(K, self.world, self.rank)
         b = self._calls & 1
-        s = _capi._stream(stream)
+        strm = _as_stream(stream, A.device)
+        s = strm.cuda_stream
         lib = _capi.lib()
         if k1 > k0:
             _capi.check(lib.bsk_gemm_f16f32_splitk_scatter(A.data_ptr(), A.stride(0), Bt.data_ptr(), Bt.stride(0), M, N,
@@ -81,7 +82,10 @@ class SplitKReduceScatterGemm:
                                                            s), "bsk_gemm_f16f32_splitk_scatter")
         else:  # no K for this rank: its slot in every owner's buffer must still be defined
             raise ValueError("K too small to give every rank a non-empty K range")
-        dist.all_reduce(self._flag, group=self.group)  # every rank's GEMM (and its peer stores) has completed
+        # The barrier goes on the GEMM's stream: NCCL then starts only after this rank's peer stores were issued
+        # and completed, and the slot sum below (same stream) starts only after every rank's have.
+        with torch.cuda.stream(strm):
+            dist.all_reduce(self._flag, group=self.group)
         _capi.check(lib.bsk_splitk_slots_reduce(self._own[b], self.world, self.rows, N, self.ld, out.data_ptr(),
                                                 out.stride(0), s), "bsk_splitk_slots_reduce")
         self._calls += 1
@@ -98,6 +102,16 @@ class SplitKReduceScatterGemm:
         for p in self._own:
             lib.bsk_peer_buffer_free(p)
         self._own = []
+
+
+def _as_stream(stream, device) -> torch.cuda.Stream:
+    """The torch stream object for `stream`: None = the current stream of `device`, an int = a raw cudaStream_t
+    handle (wrapped, not owned), else a torch.cuda.Stream."""
+    if stream is None:
+        return torch.cuda.current_stream(device)
+    if isinstance(stream, int):
+        return torch.cuda.ExternalStream(stream, device=device)
+    return stream
 
 
 def host_rows(M: int, world: int, rank: int) -> tuple[int, int, int]:

@@ -1,7 +1,7 @@
 """Generates tests/golden/golden.npz: small known-answer cases produced by the REFERENCE's own code.
 
-Run in a checkout that has the reference next to it (REF_ROOT, default /root/reference):
-    python tests/golden/make_golden.py
+Run with REF_ROOT naming the reference checkout (required):
+    REF_ROOT=<checkout> python tests/golden/make_golden.py
 What each case comes from:
   * BSR index handling: the reference's ``convert_to_bsr`` (BlackwellSparseK/python/utils.py:10-57),
     imported from the reference checkout, applied to dense matrices whose block pattern our builders
@@ -32,7 +32,9 @@ from periodicdent42_b200 import workloads as wl  # noqa: E402
 
 
 def load_reference_utils():
-    ref_root = os.environ.get("REF_ROOT", "/root/reference")
+    ref_root = os.environ.get("REF_ROOT")
+    if not ref_root:
+        raise SystemExit("set REF_ROOT to the reference checkout")
     path = os.path.join(ref_root, "BlackwellSparseK", "python", "utils.py")
     spec = importlib.util.spec_from_file_location("bsk_reference_utils", path)
     mod = importlib.util.module_from_spec(spec)
