@@ -92,65 +92,75 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const int num_units = a.num_m_tiles * a.num_n_tiles;
 
   if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer (both CTAs, one thread)
-    if (lane == 0) {
-      uint32_t stage = 0, phase = 0, issued = 0;
-      bool ok = true;
-      const uint32_t s0 = ptx::smem_u32(smem);
-      const uint32_t full0 = ptx::smem_u32(full), empty0 = ptx::smem_u32(empty);
-      const uint32_t full0_leader = ptx::mapa_shared(full0, 0);
-      const uint64_t pol_a = (BSK_BSR_PAIR_HINTS & 2) ? ptx::policy_evict_last() : 0;
-      const uint64_t pol_b = (BSK_BSR_PAIR_HINTS & 4) ? ptx::policy_evict_last() : 0;
-      for (int unit = pair; unit < num_units && ok; unit += npairs) {
-        int mt, nt;
-        gemm_tile_coords(unit, a, mt, nt);
-        const int r = a.row_begin + mt;
-        int j0, j1;
-        if (!bsr_row_range(a, r, j0, j1) && rank == 0) atomicCAS(a.err, 0u, kErrBounds | (KID << 8) | (7u << 16));
-        const int col0 = nt * kBsrPairTileN + static_cast<int>(rank) * 128;
-        for (int j = j0; j < j1 && ok; ++j) {
-          int kb = __ldg(&a.col_idx[j]);
-          if (kb < 0 || kb >= a.kb_count) {  // out-of-range column: flag it; the B rows read zero fill
-            if (rank == 0) atomicCAS(a.err, 0u, kErrBounds | (KID << 8) | (8u << 16));
-            kb = a.kb_count;
-          }
-          for (int s = 0; s < STEPS; ++s) {
-            ok = wait_bounded<true, BSK_PROD_SLEEP_NS>(empty0 + stage * 8, phase ^ 1, ctl, 1);
-            if (!ok) break;
-            if (rank == 0) ptx::mbar_arrive_expect_tx(full0 + stage * 8, PAIR_TX);
-            const uint32_t st = s0 + stage * kBsrPairStage;
-            const uint32_t fb = full0_leader + stage * 8;
-            // A block j, this CTA's 64 rows, K slice s (K-major)
-            if constexpr ((BSK_BSR_PAIR_HINTS & 2) != 0)
-              ptx::tma_load_2d_pair_hint(st + kBsrPairStageB, &tmVals, fb, s * BK,
-                                         j * 128 + 64 * static_cast<int>(rank), pol_a);
-            else
-              ptx::tma_load_2d_pair(st + kBsrPairStageB, &tmVals, fb, s * BK, j * 128 + 64 * static_cast<int>(rank));
-            // dense B rows of K slice s of block column kb, columns col0 + 256 h + 64 q (MN-major slabs)
+    // ------------------------------------------------------------------ TMA producer (both CTAs)
+    // The warp walks the block-row index: per 32 nonzeros of the row, one coalesced load of their column indices
+    // (lane l holds col_idx[jb + l]), handed to lane 0 by shuffle; lane 0 alone waits on the ring and issues the
+    // TMA loads, so no per-stage warp collective sits on the issue path.
+    uint32_t stage = 0, phase = 0, issued = 0;
+    bool ok = true;
+    const uint32_t s0 = ptx::smem_u32(smem);
+    const uint32_t full0 = ptx::smem_u32(full), empty0 = ptx::smem_u32(empty);
+    const uint32_t full0_leader = ptx::mapa_shared(full0, 0);
+    const uint64_t pol_a = (BSK_BSR_PAIR_HINTS & 2) ? ptx::policy_evict_last() : 0;
+    const uint64_t pol_b = (BSK_BSR_PAIR_HINTS & 4) ? ptx::policy_evict_last() : 0;
+    for (int unit = pair; unit < num_units && ok; unit += npairs) {
+      int mt, nt;
+      gemm_tile_coords(unit, a, mt, nt);
+      const int r = a.row_begin + mt;
+      int j0, j1;
+      if (!bsr_row_range(a, r, j0, j1) && rank == 0 && lane == 0)
+        atomicCAS(a.err, 0u, kErrBounds | (KID << 8) | (7u << 16));
+      const int col0 = nt * kBsrPairTileN + static_cast<int>(rank) * 128;
+      for (int jb = j0; jb < j1 && ok; jb += 32) {
+        const int cidx = (jb + lane < j1) ? __ldg(&a.col_idx[jb + lane]) : 0;
+        const int cnt = min(32, j1 - jb);
+        for (int jj = 0; jj < cnt && ok; ++jj) {
+          int kb = __shfl_sync(0xFFFFFFFFu, cidx, jj);
+          if (lane == 0) {
+            const int j = jb + jj;
+            if (kb < 0 || kb >= a.kb_count) {  // out-of-range column: flag it; the B rows read zero fill
+              if (rank == 0) atomicCAS(a.err, 0u, kErrBounds | (KID << 8) | (8u << 16));
+              kb = a.kb_count;
+            }
+            for (int s = 0; s < STEPS; ++s) {
+              ok = wait_bounded<true, BSK_PROD_SLEEP_NS>(empty0 + stage * 8, phase ^ 1, ctl, 1);
+              if (!ok) break;
+              if (rank == 0) ptx::mbar_arrive_expect_tx(full0 + stage * 8, PAIR_TX);
+              const uint32_t st = s0 + stage * kBsrPairStage;
+              const uint32_t fb = full0_leader + stage * 8;
+              // A block j, this CTA's 64 rows, K slice s (K-major)
+              if constexpr ((BSK_BSR_PAIR_HINTS & 2) != 0)
+                ptx::tma_load_2d_pair_hint(st + kBsrPairStageB, &tmVals, fb, s * BK,
+                                           j * 128 + 64 * static_cast<int>(rank), pol_a);
+              else
+                ptx::tma_load_2d_pair(st + kBsrPairStageB, &tmVals, fb, s * BK, j * 128 + 64 * static_cast<int>(rank));
+              // dense B rows of K slice s of block column kb, columns col0 + 256 h + 64 q (MN-major slabs)
 #pragma unroll
-            for (int h = 0; h < 2; ++h)
+              for (int h = 0; h < 2; ++h)
 #pragma unroll
-              for (int q = 0; q < 2; ++q) {
-                if constexpr ((BSK_BSR_PAIR_HINTS & 4) != 0)
-                  ptx::tma_load_2d_pair_hint(st + (2 * h + q) * kBsrPairSlab, &tmB, fb, col0 + 256 * h + 64 * q,
-                                             kb * 128 + s * BK, pol_b);
-                else
-                  ptx::tma_load_2d_pair(st + (2 * h + q) * kBsrPairSlab, &tmB, fb, col0 + 256 * h + 64 * q,
-                                        kb * 128 + s * BK);
-              }
-            ++issued;
-            if (++stage == kBsrPairStages) { stage = 0; phase ^= 1; }
+                for (int q = 0; q < 2; ++q) {
+                  if constexpr ((BSK_BSR_PAIR_HINTS & 4) != 0)
+                    ptx::tma_load_2d_pair_hint(st + (2 * h + q) * kBsrPairSlab, &tmB, fb, col0 + 256 * h + 64 * q,
+                                               kb * 128 + s * BK, pol_b);
+                  else
+                    ptx::tma_load_2d_pair(st + (2 * h + q) * kBsrPairSlab, &tmB, fb, col0 + 256 * h + 64 * q,
+                                          kb * 128 + s * BK);
+                }
+              ++issued;
+              if (++stage == kBsrPairStages) { stage = 0; phase ^= 1; }
+            }
           }
+          ok = __shfl_sync(0xFFFFFFFFu, ok, 0);
         }
       }
-      if (rank == 0) {  // every load of the pair has landed (the leader's full barriers count both CTAs' bytes)
-        const uint32_t first = issued > kBsrPairStages ? issued - kBsrPairStages : 0;
-        WaitCtl dctl = ctl;
-        volatile int never = 0;
-        dctl.abort = &never;
-        for (uint32_t i = first; i < issued; ++i)
-          wait_bounded<true>(full0 + (i % kBsrPairStages) * 8, (i / kBsrPairStages) & 1, dctl, 2);
-      }
+    }
+    if (rank == 0 && lane == 0) {  // every load of the pair has landed (the leader's full barriers count both CTAs')
+      const uint32_t first = issued > kBsrPairStages ? issued - kBsrPairStages : 0;
+      WaitCtl dctl = ctl;
+      volatile int never = 0;
+      dctl.abort = &never;
+      for (uint32_t i = first; i < issued; ++i)
+        wait_bounded<true>(full0 + (i % kBsrPairStages) * 8, (i / kBsrPairStages) & 1, dctl, 2);
     }
     __syncwarp();
   } else if (warp == 1) {
