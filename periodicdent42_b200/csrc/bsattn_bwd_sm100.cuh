@@ -24,6 +24,13 @@
 
 namespace bsk {
 
+// 12 warps per CTA in both backward passes: producer, MMA issuer, 2 idle, two compute warpgroups; the launch
+// allocation of 384 x 168 registers is split 112 (warpgroup 0) / 184 (compute warpgroups).
+constexpr int kBwdThreads = 384;
+constexpr uint32_t kBwdRegsLow = 112;
+constexpr uint32_t kBwdRegsHigh = 184;
+static_assert(128 * kBwdRegsLow + 256 * kBwdRegsHigh <= kBwdThreads * 168, "setmaxnreg split exceeds the launch allocation");
+
 constexpr uint32_t kKidBsAttnBwd = 7;
 constexpr uint32_t kBwdSuspendNs = 2000;  // suspend hint of the compute and MMA waits (woken at completion)
 // Eighths of the exponentials of P computed on the FMA pipe (ex2_poly2) instead of the MUFU, in both passes.
@@ -280,7 +287,7 @@ struct BwdDqShape {
 };
 
 template <bool kF16, int kD>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     bsattn_bwd_dq_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                          const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                          const AttnBwdArgs a) {
@@ -346,7 +353,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   WaitCtl ctl{abort_flag, a.err, a.timeout_ns, kKidBsAttnBwd};
-  if (warp < 4) ptx::setmaxnreg_dec<kAttnRegsLow>();
+  if (warp < 4) ptx::setmaxnreg_dec<kBwdRegsLow>();
 
   // item -> (bh, query block), longest rows (last blocks under a causal mask) first
   auto item_of = [&](int item, int& bh, int& qb, int& j0, int& n) {
@@ -491,7 +498,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ dS = P (dP - Delta), dQ out
-    ptx::setmaxnreg_inc<kAttnRegsHigh>();
+    ptx::setmaxnreg_inc<kBwdRegsHigh>();
     const int x = (warp - 4) >> 2;  // key half: positions [64x, 64x + 64)
     const int q = warp & 3;
     const int r = 32 * q + lane;    // query row within the block == TMEM lane
@@ -595,7 +602,7 @@ struct BwdDkdvShape {
 };
 
 template <bool kF16, int kD>
-__global__ void __launch_bounds__(kAttnThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
     bsattn_bwd_dkdv_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                            const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmdO,
                            const AttnBwdArgs a) {
@@ -662,7 +669,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem_base = *tmem_holder;
   WaitCtl ctl{abort_flag, a.err, a.timeout_ns, kKidBsAttnBwd};
-  if (warp < 4) ptx::setmaxnreg_dec<kAttnRegsLow>();
+  if (warp < 4) ptx::setmaxnreg_dec<kBwdRegsLow>();
 
   // item -> (bh, key block), column list [i0, i0 + n) of query blocks
   auto item_of = [&](int item, int& bh, int& kb, int& i0, int& n) {
@@ -825,7 +832,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     __syncwarp();
   } else if (warp >= 4) {
     // ------------------------------------------------------------------ P^T, dS^T, dK / dV out
-    ptx::setmaxnreg_inc<kAttnRegsHigh>();
+    ptx::setmaxnreg_inc<kBwdRegsHigh>();
     const int x = (warp - 4) >> 2;  // query half (positions [64x, 64x + 64))
     const int q = warp & 3;
     const int r = 32 * q + lane;    // key row within the block == TMEM lane

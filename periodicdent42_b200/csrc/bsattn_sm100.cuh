@@ -1,24 +1,35 @@
-// Block-sparse attention forward for sm_100a (bf16 in/out, fp32 online softmax), 128x128 blocks, D = 128.
+// Block-sparse attention forward for sm_100a (fp16 / bf16 in and out, fp32 online softmax), 128x128 blocks,
+// head dim 64 or 128.
 //
-// Work item = (b, h) pair and TWO query block-rows of it ("streams" A and B, rows 2t+1 and 2t counted from
-// the end, so the longest rows of a causal pattern come first). For every nonzero key block j of a stream's
-// mask row the CTA computes
-//     S_j = Q K_j^T                 tcgen05.mma 128x128x16 x 8 into the stream's TMEM S buffer
-//     P_j = exp2(S_j * c - m)       online softmax, one query row per thread; P (bf16) is written back into
-//                                   the first 64 columns of the stream's S buffer in TMEM (tcgen05.st)
+// Work item = one query block-row of one (b, h) pair (head-major; the longest rows of a causal pattern first). For
+// every nonzero key block j of the row's mask the CTA computes
+//     S_j = Q K_j^T                 tcgen05.mma 128x128x16 x (D/16) into TMEM S buffer j % 2
+//     P_j = exp2(S_j * c - m)       online softmax, one query row per thread pair; P (16-bit) is written back into
+//                                   the first 64 columns of the same S buffer (tcgen05.st)
 //     O  += P_j V_j                 tcgen05.mma with A = P from TMEM, V an MN-major shared-memory operand
-// and writes O / l as bf16. Only nonzero blocks are loaded (TMA through a 5-slot K/V ring).
+// and writes O / l. Only nonzero blocks are loaded (TMA through a 5-slot K/V ring).
 //
-// Roles (12 warps): warp 0 TMA producer, warp 1 TMEM owner + MMA issuer, warps 4-7 softmax of stream A,
-// warps 8-11 softmax of stream B (warp w reads TMEM lanes 32*(w%4)..+31). Per block j the MMA warp issues
-// PV_A(j), S_A(j+1), PV_B(j), S_B(j+1): tcgen05.mma ops of one thread execute in issue order, so S_A(j+1) may
-// overwrite the TMEM columns PV_A(j) reads, and the two streams interleave so that one stream's softmax
-// overlaps the other stream's tensor work. TMEM: S/P_A [0,128), S/P_B [128,256), O_A [256,384), O_B [384,512).
+// Why this shape: one thread issues a 128x128x16 tcgen05.mma only every ~115-160 SM cycles while the tensor pipe
+// finishes it in 64, and two to four issuing warps bring the aggregate back to 68-84 cycles (measured on B200). So
+// the S MMAs and the PV MMAs have an issuing thread each (warps 1 and 2), and S is double-buffered in TMEM, so
+// S_{j+1} is computed while the softmax of block j runs. The softmax itself is split across two warps per row:
+// warps 4-7 take keys 0-63, warps 8-11 keys 64-127 of the rows of their TMEM lane quarter, and exchange each row's
+// partial max through two spare TMEM columns. A cycle trace of this kernel on the attention workload puts a block
+// at ~2000-2250 SM cycles, set by the softmax (TMEM load ~250, max ~200, exchange ~300-550, exponentials ~950 --
+// the MUFU of a sub-partition shared by the two halves -- and ~200 per barrier wait), against 1024 cycles of tensor
+// work. Variants measured slower on B200: speculative exponentials before the exchange (735 vs 890 TFLOPS), P in
+// its own TMEM buffers with the exchange in shared memory and one Q buffer (832 vs 887), and independent halves
+// with one O accumulator each (no exchange; P aliased onto S, so S_{j+2} waits for PV_j: 850 vs 876).
 //
-// Softmax: the reference max moves only when a block raises it by more than 8 (log2 units), so P <= 2^8 and
-// O is rescaled in TMEM only on those moves. Scale, sums and the polynomial use packed fp32x2 FMA/ADD; row
-// max uses three-input max. exp2 runs on the MUFU for 3/4 of the elements and on the FMA pipe for 1/4
-// (ex2_poly2 below), balancing the MUFU against instruction issue.
+// Roles (16 warps): warp 0 TMA producer, warp 1 TMEM owner + S issuer, warp 2 PV issuer, warp 3 idle, warps 4-11
+// softmax, warps 12-15 output (O / l from TMEM to global once a row's last PV completed, so the softmax warps go
+// straight on to the next row). TMEM: S buffers [0,128) and [128,256), O [256, 256 + D), exchange columns
+// [384, 392). Shared memory: Q x 2, the K/V ring, barriers, and the row sums / maxima handed to the output warps.
+//
+// Softmax: the reference max moves only when a block raises it by more than 8 (log2 units), so P <= 2^8 and O is
+// rescaled in TMEM only on those moves. Scale, sums and the polynomial use packed fp32x2 FMA/ADD; row max uses
+// three-input max. exp2 runs on the MUFU for 3/4 of the elements and on the FMA pipe for 1/4 (ex2_poly2 below),
+// balancing the MUFU against instruction issue.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -29,7 +40,7 @@
 namespace bsk {
 
 constexpr int kAttnBlk = 128;
-constexpr int kAttnThreads = 384;
+constexpr int kAttnThreads = 512;
 constexpr int kAttnChunk = kAttnBlk * 64 * 2;  // 16 KB: 128 rows x 64 columns (one 128-B swizzle atom wide)
 constexpr int kAttnKVSlots = 5;
 // Eighths of the exponentials computed on the FMA pipe (ex2_poly2) instead of the MUFU.
@@ -44,16 +55,20 @@ struct AttnShape {
   static_assert(kD == 64 || kD == 128, "head dim 64 or 128");
   static constexpr int kTile = kAttnBlk * kD * 2;  // one 128 x D tile: kD / 64 chunks of 16 KB
   static constexpr int kChunks = kD / 64;
-  static constexpr int kSmemBytes = 1024 + kTile * (2 /*Q*/ + kAttnKVSlots) + 256;
+  static constexpr int kSmemBytes = 1024 + kTile * (2 /*Q*/ + kAttnKVSlots) + 512 + 3 * 128 * 4;
   static constexpr uint32_t kFmt = kF16 ? 0u : 1u;  // tcgen05 kind::f16 A/B format: 0 f16, 1 bf16
 };
 constexpr int kAttnSmemBytes = AttnShape<false, 128>::kSmemBytes;  // largest instantiation
 constexpr int kAttnTmemCols = 512;
-constexpr uint32_t kAttnRegsLaunch = 168;  // 65536 / 384, rounded down to a multiple of 8
-constexpr uint32_t kAttnRegsLow = 112;
-constexpr uint32_t kAttnRegsHigh = 184;
-static_assert(128 * kAttnRegsLow + 256 * kAttnRegsHigh <= kAttnThreads * kAttnRegsLaunch,
+constexpr uint32_t kAttnTmemO = 256;  // O accumulator columns [256, 256 + D)
+constexpr uint32_t kAttnTmemX = 384;  // exchange columns: 2 slots x 2 halves
+constexpr uint32_t kAttnRegsLaunch = 128;  // 65536 / 512
+constexpr uint32_t kAttnRegsLow = 80;      // producer and MMA issuers
+constexpr uint32_t kAttnRegsHigh = 168;    // softmax warpgroups
+constexpr uint32_t kAttnRegsOut = 96;      // output warpgroup
+static_assert(128 * (kAttnRegsLow + 2 * kAttnRegsHigh + kAttnRegsOut) <= kAttnThreads * kAttnRegsLaunch,
               "setmaxnreg split exceeds the launch allocation");
+static_assert(AttnShape<false, 128>::kSmemBytes <= 232448, "shared memory above the 227 KB per-CTA limit");
 
 struct AttnArgs {
   void* O;            // fp16 or bf16 [B*H*S, D]
@@ -62,40 +77,28 @@ struct AttnArgs {
   const int* col_idx;
   int S;              // sequence length
   int nqb;            // S / 128
-  int items_per_pair; // ceil(nqb / 2)
   int bh_begin;       // first (b,h) pair of this launch
-  int num_items;      // (#pairs) * items_per_pair
+  int num_items;      // (#pairs) * nqb
   float scale_log2;   // softmax scale * log2(e)
   int causal_diag;
   uint32_t* err;
   uint64_t timeout_ns;
 };
 
-struct AttnStream {
-  int qb;  // query block-row (-1: no row)
-  int j0;  // first nonzero of the row
-  int n;   // nonzero blocks of the row
-};
-
-// Work item -> (bh, two query block-rows). Head-major, so concurrent CTAs share a head's K/V in L2.
-__device__ __forceinline__ void attn_item(const AttnArgs& a, int item, int& bh, AttnStream& sa, AttnStream& sb) {
-  bh = a.bh_begin + item / a.items_per_pair;
-  const int t = item % a.items_per_pair;
-  sa.qb = a.nqb - 1 - 2 * t;
-  sb.qb = a.nqb - 2 - 2 * t;
-  const int pa = bh * a.nqb + sa.qb;
-  sa.j0 = __ldg(&a.row_ptr[pa]);
-  sa.n = __ldg(&a.row_ptr[pa + 1]) - sa.j0;
-  if (sb.qb >= 0) {
-    sb.j0 = __ldg(&a.row_ptr[pa - 1]);
-    sb.n = sa.j0 - sb.j0;
-  } else {
-    sb.j0 = 0;
-    sb.n = 0;
-  }
-  sa.n = max(sa.n, 0);
-  sb.n = max(sb.n, 0);
+// Work item -> (bh, query block-row qb, first nonzero j0, nonzero count n). Head-major, so concurrent CTAs share a
+// head's K/V in L2; within a head the last rows (the longest of a causal pattern) come first.
+__device__ __forceinline__ void attn_row(const AttnArgs& a, int item, int& bh, int& qb, int& j0, int& n) {
+  bh = a.bh_begin + item / a.nqb;
+  qb = a.nqb - 1 - item % a.nqb;
+  const int p = bh * a.nqb + qb;
+  j0 = __ldg(&a.row_ptr[p]);
+  n = max(__ldg(&a.row_ptr[p + 1]) - j0, 0);
 }
+
+// Position of a row's tiles in the K/V ring sequence (t = 0 .. 2n-1 within the row): K_0, then K_j, V_{j-1} for
+// j = 1 .. n-1, then V_{n-1}. The producer pushes in this order; each issuer counts through it and takes its own.
+__device__ __forceinline__ int attn_k_pos(int j) { return j == 0 ? 0 : 2 * j - 1; }
+__device__ __forceinline__ int attn_v_pos(int j, int n) { return j == n - 1 ? 2 * n - 1 : 2 * j + 2; }
 
 __device__ __forceinline__ float ex2_approx(float x) {
   float y;
@@ -172,41 +175,53 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
                         const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
   using Sh = AttnShape<kF16, kD>;
   constexpr int kAttnTile = Sh::kTile;
+  constexpr int kHalfD = kD / 2;  // O columns a softmax warp writes
   constexpr uint32_t IDESC_S = ptx::instr_desc(128, 128, Sh::kFmt, Sh::kFmt, 0, 0);  // K = D, both K-major
   constexpr uint32_t IDESC_PV = ptx::instr_desc(128, kD, Sh::kFmt, Sh::kFmt, 0, 1);  // N = D, V MN-major
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;                       // [2] Q_A, Q_B
+  uint8_t* sQ = smem;                       // [2] Q of alternate rows
   uint8_t* sKV = sQ + 2 * kAttnTile;        // [kAttnKVSlots]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kAttnKVSlots * kAttnTile);
-  uint64_t* q_full = bars + 0;
-  uint64_t* q_empty = bars + 1;
-  uint64_t* kv_full = bars + 2;                 // [3]
-  uint64_t* kv_empty = bars + 2 + kAttnKVSlots;  // [3]
-  uint64_t* s_full = bars + 2 + 2 * kAttnKVSlots;  // [2] per stream: S_j in TMEM
-  uint64_t* p_full = s_full + 2;                   // [2] P_j written to TMEM (4 warp arrivals)
-  uint64_t* o_done = p_full + 2;                   // [2] last PV of the stream's row completed
-  uint64_t* drain = o_done + 2;
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* q_full = bars + 0;                       // [2]
+  uint64_t* q_empty = bars + 2;                      // [2] the row's last S MMAs completed
+  uint64_t* kv_full = bars + 4;                      // [kAttnKVSlots]
+  uint64_t* kv_empty = kv_full + kAttnKVSlots;       // [kAttnKVSlots]
+  uint64_t* s_full = kv_empty + kAttnKVSlots;        // [2] S_j in TMEM buffer j % 2
+  uint64_t* s_free = s_full + 2;                     // [2] PV_j completed: buffer j % 2 free, O holds block j
+  uint64_t* p_full = s_free + 2;                     // [2] P_j written (8 softmax warps)
+  uint64_t* o_done = p_full + 2;                     // last PV of a row completed
+  uint64_t* xbar = o_done + 1;                       // [4 quarters][2 slots]: both halves stored their value
+  uint64_t* drain = xbar + 8;                        // [2] issuers' final commits
+  uint64_t* l_ready = drain + 2;                     // a row's sums and max are in shared memory (8 warps)
+  uint64_t* o_free = l_ready + 1;                    // the output warps read a row's O (4 warps)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(o_free + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
+  static_assert(4 + 2 * kAttnKVSlots + 2 + 2 + 2 + 1 + 8 + 2 + 2 <= 63, "barrier area exceeds its 512 bytes");
+  float* l_part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512);  // [2 halves][128 rows]
+  float* m_row = l_part + 256;                                                         // [128 rows]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    ptx::mbar_init(ptx::smem_u32(q_full), 1);
-    ptx::mbar_init(ptx::smem_u32(q_empty), 1);
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&q_full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&q_empty[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&s_full[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&s_free[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&p_full[s]), 8);
+      ptx::mbar_init(ptx::smem_u32(&drain[s]), 1);
+    }
     for (int s = 0; s < kAttnKVSlots; ++s) {
       ptx::mbar_init(ptx::smem_u32(&kv_full[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&kv_empty[s]), 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      ptx::mbar_init(ptx::smem_u32(&s_full[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&p_full[s]), 4);
-      ptx::mbar_init(ptx::smem_u32(&o_done[s]), 1);
-    }
-    ptx::mbar_init(ptx::smem_u32(drain), 1);
+    ptx::mbar_init(ptx::smem_u32(o_done), 1);
+    ptx::mbar_init(ptx::smem_u32(l_ready), 8);
+    ptx::mbar_init(ptx::smem_u32(o_free), 4);
+    for (int s = 0; s < 8; ++s) ptx::mbar_init(ptx::smem_u32(&xbar[s]), 2);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -225,15 +240,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
   WaitCtl ctl{abort_flag, a.err, a.timeout_ns, kKidBsAttn};
 
-  // Launch allocation 384 x 168 = 64512 registers; warpgroup 0 (producer, MMA, 2 idle warps) drops to
-  // kAttnRegsLow per thread, the two softmax warpgroups rise to kAttnRegsHigh (sum checked at compile time).
-  static_assert(kAttnThreads == 384, "register split assumes 12 warps");
+  // Launch allocation 512 x 128 registers; warpgroup 0 (producer, issuers, 1 idle warp) drops to kAttnRegsLow per
+  // thread and the output warpgroup to kAttnRegsOut, the two softmax warpgroups rise to kAttnRegsHigh (sum checked
+  // at compile time).
+  static_assert(kAttnThreads == 512, "register split assumes 16 warps");
   if (warp < 4) ptx::setmaxnreg_dec<kAttnRegsLow>();
+  if (warp >= 12) ptx::setmaxnreg_dec<kAttnRegsOut>();
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer (one thread)
     if (lane == 0) {
-      uint32_t q_phase = 0, slot = 0, slot_phase = 0, q_issued = 0, kv_issued = 0;
+      uint32_t slot = 0, slot_phase = 0, q_issued = 0, kv_issued = 0;
       bool ok = true;
       const uint32_t kv0 = ptx::smem_u32(sKV);
       auto push = [&](const CUtensorMap* m, int row) -> bool {
@@ -247,201 +264,203 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         if (++slot == kAttnKVSlots) { slot = 0; slot_phase ^= 1; }
         return true;
       };
-      // key block j of a stream -> first row of its K/V tile in the [B*H*S, D] view
-      auto kvrow = [&](int bh, const AttnStream& st, int j) -> int {
-        int kb = __ldg(&a.col_idx[st.j0 + j]);
-        if (kb < 0 || kb >= a.nqb) {  // out-of-range index: flag it; the load reads zero fill
-          atomicCAS(a.err, 0u, kErrBounds | (kKidBsAttn << 8) | (7u << 16));
-          kb = a.nqb;
-        }
-        return bh * a.S + kb * kAttnBlk;
-      };
       for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
-        int bh;
-        AttnStream A, B;
-        attn_item(a, item, bh, A, B);
-        if (A.n + B.n == 0) continue;
-        ok = wait_bounded<false, 512>(ptx::smem_u32(q_empty), q_phase ^ 1, ctl, 1);
+        int bh, qb, j0, n;
+        attn_row(a, item, bh, qb, j0, n);
+        if (n == 0) continue;
+        const uint32_t qbuf = q_issued & 1;
+        ok = wait_bounded<false, 512>(ptx::smem_u32(&q_empty[qbuf]), ((q_issued >> 1) & 1) ^ 1, ctl, 1);
         if (!ok) break;
-        const uint32_t qf = ptx::smem_u32(q_full);
-        ptx::mbar_arrive_expect_tx(qf, (A.n > 0 ? kAttnTile : 0) + (B.n > 0 ? kAttnTile : 0));
+        const uint32_t qf = ptx::smem_u32(&q_full[qbuf]);
+        ptx::mbar_arrive_expect_tx(qf, kAttnTile);
         const int row0 = bh * a.S;
 #pragma unroll
-        for (int c = 0; c < Sh::kChunks; ++c) {
-          if (A.n > 0)
-            ptx::tma_load_2d(ptx::smem_u32(sQ) + c * kAttnChunk, &tmQ, qf, 64 * c, row0 + A.qb * kAttnBlk);
-          if (B.n > 0)
-            ptx::tma_load_2d(ptx::smem_u32(sQ) + kAttnTile + c * kAttnChunk, &tmQ, qf, 64 * c,
-                             row0 + B.qb * kAttnBlk);
-        }
+        for (int c = 0; c < Sh::kChunks; ++c)
+          ptx::tma_load_2d(ptx::smem_u32(sQ) + qbuf * kAttnTile + c * kAttnChunk, &tmQ, qf, 64 * c,
+                           row0 + qb * kAttnBlk);
         ++q_issued;
-        q_phase ^= 1;
-        // Same order as the MMA warp consumes: K_A0, K_B0, then per j: V_A(j), K_A(j+1), V_B(j), K_B(j+1).
-        if (A.n > 0) ok = ok && push(&tmK, kvrow(bh, A, 0));
-        if (B.n > 0) ok = ok && push(&tmK, kvrow(bh, B, 0));
-        const int n = max(A.n, B.n);
-        for (int j = 0; j < n && ok; ++j) {
-          if (j < A.n) ok = ok && push(&tmV, kvrow(bh, A, j));
-          if (j + 1 < A.n) ok = ok && push(&tmK, kvrow(bh, A, j + 1));
-          if (j < B.n) ok = ok && push(&tmV, kvrow(bh, B, j));
-          if (j + 1 < B.n) ok = ok && push(&tmK, kvrow(bh, B, j + 1));
+        // key block j of the row -> first row of its K/V tile in the [B*H*S, D] view
+        auto kvrow = [&](int j) -> int {
+          int kb = __ldg(&a.col_idx[j0 + j]);
+          if (kb < 0 || kb >= a.nqb) {  // out-of-range index: flag it; the load reads zero fill
+            atomicCAS(a.err, 0u, kErrBounds | (kKidBsAttn << 8) | (7u << 16));
+            kb = a.nqb;
+          }
+          return row0 + kb * kAttnBlk;
+        };
+        ok = push(&tmK, kvrow(0));
+        for (int j = 1; j < n && ok; ++j) {
+          ok = push(&tmK, kvrow(j));
+          if (ok) ok = push(&tmV, kvrow(j - 1));
         }
+        if (ok) ok = push(&tmV, kvrow(n - 1));
       }
       // Drain loads still in flight.
       WaitCtl dctl = ctl;
       volatile int never = 0;
       dctl.abort = &never;
-      if (q_issued) wait_bounded(ptx::smem_u32(q_full), (q_issued - 1) & 1, dctl, 8);
+      for (uint32_t i = q_issued > 2 ? q_issued - 2 : 0; i < q_issued; ++i)
+        wait_bounded(ptx::smem_u32(&q_full[i & 1]), (i >> 1) & 1, dctl, 8);
       const uint32_t first = kv_issued > kAttnKVSlots ? kv_issued - kAttnKVSlots : 0;
       for (uint32_t i = first; i < kv_issued; ++i)
         wait_bounded(ptx::smem_u32(&kv_full[i % kAttnKVSlots]), (i / kAttnKVSlots) & 1, dctl, 8);
     }
     __syncwarp();
-  } else if (warp == 1) {
-    // ------------------------------------------------------------------ MMA issuer (one thread)
+  } else if (warp == 1 || warp == 2) {
+    // ------------------------------------------------------------------ MMA issuers (one thread each)
+    // warp 1: S_j = Q K_j^T into buffer j % 2, once PV_{j-2} has released it; warp 2: O += P_j V_j, once the
+    // softmax has written P_j. The two threads' MMAs interleave on the tensor pipe.
     if (lane == 0) {
-      uint32_t q_phase = 0, slot = 0, slot_phase = 0;
-      uint32_t p_uses[2] = {0, 0};
+      const bool s_role = warp == 1;
+      uint32_t g = 0, rows = 0, seq = 0;  // blocks, non-empty rows and ring positions passed
       bool ok = true;
-      const uint32_t sQa = ptx::smem_u32(sQ), kv0 = ptx::smem_u32(sKV);
-      const uint64_t qdesc0 = ptx::smem_desc(sQa, 16, 1024);              // Q, K: K-major
-      const uint64_t kvdesc_k0 = ptx::smem_desc(kv0, 16, 1024);
-      const uint64_t kvdesc_v0 = ptx::smem_desc(kv0, kAttnChunk, 1024);   // V: MN-major, 64-column slabs
-      auto advance = [&]() {
-        if (++slot == kAttnKVSlots) { slot = 0; slot_phase ^= 1; }
-      };
-      // A shared-memory access (an mbarrier poll included) issued after tcgen05.mma waits until the queued MMAs
-      // have been handed to the tensor pipe, so the pipe runs dry during every poll that follows an MMA group.
-      // The barrier waits of a block are therefore made back to back, before its MMAs: PV_x(j) and S_x(j+1)
-      // go out as one group of 16 behind one burst of waits (P_x(j), V_x(j), K_x(j+1)).
-      auto s_mmas = [&](int x, uint32_t sl) {  // S_x = Q_x K^T from ring slot sl
-        const uint64_t qd = qdesc0 + ((x * kAttnTile) >> 4), kd = kvdesc_k0 + ((sl * kAttnTile) >> 4);
-#pragma unroll
-        for (int k = 0; k < kD / 16; ++k) {  // K = D in steps of 16: 4 steps per 64-column chunk
-          const uint32_t off = ((k >> 2) * kAttnChunk + (k & 3) * 32) >> 4;
-          ptx::mma_f16_ss(tmem_base + x * 128, qd + off, kd + off, IDESC_S, k != 0);
-        }
-      };
-      auto issue_s = [&](int x) -> bool {  // S_x(0) of a row
-        const uint32_t sk = slot;
-        if (!wait_bounded(ptx::smem_u32(&kv_full[sk]), slot_phase, ctl, 11)) return false;
-        advance();
-        ptx::tc_fence_after();
-        s_mmas(x, sk);
-        ptx::mma_commit(ptx::smem_u32(&kv_empty[sk]));
-        ptx::mma_commit(ptx::smem_u32(&s_full[x]));
-        return true;
-      };
-      // O_x += P_x(j) V_x(j) (P from TMEM), then (next) S_x(j+1), which may overwrite the P columns: in issue order.
-      auto issue_pv_s = [&](int x, bool first, bool last, bool next) -> bool {
-        if (!wait_bounded(ptx::smem_u32(&p_full[x]), p_uses[x] & 1, ctl, 12)) return false;
-        ++p_uses[x];
-        const uint32_t sv = slot;
-        if (!wait_bounded(ptx::smem_u32(&kv_full[sv]), slot_phase, ctl, 13)) return false;
-        advance();
-        uint32_t sk = 0;
-        if (next) {
-          sk = slot;
-          if (!wait_bounded(ptx::smem_u32(&kv_full[sk]), slot_phase, ctl, 11)) return false;
-          advance();
-        }
-        ptx::tc_fence_after();
-        const uint64_t vd = kvdesc_v0 + ((sv * kAttnTile) >> 4);
-#pragma unroll
-        for (int k = 0; k < 8; ++k)  // K step k: P columns [8k, 8k+8) hold kv positions [16k, 16k+16)
-          ptx::mma_f16_ts(tmem_base + 256 + x * 128, tmem_base + x * 128 + 8 * k, vd + ((k * 2048) >> 4), IDESC_PV,
-                          (first && k == 0) ? 0u : 1u);
-        ptx::mma_commit(ptx::smem_u32(&kv_empty[sv]));
-        if (last) ptx::mma_commit(ptx::smem_u32(&o_done[x]));
-        if (next) {
-          s_mmas(x, sk);
-          ptx::mma_commit(ptx::smem_u32(&kv_empty[sk]));
-          ptx::mma_commit(ptx::smem_u32(&s_full[x]));
-        }
-        return true;
-      };
+      const uint32_t kv0 = ptx::smem_u32(sKV);
+      const uint64_t qdesc0 = ptx::smem_desc(ptx::smem_u32(sQ), 16, 1024);  // Q, K: K-major
+      const uint64_t kdesc0 = ptx::smem_desc(kv0, 16, 1024);
+      const uint64_t vdesc0 = ptx::smem_desc(kv0, kAttnChunk, 1024);       // V: MN-major, 64-column slabs
       for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
-        int bh;
-        AttnStream A, B;
-        attn_item(a, item, bh, A, B);
-        if (A.n + B.n == 0) continue;
-        ok = wait_bounded(ptx::smem_u32(q_full), q_phase, ctl, 14);
-        if (!ok) break;
-        q_phase ^= 1;
-        // Ring order (the producer's): K_A(0), K_B(0), then per j: V_A(j), K_A(j+1), V_B(j), K_B(j+1).
-        if (A.n > 0) ok = ok && issue_s(0);
-        if (B.n > 0) ok = ok && issue_s(1);
-        const int n = max(A.n, B.n);
-        for (int j = 0; j < n && ok; ++j) {
-          if (j < A.n) ok = ok && issue_pv_s(0, j == 0, j + 1 == A.n, j + 1 < A.n);
-          if (j < B.n) ok = ok && issue_pv_s(1, j == 0, j + 1 == B.n, j + 1 < B.n);
+        int bh, qb, j0, n;
+        attn_row(a, item, bh, qb, j0, n);
+        if (n == 0) continue;
+        const uint32_t qbuf = rows & 1;
+        if (s_role) {
+          ok = wait_bounded(ptx::smem_u32(&q_full[qbuf]), (rows >> 1) & 1, ctl, 14);
+          if (!ok) break;
         }
-        if (ok) ptx::mma_commit(ptx::smem_u32(q_empty));
+        for (int j = 0; j < n && ok; ++j, ++g) {
+          const uint32_t b = g & 1;
+          if (s_role) {
+            if (g >= 2) {  // PV_{g-2} read P from this buffer
+              ok = wait_bounded(ptx::smem_u32(&s_free[b]), ((g - 2) >> 1) & 1, ctl, 11);
+              if (!ok) break;
+            }
+            const uint32_t pos = seq + attn_k_pos(j);
+            const uint32_t sl = pos % kAttnKVSlots;
+            ok = wait_bounded(ptx::smem_u32(&kv_full[sl]), (pos / kAttnKVSlots) & 1, ctl, 12);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            const uint64_t qd = qdesc0 + ((qbuf * kAttnTile) >> 4), kd = kdesc0 + ((sl * kAttnTile) >> 4);
+#pragma unroll
+            for (int k = 0; k < kD / 16; ++k) {  // K = D in steps of 16: 4 steps per 64-column chunk
+              const uint32_t off = ((k >> 2) * kAttnChunk + (k & 3) * 32) >> 4;
+              ptx::mma_f16_ss(tmem_base + 128 * b, qd + off, kd + off, IDESC_S, k != 0);
+            }
+            ptx::mma_commit(ptx::smem_u32(&kv_empty[sl]));
+            ptx::mma_commit(ptx::smem_u32(&s_full[b]));
+            if (j == n - 1) ptx::mma_commit(ptx::smem_u32(&q_empty[qbuf]));
+          } else {
+            if (j == 0 && rows > 0) {  // the first PV of a row overwrites O: the previous row's O must be read
+              ok = wait_bounded(ptx::smem_u32(o_free), (rows - 1) & 1, ctl, 17);
+              if (!ok) break;
+            }
+            ok = wait_bounded(ptx::smem_u32(&p_full[b]), (g >> 1) & 1, ctl, 13);
+            if (!ok) break;
+            const uint32_t pos = seq + attn_v_pos(j, n);
+            const uint32_t sl = pos % kAttnKVSlots;
+            ok = wait_bounded(ptx::smem_u32(&kv_full[sl]), (pos / kAttnKVSlots) & 1, ctl, 15);
+            if (!ok) break;
+            ptx::tc_fence_after();
+            const uint64_t vd = vdesc0 + ((sl * kAttnTile) >> 4);
+#pragma unroll
+            for (int k = 0; k < 8; ++k)  // K step k: P columns [8k, 8k+8) hold key positions [16k, 16k+16)
+              ptx::mma_f16_ts(tmem_base + kAttnTmemO, tmem_base + 128 * b + 8 * k, vd + ((k * 2048) >> 4),
+                              IDESC_PV, (j == 0 && k == 0) ? 0u : 1u);
+            ptx::mma_commit(ptx::smem_u32(&kv_empty[sl]));
+            ptx::mma_commit(ptx::smem_u32(&s_free[b]));
+            if (j == n - 1) ptx::mma_commit(ptx::smem_u32(o_done));
+          }
+        }
+        seq += 2 * n;
+        ++rows;
       }
-      ptx::mma_commit(ptx::smem_u32(drain));
+      const uint32_t dr = ptx::smem_u32(&drain[s_role ? 0 : 1]);
+      ptx::mma_commit(dr);
       WaitCtl dctl = ctl;
       volatile int never = 0;
       dctl.abort = &never;
-      wait_bounded(ptx::smem_u32(drain), 0, dctl, 15);
+      wait_bounded(dr, 0, dctl, 16);
     }
     __syncwarp();
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------------ softmax + output (warps 4..11)
+  } else if (warp >= 4 && warp < 12) {
+    // ------------------------------------------------------------------ softmax (warps 4..11)
     ptx::setmaxnreg_inc<kAttnRegsHigh>();
-    const int x = (warp - 4) >> 2;  // stream of this warp group
-    const int q = warp & 3;
-    const int r = 32 * q + lane;  // query row within the block == TMEM lane
+    const int h = (warp - 4) >> 2;  // key half: S columns [64 h, 64 h + 64)
+    const int q = warp & 3;         // TMEM lane quarter
+    const int r = 32 * q + lane;    // query row within the block == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
-    const uint32_t tS = tmem_base + x * 128 + lane_off;
-    const uint32_t tO = tmem_base + 256 + x * 128 + lane_off;
+    const uint32_t tO = tmem_base + kAttnTmemO + lane_off + h * kHalfD;  // this warp's O columns
+    const uint32_t tX = tmem_base + kAttnTmemX + lane_off;
     const float c = a.scale_log2;
-    uint32_t s_cnt = 0, o_cnt = 0;
+    uint32_t g = 0, rows = 0, x_cnt = 0;
     bool ok = true;
-    for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
-      int bh;
-      AttnStream A, B;
-      attn_item(a, item, bh, A, B);
-      const AttnStream st = x == 0 ? A : B;
-      if (st.qb < 0) continue;
-      const int64_t grow = static_cast<int64_t>(bh) * a.S + st.qb * kAttnBlk + r;
-      uint16_t* orow = static_cast<uint16_t*>(a.O) + grow * kD;
-      if (st.n <= 0) {
+    // Row-wise exchange with the warp of the other key half (same rows): store this half's value in TMEM, meet on
+    // the quarter's barrier of this slot, read the other half's value. Slots alternate, so a value is read before
+    // its column is written again.
+    auto exchange = [&](float v, float& other) -> bool {
+      const uint32_t slot = x_cnt & 1;
+      ptx::tmem_st_32x32b_x1(tX + 4 * slot + h, __float_as_uint(v));
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      __syncwarp();
+      const uint32_t xb = ptx::smem_u32(&xbar[q * 2 + slot]);
+      if (lane == 0) ptx::mbar_arrive(xb);
+      if (!warp_wait_bounded(xb, (x_cnt >> 1) & 1, ctl, 23)) return false;
+      ++x_cnt;
+      ptx::tc_fence_after();
+      other = __uint_as_float(ptx::tmem_ld_32x32b_x1(tX + 4 * slot + (h ^ 1)));
+      ptx::tmem_wait_ld();
+      return true;
+    };
+    // The next row's bounds are looked up one row ahead (their loads overlap this row's blocks).
+    int item = blockIdx.x;
+    int bh = 0, qb = 0, j0 = 0, n = 0;
+    if (item < a.num_items) attn_row(a, item, bh, qb, j0, n);
+    for (; item < a.num_items && ok; item += gridDim.x) {
+      const int rbh = bh, rqb = qb, rj0 = j0, rn = n;  // this row; (bh, qb, j0, n) become the next row's
+      if (item + static_cast<int>(gridDim.x) < a.num_items) attn_row(a, item + gridDim.x, bh, qb, j0, n);
+      const int64_t grow = static_cast<int64_t>(rbh) * a.S + rqb * kAttnBlk + r;
+      uint16_t* orow = static_cast<uint16_t*>(a.O) + grow * kD + h * kHalfD;
+      if (rn == 0) {
         const uint4 z = make_uint4(0, 0, 0, 0);
 #pragma unroll
-        for (int cc = 0; cc < kD / 8; ++cc) reinterpret_cast<uint4*>(orow)[cc] = z;
-        if (a.lse) a.lse[grow] = -INFINITY;
+        for (int cc = 0; cc < kHalfD / 8; ++cc) reinterpret_cast<uint4*>(orow)[cc] = z;
+        if (a.lse && h == 0) a.lse[grow] = -INFINITY;
         continue;
       }
-      float m_run = -INFINITY, l_run = 0.0f;  // m_run in scaled log2 units
-      for (int j = 0; j < st.n; ++j) {
-        const int kb = __ldg(&a.col_idx[st.j0 + j]);
-        const bool diag = a.causal_diag && kb == st.qb;
-        // S_j complete; it was issued after PV_{j-1}, so O already holds block j-1's contribution.
-        ok = warp_wait_bounded(ptx::smem_u32(&s_full[x]), s_cnt & 1, ctl, 20);
+      float m_run = -INFINITY, l_run = 0.0f;  // m_run in scaled log2 units; l_run sums this half's keys
+      int cidx = 0;  // lane l: column index of nonzero (j & ~31) + l of the row (warp-level prefetch)
+      for (int j = 0; j < rn; ++j, ++g) {
+        if ((j & 31) == 0) cidx = (j + lane < rn) ? __ldg(&a.col_idx[rj0 + j + lane]) : 0;
+        const int kb = __shfl_sync(0xffffffffu, cidx, j & 31);
+        const bool diag = a.causal_diag && kb == rqb;
+        const uint32_t b = g & 1;
+        const uint32_t tS = tmem_base + 128 * b + lane_off;
+        ok = warp_wait_bounded(ptx::smem_u32(&s_full[b]), (g >> 1) & 1, ctl, 20);
         if (!ok) break;
-        ++s_cnt;
         ptx::tc_fence_after();
-        uint32_t sv[128];  // S row, loaded straight into the registers the softmax works in
-#pragma unroll
-        for (int cc = 0; cc < 4; ++cc)
-          ptx::tmem_ld_32x32b_x32(tS + cc * 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[cc * 32]));
-        ptx::tmem_wait_ld();
+        uint32_t sv[64];  // this half of the S row, loaded straight into the registers the softmax works in
+        ptx::tmem_ld_32x32b_x32(tS + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        ptx::tmem_ld_32x32b_x32(tS + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        ptx::tmem_wait_ld();  // (before the exchange: the other half overwrites columns 32..63 with P after it)
         float* v = reinterpret_cast<float*>(sv);
         if (diag) {
 #pragma unroll
-          for (int i = 0; i < 128; ++i)
-            if (i > r) v[i] = -INFINITY;
+          for (int i = 0; i < 64; ++i)
+            if (64 * h + i > r) v[i] = -INFINITY;
         }
-        // Row max and row sum as 8 independent partial chains (a single chain is 127 dependent ops deep).
+        // Row max as 8 independent partial chains, then the other half's partial max.
         float pm[8];
 #pragma unroll
         for (int k = 0; k < 8; ++k) pm[k] = v[k];
 #pragma unroll
-        for (int i = 8; i < 128; i += 16)
+        for (int i = 8; i < 64; i += 16)
 #pragma unroll
           for (int k = 0; k < 8; ++k) pm[k] = max3f(pm[k], v[i + k], v[i + 8 + k]);
-        const float mb = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
-        const float mbs = mb * c;
+        const float mh = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
+        float mo;
+        ok = exchange(mh, mo);
+        if (!ok) break;
+        const float mbs = fmaxf(mh, mo) * c;
         const bool move = mbs > m_run + 8.0f;
         float alpha = 1.0f;
         if (move) alpha = (m_run == -INFINITY) ? 0.0f : ex2_approx(m_run - mbs);
@@ -449,11 +468,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         const bool need_rescale = __any_sync(0xffffffffu, move && j > 0);
         const float m_sub = (m_run == -INFINITY) ? 0.0f : m_run;  // fully masked so far: P = 0, no NaN
         // exp2 on pairs: t = s * c - m by fma.f32x2; 3 of every 4 pairs on the MUFU, 1 on the FMA pipe.
-        // P is packed to bf16 pairs in place: pair k lands in sv[k], whose S value (element k <= i) is used.
+        // P is packed to 16-bit pairs in place: pair k lands in sv[k], whose S value (element k <= i) is used.
         const uint64_t c2 = f2_pack(c, c), nm2 = f2_pack(-m_sub, -m_sub);
         uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
-        for (int i = 0; i < 128; i += 2) {
+        for (int i = 0; i < 64; i += 2) {
           float t0, t1, e0, e1;
           f2_unpack(f2_fma(f2_pack(v[i], v[i + 1]), c2, nm2), t0, t1);
           if (((i >> 1) & 7) >= 8 - kAttnPolyEighths) {
@@ -473,10 +492,13 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           rs = lo + hi;
         }
         l_run = l_run * alpha + rs;
-        if (need_rescale) {  // O (complete through block j-1) *= alpha, in TMEM
+        if (need_rescale) {  // O *= alpha once it holds block j-1 (PV_{g-1} completed), this half's columns
+          ok = warp_wait_bounded(ptx::smem_u32(&s_free[(g - 1) & 1]), ((g - 1) >> 1) & 1, ctl, 21);
+          if (!ok) break;
+          ptx::tc_fence_after();
           const float al = move ? alpha : 1.0f;
 #pragma unroll 1
-          for (int cc = 0; cc < kD / 32; ++cc) {
+          for (int cc = 0; cc < kHalfD / 32; ++cc) {
             uint32_t u[32];
             ptx::tmem_ld_32x32b_x32(tO + cc * 32, u);
             ptx::tmem_wait_ld();
@@ -485,23 +507,49 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             ptx::tmem_st_32x32b_x32(tO + cc * 32, u);
           }
         }
-        // P row r (bf16 pairs) -> TMEM columns [0, 64) of this stream's S buffer.
-        ptx::tmem_st_32x32b_x32(tS, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-        ptx::tmem_st_32x32b_x32(tS + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+        // P of this half (32 packed columns) -> TMEM columns [32 h, 32 h + 32) of the S buffer.
+        ptx::tmem_st_32x32b_x32(tS + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&p_full[x]));
+        if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&p_full[b]));
       }
       if (!ok) break;
-      // Output: wait for the last PV of this row, then O / l -> bf16.
-      ok = warp_wait_bounded<false, 256>(ptx::smem_u32(&o_done[x]), o_cnt & 1, ctl, 22);
+      // Hand this half's row sum (and half 0's max, for the LSE) to the output warps. The previous row's values
+      // must have been read first (its O read completes after them).
+      if (rows > 0) {
+        ok = warp_wait_bounded(ptx::smem_u32(o_free), (rows - 1) & 1, ctl, 24);
+        if (!ok) break;
+      }
+      l_part[h * 128 + r] = l_run;
+      if (h == 0) m_row[r] = m_run;
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(l_ready));
+      ++rows;
+    }
+  } else if (warp >= 12) {
+    // ------------------------------------------------------------------ output (warps 12..15)
+    const int q = warp & 3;
+    const int r = 32 * q + lane;
+    const uint32_t tO = tmem_base + kAttnTmemO + (static_cast<uint32_t>(32 * q) << 16);
+    uint32_t rows = 0;
+    bool ok = true;
+    for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
+      int bh, qb, j0, n;
+      attn_row(a, item, bh, qb, j0, n);
+      if (n == 0) continue;  // written by the softmax warps
+      ok = warp_wait_bounded<false, 256>(ptx::smem_u32(l_ready), rows & 1, ctl, 25);
+      if (ok) ok = warp_wait_bounded<false, 256>(ptx::smem_u32(o_done), rows & 1, ctl, 22);
       if (!ok) break;
-      ++o_cnt;
+      ++rows;
       ptx::tc_fence_after();
-      const float inv_l = l_run > 0.0f ? 1.0f / l_run : 0.0f;
-      // l_run sums 2^(s*c - m_run) whatever m_run lagged behind, so m_run + log2(l_run) is exact
-      if (a.lse) a.lse[grow] = l_run > 0.0f ? (m_run + log2f(l_run)) * 0.6931471805599453f : -INFINITY;
+      const float l_tot = l_part[r] + l_part[128 + r];  // half 0 + half 1, a fixed order
+      const float m_run = m_row[r];
+      const int64_t grow = static_cast<int64_t>(bh) * a.S + qb * kAttnBlk + r;
+      uint16_t* orow = static_cast<uint16_t*>(a.O) + grow * kD;
+      const float inv_l = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
+      // l sums 2^(s*c - m_run) whatever m_run lagged behind, so m_run + log2(l) is exact
+      if (a.lse) a.lse[grow] = l_tot > 0.0f ? (m_run + log2f(l_tot)) * 0.6931471805599453f : -INFINITY;
 #pragma unroll 1
       for (int cc = 0; cc < kD / 32; ++cc) {
         uint32_t u[32];
@@ -509,14 +557,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         ptx::tmem_wait_ld();
         uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
 #pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          dst[g] = make_uint4(pack2<kF16>(__uint_as_float(u[8 * g + 0]) * inv_l, __uint_as_float(u[8 * g + 1]) * inv_l),
-                              pack2<kF16>(__uint_as_float(u[8 * g + 2]) * inv_l, __uint_as_float(u[8 * g + 3]) * inv_l),
-                              pack2<kF16>(__uint_as_float(u[8 * g + 4]) * inv_l, __uint_as_float(u[8 * g + 5]) * inv_l),
-                              pack2<kF16>(__uint_as_float(u[8 * g + 6]) * inv_l, __uint_as_float(u[8 * g + 7]) * inv_l));
+        for (int gg = 0; gg < 4; ++gg) {
+          dst[gg] = make_uint4(
+              pack2<kF16>(__uint_as_float(u[8 * gg + 0]) * inv_l, __uint_as_float(u[8 * gg + 1]) * inv_l),
+              pack2<kF16>(__uint_as_float(u[8 * gg + 2]) * inv_l, __uint_as_float(u[8 * gg + 3]) * inv_l),
+              pack2<kF16>(__uint_as_float(u[8 * gg + 4]) * inv_l, __uint_as_float(u[8 * gg + 5]) * inv_l),
+              pack2<kF16>(__uint_as_float(u[8 * gg + 6]) * inv_l, __uint_as_float(u[8 * gg + 7]) * inv_l));
         }
       }
       ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(o_free));
     }
   }
 

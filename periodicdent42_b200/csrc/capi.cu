@@ -1125,9 +1125,8 @@ int bsattn_launch(bool f16, const void* Q, const void* K, const void* V, void* O
   a.col_idx = col_idx;
   a.S = S;
   a.nqb = S / blk;
-  a.items_per_pair = (a.nqb + 1) / 2;
   a.bh_begin = bh_begin;
-  a.num_items = (bh_end - bh_begin) * a.items_per_pair;
+  a.num_items = (bh_end - bh_begin) * a.nqb;
   a.scale_log2 = scale * 1.4426950408889634f;
   a.causal_diag = causal_diag;
   a.err = st->err_word;
@@ -1598,8 +1597,8 @@ int bsk_bsattn_bwd(int dtype, const void* dO, const void* Q, const void* K, cons
 #define BSK_BWD(F16, DD)                                                                                            \
   do {                                                                                                              \
     bsattn_bwd_delta_kernel<F16, DD><<<dgrid, 256, 0, s>>>(dO16, O16, lse, delta, delta + rows, (int64_t)rows);     \
-    bsattn_bwd_dkdv_kernel<F16, DD><<<grid, kAttnThreads, BwdDkdvShape<F16, DD>::kSmemBytes, s>>>(tq, tk, tv, tdo, a); \
-    bsattn_bwd_dq_kernel<F16, DD><<<grid, kAttnThreads, BwdDqShape<F16, DD>::kSmemBytes, s>>>(tq, tk, tv, tdo, a);     \
+    bsattn_bwd_dkdv_kernel<F16, DD><<<grid, kBwdThreads, BwdDkdvShape<F16, DD>::kSmemBytes, s>>>(tq, tk, tv, tdo, a); \
+    bsattn_bwd_dq_kernel<F16, DD><<<grid, kBwdThreads, BwdDqShape<F16, DD>::kSmemBytes, s>>>(tq, tk, tv, tdo, a);     \
   } while (0)
   if (dtype == 1 && D == 128) BSK_BWD(true, 128);
   else if (dtype == 1) BSK_BWD(true, 64);
