@@ -653,7 +653,7 @@ int launch_pair_f16(const DeviceState& st, const SplitPlan& p, const __half* Ah,
   a.num_m_tiles = (M + kPairBM - 1) / kPairBM;
   a.num_n_tiles = (N + tn - 1) / tn;
   a.num_k_blocks = (kr + 63) / 64;
-  a.group_m = pick_group_m(a.num_m_tiles, p.kind);
+  a.group_m = pick_group_m(a.num_m_tiles, p.kind, p.kb_per_split * 64);
   a.k_splits = p.splits;
   a.kb_per_split = p.kb_per_split;
   a.split_stride = split_stride;

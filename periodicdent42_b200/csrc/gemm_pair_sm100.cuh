@@ -112,11 +112,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
   const uint32_t tmem_base = *tmem_holder;
 
   WaitCtl ctl{abort_flag, a.err, a.timeout_ns, KID};
-  // Work unit = (output tile, K split); the splits of one tile are adjacent units.
-  const int num_units = a.num_m_tiles * a.num_n_tiles * a.k_splits;
+  // Work unit = (output tile, K split), the split outer: units running at the same time cover the same K range of
+  // different tiles, so their A and B panels are shared in L2 as in an unsplit GEMM.
+  const int num_tiles = a.num_m_tiles * a.num_n_tiles;
+  const int num_units = num_tiles * a.k_splits;
   auto unit_coords = [&](int unit, int& mt, int& nt, int& kb0, int& kb1) {
-    gemm_tile_coords(unit / a.k_splits, a, mt, nt);
-    kb0 = (unit % a.k_splits) * a.kb_per_split;
+    gemm_tile_coords(unit % num_tiles, a, mt, nt);
+    kb0 = (unit / num_tiles) * a.kb_per_split;
     kb1 = min(a.num_k_blocks, kb0 + a.kb_per_split);
   };
 
@@ -220,7 +222,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
     for (int unit = pair; unit < num_units; unit += npairs) {
       int mt, nt, kb0, kb1;
       unit_coords(unit, mt, nt, kb0, kb1);
-      const int split = unit % a.k_splits;
+      const int split = unit / num_tiles;
       const int n0 = nt * kTileN;
       if (!warp_wait_bounded<true, BSK_EPI_SLEEP_NS>(ptx::smem_u32(&tfull[acc]), acc_phase, ctl, 6)) break;
       ptx::tc_fence_after();
