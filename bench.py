@@ -268,6 +268,27 @@ def time_region(ctx: Ctx, fn, steps: int, warmup: int, name: str = ""):
     return ctx.max(s.elapsed_time(e) / steps)
 
 
+# ----------------------------------------------------------------------------------------- output self-checks
+# After each timed region, every rank checks a sample of its own output against an fp64 recompute on the device
+# (rows and columns drawn from a fixed seed; the max error over ranks is reported), so the 2-8 GPU runs carry
+# evidence that the sharded results are right, not only fast.
+def _rel_err(out: torch.Tensor, ref: torch.Tensor) -> float:
+    o, r = out.double(), ref.double()
+    den = torch.linalg.vector_norm(r).item()
+    return torch.linalg.vector_norm(o - r).item() / den if den > 0 else torch.linalg.vector_norm(o).item()
+
+
+def _pick(n: int, k: int, seed: int) -> torch.Tensor:
+    g = torch.Generator().manual_seed(seed)
+    return torch.sort(torch.randperm(n, generator=g)[:min(k, n)]).values
+
+
+def _check_entry(ctx: Ctx, err: float, tol: float, sample: str) -> dict:
+    err = ctx.max(err)
+    return {"err": err, "tol": tol, "ok": bool(err <= tol), "sample": sample, "ranks": ctx.world,
+            "reference": "fp64 recompute on the device"}
+
+
 # ----------------------------------------------------------------------------------------- dense GEMM
 def bench_cublas_dense(ctx: Ctx, args, res: dict):
     """Same-box yardstick, opt-in (`--ops dense,cublas`): the library GEMM (cuBLAS through torch.matmul, fp16 in,
@@ -339,6 +360,19 @@ def bench_dense(ctx: Ctx, args, res: dict):
     res["dense"] = {"ms": ms, "tflops": tflops, "flops": total_flops, "launches_per_step": launches,
                     "mode": args.dense_mode, "comm": comm,
                     "per_rank_flops": total_flops / ctx.world}
+    torch.cuda.synchronize()
+    if args.dense_mode == "nshard":  # this rank's output columns [n0, n1)
+        rows = _pick(cfg.M, 64, 101).to(ctx.dev)
+        cols = _pick(n1 - n0, 64, 102 + ctx.rank).to(ctx.dev)
+        ref = A[rows].double() @ Bt_r[cols].double().t()
+        err = _rel_err(C_r[rows][:, cols], ref)
+    else:  # this rank's reduce-scattered rows
+        mr = cfg.M // ctx.world
+        rows = _pick(mr, 64, 103 + ctx.rank).to(ctx.dev)
+        cols = _pick(cfg.N, 64, 104).to(ctx.dev)
+        ref = A[rows + ctx.rank * mr].double() @ Bt[cols].double().t()
+        err = _rel_err(out[rows][:, cols], ref)
+    res["dense"]["check"] = _check_entry(ctx, err, 1e-3, "64 rows x 64 columns of each rank's output")
     # e2e through the public API: host (pinned) inputs -> device, GEMM, result -> host, every step
     if not args.no_e2e and args.dense_mode == "nshard":
         import periodicdent42_b200 as bsk
@@ -390,7 +424,16 @@ def bench_fp8(ctx: Ctx, args, res: dict):
     # 0.5 GB inputs: flush L2 between steps by rotating through 4 input copies is not needed at
     # 268 MB per operand (> 126 MB L2); each step re-reads both operands from HBM.
     ms = time_region(ctx, step, args.op_steps, args.warmup, "fp8")
+    torch.cuda.synchronize()
+    rows = _pick(cfg.M, 64, 201).to(ctx.dev)
+    cols = _pick(n1 - n0, 64, 202 + ctx.rank).to(ctx.dev)
+    a_s = Aq.view(torch.uint8)[rows].view(Aq.dtype).double()  # row gathers on the byte view
+    b_s = Bq_r.view(torch.uint8)[cols].view(Bq_r.dtype).double()
+    ref = (a_s @ b_s.t()) * (sa.double() * sb.double())
+    fp8_check = _check_entry(ctx, _rel_err(D[rows][:, cols], ref), 3e-2,
+                             "64 rows x 64 columns of each rank's output")
     res["fp8"] = {"ms": ms, "tflops": cfg.flops / (ms * 1e-3) / 1e12, "flops": cfg.flops, "launches_per_step": 1,
+                  "check": fp8_check,
                   # per rank: e4m3 A and this rank's B^T rows once, bf16 D columns once
                   "algorithmic_bytes": (cfg.M + (n1 - n0)) * cfg.K + cfg.M * (n1 - n0) * 2}
     del Aq, Bqt, D
@@ -411,7 +454,21 @@ def bench_bsr(ctx: Ctx, args, res: dict):
         _capi.spmm_bsr_f16f32(rp32, ci32, vals, B, C, cfg.M, r0, r1, stream=ctx.stream)
     ms = time_region(ctx, step, args.op_steps, args.warmup, "bsr")
     blocks_r = int(crow[r1].item() - crow[r0].item())
+    torch.cuda.synchronize()
+    brs = (_pick(r1 - r0, 2, 301 + ctx.rank) + r0).tolist() if r1 > r0 else []
+    cols = _pick(cfg.N, 64, 302).to(ctx.dev)
+    crow_h, col_h = crow.cpu().tolist(), col.cpu().tolist()
+    errs = []
+    for br in brs:
+        ref = torch.zeros(cfg.block, cols.numel(), dtype=torch.float64, device=ctx.dev)
+        for j in range(crow_h[br], crow_h[br + 1]):
+            kb = col_h[j]
+            ref += vals[j].double() @ B[kb * cfg.block:(kb + 1) * cfg.block][:, cols].double()
+        errs.append(_rel_err(C[br * cfg.block:(br + 1) * cfg.block][:, cols], ref))
+    bsr_check = _check_entry(ctx, max(errs) if errs else 0.0, 1e-3,
+                             "2 block-rows x 64 columns of each rank's block-row range")
     res["bsr"] = {"ms": ms, "tflops": cfg.flops / (ms * 1e-3) / 1e12, "flops": cfg.flops, "launches_per_step": 1,
+                  "check": bsr_check,
                   # per rank: its stored blocks, the dense B, its C rows
                   "algorithmic_bytes": blocks_r * cfg.block * cfg.block * 2 + cfg.K * cfg.N * 2
                   + (r1 - r0) * cfg.block * cfg.N * 4,
@@ -421,6 +478,24 @@ def bench_bsr(ctx: Ctx, args, res: dict):
 
 
 # ----------------------------------------------------------------------------------------- attention backward
+def _attn_bwd_fp64(q, k, v, dO, rp, ci, bh: int, qb: int, kb: int, scale: float, cfg):
+    """fp64 autograd gradients of pair bh: dQ of query block-row qb, dK and dV of key block-row kb. Query rows are
+    independent, so the loss sum(O_i * dO_i) over qb and every query block-row whose mask holds kb gives those
+    blocks exactly."""
+    nqb, blk = cfg.S // cfg.block, cfg.block
+    rpl, cil = rp.tolist(), ci.tolist()
+    rows = sorted({qb} | {i for i in range(nqb) if kb in cil[rpl[bh * nqb + i]:rpl[bh * nqb + i + 1]]})
+    qd, kd, vd = (t.view(-1, cfg.S, cfg.D)[bh].double().requires_grad_() for t in (q, k, v))
+    dOd = dO.view(-1, cfg.S, cfg.D)[bh].double()
+    loss = 0.0
+    for i in rows:
+        o = _attn_block_fp64(qd.unsqueeze(0), kd.unsqueeze(0), vd.unsqueeze(0), rp[bh * nqb:], ci, 0, i, scale,
+                             cfg, row_base=0)
+        loss = loss + (o * dOd[i * blk:(i + 1) * blk]).sum()
+    gq, gk, gv = torch.autograd.grad(loss, (qd, kd, vd))
+    return gq[qb * blk:(qb + 1) * blk], gk[kb * blk:(kb + 1) * blk], gv[kb * blk:(kb + 1) * blk]
+
+
 def bench_attn_bwd(ctx: Ctx, args, res: dict):
     """Backward of the attention workload (the forward's shapes and mask): delta + dK/dV pass + dQ pass, through
     the C ABI, LSE and column lists prepared outside the timed region. Useful FLOPs: the standard count of 5
@@ -455,12 +530,21 @@ def bench_attn_bwd(ctx: Ctx, args, res: dict):
         _capi.bsattn_bwd(Bv(dO), Bv(q), Bv(k), Bv(v), Bv(O), lse_r, Bv(dQ), Bv(dK), Bv(dV), rp_r, ci_r, cp_r, ri_r,
                          scale, True, delta=dl_r, stream=ctx.stream)
     ms = time_region(ctx, step, args.op_steps, args.warmup, "attn_bwd")
+    torch.cuda.synchronize()
+    errs = []
+    for bh in (_pick(b1 - b0, 2, 501 + ctx.rank) + b0).tolist():
+        qb, kb = _pick(nqb, 2, 502 + bh).tolist()
+        gq, gk, gv = _attn_bwd_fp64(q, k, v, dO, rp, ci, bh, qb, kb, scale, cfg)
+        blk = lambda t, b: t.view(-1, cfg.S, cfg.D)[bh, b * 128:(b + 1) * 128]  # noqa: E731
+        errs += [_rel_err(blk(dQ, qb), gq), _rel_err(blk(dK, kb), gk), _rel_err(blk(dV, kb), gv)]
+    bwd_check = _check_entry(ctx, max(errs), 2e-2, "dQ of 1 query block-row, dK and dV of 1 key block-row, "
+                                                  "of 2 (b,h) pairs per rank")
     nnz = int(rp[-1])
     flops = 2.5 * 4 * 128 ** 2 * cfg.D * nnz
     res["attn_bwd"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "flops": flops, "launches_per_step": 3,
                        # per rank: read Q, K, V, O, dO and the LSE, write dQ, dK, dV (its pairs)
                        "algorithmic_bytes": (b1 - b0) * cfg.S * (8 * cfg.D * 2 + 4),
-                       "nnz_blocks": nnz, "executed_gemm_ratio": 7 / 5}
+                       "nnz_blocks": nnz, "executed_gemm_ratio": 7 / 5, "check": bwd_check}
     del q, k, v, O, dO, dQ, dK, dV
     torch.cuda.empty_cache()
 
@@ -513,7 +597,20 @@ def bench_bsr_bsr(ctx: Ctx, args, res: dict):
     def step():
         _capi.spmm_bsr_bsr_f16f32(rp, ci, vals, brp, bci, bvals, C, cfg.M, cfg.N, cfg.K, r0, r1, stream=ctx.stream)
     ms = time_region(ctx, step, args.op_steps, args.warmup, "bsr_bsr")
+    torch.cuda.synchronize()
+    crow_h, col_h, bcrow_h, bcol_h = crow.cpu().tolist(), col.cpu().tolist(), bcrow.tolist(), bcol.tolist()
+    errs = []
+    for br in ((_pick(r1 - r0, 2, 601 + ctx.rank) + r0).tolist() if r1 > r0 else []):
+        ref = torch.zeros(128, cfg.N, dtype=torch.float64, device=ctx.dev)
+        for j in range(crow_h[br], crow_h[br + 1]):
+            kb = col_h[j]
+            for t in range(bcrow_h[kb], bcrow_h[kb + 1]):
+                nb = bcol_h[t]
+                ref[:, nb * 128:(nb + 1) * 128] += vals[j].double() @ bvals[t].double()
+        errs.append(_rel_err(C[br * 128:(br + 1) * 128], ref))
+    bb_check = _check_entry(ctx, max(errs) if errs else 0.0, 1e-3, "2 whole block-rows of each rank's range")
     res["bsr_bsr"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "flops": flops, "launches_per_step": 1,
+                      "check": bb_check,
                       "algorithmic_bytes": int(crow[r1] - crow[r0]) * 128 * 128 * 2 + int(bcrow[-1]) * 128 * 128 * 2
                       + (r1 - r0) * 128 * cfg.N * 4,
                       "block_pairs": pairs, "nnzb": int(crow[-1].item()), "b_nnzb": int(bcrow[-1])}
@@ -592,6 +689,27 @@ def bench_convert(ctx: Ctx, args, res: dict):
 
 
 # ----------------------------------------------------------------------------------------- attention
+def _attn_block_fp64(q, k, v, rp, ci, bh: int, qb: int, scale: float, cfg, row_base: int | None = None
+                     ) -> torch.Tensor:
+    """fp64 block-sparse attention of query block-row qb of pair bh (the key blocks of its mask row, the diagonal
+    block causal), on the device. The row's entry in rp is row_base + qb (default bh * S/block + qb)."""
+    nqb, blk = cfg.S // cfg.block, cfg.block
+    p = (bh * nqb if row_base is None else row_base) + qb
+    cols = ci[int(rp[p]):int(rp[p + 1])].tolist()
+    if not cols:
+        return torch.zeros(blk, cfg.D, dtype=torch.float64, device=q.device)
+    qv, kv, vv = (t.view(-1, cfg.S, cfg.D)[bh] for t in (q, k, v))
+    Qb = qv[qb * blk:(qb + 1) * blk].double()
+    Kc = torch.cat([kv[c * blk:(c + 1) * blk] for c in cols]).double()
+    Vc = torch.cat([vv[c * blk:(c + 1) * blk] for c in cols]).double()
+    s = (Qb @ Kc.t()) * scale
+    kpos = torch.cat([torch.arange(c * blk, (c + 1) * blk, device=q.device) for c in cols])
+    diag = torch.cat([torch.full((blk,), c == qb, device=q.device) for c in cols])
+    qpos = torch.arange(qb * blk, (qb + 1) * blk, device=q.device)
+    s = s.masked_fill(diag[None, :] & (kpos[None, :] > qpos[:, None]), float("-inf"))
+    return torch.softmax(s, dim=1) @ Vc
+
+
 def bench_attn(ctx: Ctx, args, res: dict):
     cfg = wl.ATTN
     q, k, v = wl.attn_inputs(cfg, ctx.dev)
@@ -608,7 +726,19 @@ def bench_attn(ctx: Ctx, args, res: dict):
         _capi.bsattn_fwd_bf16(q, k, v, O, rp32, ci32, scale, True, b0, b1, stream=ctx.stream)
     ms = time_region(ctx, step, args.op_steps, args.warmup, "attn")
     flops = wl.attn_flops(rp, cfg.block, cfg.D)
+    torch.cuda.synchronize()
+    attn_errs, attn_tols = [], []
+    for bh in (_pick(b1 - b0, 2, 401 + ctx.rank) + b0).tolist():
+        for qb in _pick(nqb, 2, 402 + bh).tolist():
+            ref = _attn_block_fp64(q, k, v, rp, ci, bh, qb, scale, cfg)
+            got = O.view(-1, cfg.S, cfg.D)[bh, qb * cfg.block:(qb + 1) * cfg.block]
+            attn_errs.append(_rel_err(got, ref))
+            attn_tols.append(_rel_err(ref.to(O.dtype), ref) + 1e-3)  # bf16 storage floor + 1e-3
+    worst = max((e - t for e, t in zip(attn_errs, attn_tols)), default=-1.0)
+    attn_check = _check_entry(ctx, worst, 0.0, "2 query block-rows of 2 (b,h) pairs per rank; err = error - "
+                                              "(bf16 storage floor + 1e-3), ok when <= 0")
     res["attn"] = {"ms": ms, "tflops": flops / (ms * 1e-3) / 1e12, "flops": flops, "launches_per_step": 1,
+                   "check": attn_check,
                    # per rank: read Q, K, V and write O of its (b,h) pairs
                    "algorithmic_bytes": (b1 - b0) * cfg.S * cfg.D * 2 * 4,
                    "nnz_blocks": int(rp[-1].item()), "pairs": [b0, b1]}
@@ -831,6 +961,7 @@ def main():
                                 "algorithmic_bytes": (dense_cfg(args).M + dense_cfg(args).N // ctx.world)
                                 * dense_cfg(args).K * 2 + dense_cfg(args).M * dense_cfg(args).N // ctx.world * 4}
             line["e2e"] = d.get("e2e")
+            line["check"] = d.get("check")
             line["gpu_launches"] = args.steps * d["launches_per_step"]
         line["cpu_baseline"] = cpu
         line["clocks"] = clk
@@ -846,7 +977,7 @@ def main():
                                "roofline": op_roofline(name, r, regions.get(name), peaks, peak_src, ctx.world,
                                                        sm_count, traffic.get(name)),
                                "cpu_baseline": cpu_ops.get(name)}
-                for kk in ("nnzb", "nnz_blocks", "block_pairs", "b_nnzb", "algorithmic_bytes"):
+                for kk in ("nnzb", "nnz_blocks", "block_pairs", "b_nnzb", "algorithmic_bytes", "check"):
                     if kk in r:
                         opsum[name][kk] = r[kk]
         if "convert" in res:
@@ -873,6 +1004,9 @@ def main():
                     r[f"{name}_flop_per_clk_per_sm"] = tf / ctx.world * 1e12 / (reg["sm_mhz"] * 1e6 * sm_count)
             opsum["cublas_dense"] = r
         line["ops"] = opsum
+        checks = {name: {kk: r["check"][kk] for kk in ("err", "tol", "ok")}
+                  for name, r in res.items() if isinstance(r, dict) and "check" in r}
+        line["checks"] = {"all_ok": all(c["ok"] for c in checks.values()), "ranks": ctx.world, **checks}
         line["device_error_word"] = err_word
         print(json.dumps(line), flush=True)
     ctx.close()
