@@ -18,8 +18,11 @@
 // at ~2000-2250 SM cycles, set by the softmax (TMEM load ~250, max ~200, exchange ~300-550, exponentials ~950 --
 // the MUFU of a sub-partition shared by the two halves -- and ~200 per barrier wait), against 1024 cycles of tensor
 // work. Variants measured slower on B200: speculative exponentials before the exchange (735 vs 890 TFLOPS), P in
-// its own TMEM buffers with the exchange in shared memory and one Q buffer (832 vs 887), and independent halves
-// with one O accumulator each (no exchange; P aliased onto S, so S_{j+2} waits for PV_j: 850 vs 876).
+// its own TMEM buffers with the exchange in shared memory and one Q buffer (832 vs 887), independent halves
+// with one O accumulator each (no exchange; P aliased onto S, so S_{j+2} waits for PV_j: 850 vs 876), and both
+// halves loading the whole S row to take the max without an exchange, P in its own TMEM buffers so S_{j+2} only
+// waits for S_j to be loaded (790 vs 917: the S row is read from TMEM twice, and the longer load costs more than
+// the exchange it removes).
 //
 // Roles (16 warps): warp 0 TMA producer, warp 1 TMEM owner + S issuer, warp 2 PV issuer, warp 3 idle, warps 4-11
 // softmax, warps 12-15 output (O / l from TMEM to global once a row's last PV completed, so the softmax warps go
