@@ -22,7 +22,8 @@
 // with one O accumulator each (no exchange; P aliased onto S, so S_{j+2} waits for PV_j: 850 vs 876), and both
 // halves loading the whole S row to take the max without an exchange, P in its own TMEM buffers so S_{j+2} only
 // waits for S_j to be loaded (790 vs 917: the S row is read from TMEM twice, and the longer load costs more than
-// the exchange it removes).
+// the exchange it removes), and suspend-hint waits (try_wait with a time hint) for the MMA issuers (872 vs 884) or
+// for the issuers and the softmax warps (867 vs 884): the re-polling waits stay.
 //
 // Roles (16 warps): warp 0 TMA producer, warp 1 TMEM owner + S issuer, warp 2 PV issuer, warp 3 idle, warps 4-11
 // softmax, warps 12-15 output (O / l from TMEM to global once a row's last PV completed, so the softmax warps go
