@@ -84,7 +84,9 @@ int bsk_gemm_f16f32_acc(const void* A, int64_t lda, const void* B, int64_t ldb, 
 /*
  * Dense GEMM from HOST memory: C_host[M,N] = A_host[M,K] * B_host[K,N] (same layouts as bsk_gemm_f16f32), streamed
  * through the GPU in K chunks: the host-to-device copies of chunk i+1 (on a stream of this call's own) overlap
- * the tensor-core work on chunk i, C accumulates in device memory and is copied back once at the end.
+ * the tensor-core work on chunk i and C accumulates in device memory. The last chunk goes by row panels (about
+ * M/8 rows, whole 256-row tiles): each panel's C rows are final after its GEMM and are copied back while the
+ * next panel's rows are still being uploaded.
  *   A_host, B_host, C_host : host memory; page-locked (cudaHostAlloc / cudaHostRegister) for the copies to be
  *                            asynchronous and overlap; pageable memory works but serialises.
  *   k_chunk   : K elements per chunk, a multiple of 64; <= 0 chooses (about 16 chunks of at least 4096).

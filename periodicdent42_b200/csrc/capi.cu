@@ -429,6 +429,13 @@ struct HostPlan {
 
 int64_t round256(int64_t x) { return (x + 255) / 256 * 256; }
 
+// Row panel of the host-streaming GEMM's last chunk: about 8 panels, whole 256-row tiles, at least one tile.
+int host_panel_rows(int M) {
+  int r = (M + 7) / 8;
+  r = (r + 255) / 256 * 256;
+  return r > 0 ? r : 256;
+}
+
 HostPlan plan_host(int M, int N, int K, int k_chunk) {
   HostPlan p;
   int kc = k_chunk;
@@ -499,59 +506,96 @@ int bsk_gemm_f16f32_host(const void* A_host, int64_t lda, const void* B_host, in
 
   // Copies run on their own stream so chunk i+1 crosses PCIe while chunk i is on the tensor cores; events order
   // them: ready[b] (chunk in buffer b has landed) before its GEMM, freed[b] (that GEMM has finished reading
-  // buffer b) before the copy two chunks later overwrites it. Stream and events are released at the end of
-  // this call; CUDA keeps them alive until the enqueued work that uses them has completed.
-  cudaStream_t cs = nullptr;
-  cudaEvent_t start = nullptr, ready[2] = {nullptr, nullptr}, freed[2] = {nullptr, nullptr};
+  // buffer b) before the copy two chunks later overwrites it. The LAST chunk goes by row panels: its B part
+  // first, then A's rows panel by panel, each panel's GEMM as soon as it lands, and that panel's C rows (now
+  // final) back to the host on a third stream while the next panel's rows still cross the link (the two copy
+  // directions run concurrently), so only one panel's GEMM and copy back remain after the last upload. Streams
+  // and events are released at the end of this call; CUDA keeps them alive until the enqueued work that uses
+  // them has completed (a wait captures the event's most recent record, so one event serves every panel).
+  cudaStream_t cs = nullptr, ds = nullptr;
+  cudaEvent_t start = nullptr, ready[2] = {nullptr, nullptr}, freed[2] = {nullptr, nullptr}, panel = nullptr;
   int rc = BSK_OK;
   cudaError_t e = cudaStreamCreateWithFlags(&cs, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ds, cudaStreamNonBlocking);
   if (e == cudaSuccess) e = cudaEventCreateWithFlags(&start, cudaEventDisableTiming);
+  if (e == cudaSuccess) e = cudaEventCreateWithFlags(&panel, cudaEventDisableTiming);
   for (int b = 0; b < 2 && e == cudaSuccess; ++b) {
     e = cudaEventCreateWithFlags(&ready[b], cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&freed[b], cudaEventDisableTiming);
   }
   if (e == cudaSuccess) e = cudaEventRecord(start, s);  // earlier work on `stream` (e.g. a previous user of the
-  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, start, 0);  // workspace) comes before the first copy
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(cs, start, 0);  // workspace or of C_host) comes first
+  if (e == cudaSuccess) e = cudaStreamWaitEvent(ds, start, 0);
   if (e != cudaSuccess) rc = cuda_fail(e, "gemm_host: stream/event setup");
+  const int rows_per_panel = host_panel_rows(M);
   for (int i = 0; i < nchunks && rc == BSK_OK; ++i) {
     const int b = i & 1;
     const int k0 = i * p.kc;
     const int kw = K - k0 < p.kc ? K - k0 : p.kc;
+    const bool last = i == nchunks - 1;
     if (i >= 2) e = cudaStreamWaitEvent(cs, freed[b], 0);
-    if (e == cudaSuccess)
-      e = cudaMemcpy2DAsync(abuf[b], (size_t)p.kc * 2, static_cast<const __half*>(A_host) + k0, (size_t)lda * 2,
-                            (size_t)kw * 2, M, cudaMemcpyHostToDevice, cs);
     if (e == cudaSuccess)
       e = cudaMemcpy2DAsync(bbuf[b], (size_t)p.kc * 2, static_cast<const __half*>(B_host) + k0, (size_t)ldb * 2,
                             (size_t)kw * 2, N, cudaMemcpyHostToDevice, cs);
-    if (e == cudaSuccess) e = cudaEventRecord(ready[b], cs);
-    if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ready[b], 0);
-    if (e != cudaSuccess) {
-      rc = cuda_fail(e, "gemm_host: chunk copy");
-      break;
+    if (!last) {
+      if (e == cudaSuccess)
+        e = cudaMemcpy2DAsync(abuf[b], (size_t)p.kc * 2, static_cast<const __half*>(A_host) + k0, (size_t)lda * 2,
+                              (size_t)kw * 2, M, cudaMemcpyHostToDevice, cs);
+      if (e == cudaSuccess) e = cudaEventRecord(ready[b], cs);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ready[b], 0);
+      if (e != cudaSuccess) {
+        rc = cuda_fail(e, "gemm_host: chunk copy");
+        break;
+      }
+      rc = gemm_f16_launch(abuf[b], p.kc, bbuf[b], p.kc, Cd, p.ldc_dev, M, N, kw, 0, kw, i > 0 ? 1 : 0, stream);
+      if (rc == BSK_OK && (e = cudaEventRecord(freed[b], s)) != cudaSuccess) rc = cuda_fail(e, "gemm_host: event");
+      continue;
     }
-    rc = gemm_f16_launch(abuf[b], p.kc, bbuf[b], p.kc, Cd, p.ldc_dev, M, N, kw, 0, kw, i > 0 ? 1 : 0, stream);
-    if (rc == BSK_OK && (e = cudaEventRecord(freed[b], s)) != cudaSuccess) rc = cuda_fail(e, "gemm_host: event");
+    for (int m0 = 0; m0 < M && rc == BSK_OK; m0 += rows_per_panel) {
+      const int mr = M - m0 < rows_per_panel ? M - m0 : rows_per_panel;
+      __half* ap = abuf[b] + (int64_t)m0 * p.kc;
+      float* cp = Cd + (int64_t)m0 * p.ldc_dev;
+      if (e == cudaSuccess)
+        e = cudaMemcpy2DAsync(ap, (size_t)p.kc * 2, static_cast<const __half*>(A_host) + (int64_t)m0 * lda + k0,
+                              (size_t)lda * 2, (size_t)kw * 2, mr, cudaMemcpyHostToDevice, cs);
+      if (e == cudaSuccess) e = cudaEventRecord(ready[b], cs);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(s, ready[b], 0);
+      if (e != cudaSuccess) {
+        rc = cuda_fail(e, "gemm_host: panel copy");
+        break;
+      }
+      rc = gemm_f16_launch(ap, p.kc, bbuf[b], p.kc, cp, p.ldc_dev, mr, N, kw, 0, kw, i > 0 ? 1 : 0, stream);
+      if (rc != BSK_OK) break;
+      e = cudaEventRecord(panel, s);
+      if (e == cudaSuccess) e = cudaStreamWaitEvent(ds, panel, 0);
+      if (e == cudaSuccess)
+        e = cudaMemcpy2DAsync(C_host + (int64_t)m0 * ldc, (size_t)ldc * 4, cp, (size_t)p.ldc_dev * 4,
+                              (size_t)N * 4, mr, cudaMemcpyDeviceToHost, ds);
+      if (e != cudaSuccess) rc = cuda_fail(e, "gemm_host: result copy");
+    }
   }
   if (rc == BSK_OK && nchunks == 0) {
     e = cudaMemset2DAsync(Cd, p.ldc_dev * 4, 0, (size_t)N * 4, M, s);
+    if (e == cudaSuccess)
+      e = cudaMemcpy2DAsync(C_host, (size_t)ldc * 4, Cd, (size_t)p.ldc_dev * 4, (size_t)N * 4, M,
+                            cudaMemcpyDeviceToHost, s);
     if (e != cudaSuccess) rc = cuda_fail(e, "gemm_host: zero fill");
   }
-  if (rc == BSK_OK) {
-    e = cudaMemcpy2DAsync(C_host, (size_t)ldc * 4, Cd, (size_t)p.ldc_dev * 4, (size_t)N * 4, M,
-                          cudaMemcpyDeviceToHost, s);
-    if (e != cudaSuccess) rc = cuda_fail(e, "gemm_host: result copy");
-  }
-  // If a step failed part-way, `stream` must still not run ahead of copies already queued on cs.
+  // `stream` must not run ahead of copies already queued on cs and ds (also when a step failed part-way).
   if (cs && start) {
     if (cudaEventRecord(start, cs) == cudaSuccess) cudaStreamWaitEvent(s, start, 0);
+  }
+  if (ds && panel) {
+    if (cudaEventRecord(panel, ds) == cudaSuccess) cudaStreamWaitEvent(s, panel, 0);
   }
   for (int b = 0; b < 2; ++b) {
     if (ready[b]) cudaEventDestroy(ready[b]);
     if (freed[b]) cudaEventDestroy(freed[b]);
   }
   if (start) cudaEventDestroy(start);
+  if (panel) cudaEventDestroy(panel);
   if (cs) cudaStreamDestroy(cs);
+  if (ds) cudaStreamDestroy(ds);
   return rc;
 }
 

@@ -228,7 +228,8 @@ def gemm_from_host(A: torch.Tensor, B: torch.Tensor, out: Optional[torch.Tensor]
                    device=None, sync: bool = True) -> torch.Tensor:
     """C = A @ B for fp16 operands in HOST memory, fp32 result in host memory, computed on the GPU with the
     K dimension streamed in chunks: the PCIe copy of chunk i+1 overlaps the tensor-core work on chunk i and C
-    accumulates on the device (one copy back at the end). A [M, K] row-major; B [K, N], column-major preferred
+    accumulates on the device (the last chunk by row panels, each panel's C rows copied back while the next
+    panel uploads). A [M, K] row-major; B [K, N], column-major preferred
     (``B = Bt.t()``). Use page-locked tensors (``pin_memory=True``) for A, B and ``out``: pageable memory works
     but its copies do not overlap. ``k_chunk``: K per chunk (multiple of 64), 0 = automatic. ``sync``: wait for
     the result (False leaves it pending on the current stream of ``device``)."""

@@ -62,7 +62,10 @@ def test_gemm_acc_empty_range_leaves_c(no_device_error):
 
 
 @pytest.mark.parametrize("M,N,K,k_chunk", [(512, 1024, 4096, 1024), (300, 520, 1000, 256), (256, 256, 64, 0),
-                                           (1024, 1024, 20000, 0), (130, 136, 72, 64)])
+                                           (1024, 1024, 20000, 0), (130, 136, 72, 64),
+                                           # the last chunk goes by row panels (~M/8 rounded up to 256 rows):
+                                           # several panels with a ragged last one, and a single-chunk call
+                                           (2600, 520, 3000, 1024), (2048, 264, 64, 0), (3000, 384, 9000, 0)])
 def test_gemm_from_host(no_device_error, M, N, K, k_chunk):
     A, Bt, _ = _operands(M, N, K, 11 + M)
     A_h, Bt_h = A.pin_memory(), Bt.pin_memory()
