@@ -23,7 +23,12 @@
 // halves loading the whole S row to take the max without an exchange, P in its own TMEM buffers so S_{j+2} only
 // waits for S_j to be loaded (790 vs 917: the S row is read from TMEM twice, and the longer load costs more than
 // the exchange it removes), and suspend-hint waits (try_wait with a time hint) for the MMA issuers (872 vs 884) or
-// for the issuers and the softmax warps (867 vs 884): the re-polling waits stay.
+// for the issuers and the softmax warps (867 vs 884): the re-polling waits stay. Two blocks per softmax step
+// (warps 4-7 take block 2t, warps 8-11 block 2t+1, each thread a whole 128-column row, the two blocks' maxima
+// exchanged once per pair, P in its own TMEM columns) ran at 744 vs 888: 128 live scores per thread spill under
+// the 176-register cap and the two warps of a sub-partition still run their exponentials in lockstep. The MUFU
+// computes 16 exp2 per clock per SM in the f32, f16x2 and bf16x2 forms alike (measured), so packed exponentials
+// do not raise that ceiling.
 //
 // Roles (16 warps): warp 0 TMA producer, warp 1 TMEM owner + S issuer, warp 2 PV issuer, warp 3 idle, warps 4-11
 // softmax, warps 12-15 output (O / l from TMEM to global once a row's last PV completed, so the softmax warps go
