@@ -5,35 +5,43 @@
 // every nonzero key block j of the row's mask the CTA computes
 //     S_j = Q K_j^T                 tcgen05.mma 128x128x16 x (D/16) into TMEM S buffer j % 2
 //     P_j = exp2(S_j * c - m)       online softmax, one query row per thread pair; P (16-bit) is written back into
-//                                   the first 64 columns of the same S buffer (tcgen05.st)
+//                                   the S buffer (tcgen05.st): keys 0-63 in columns [0, 32), 64-127 in [64, 96)
 //     O  += P_j V_j                 tcgen05.mma with A = P from TMEM, V an MN-major shared-memory operand
 // and writes O / l. Only nonzero blocks are loaded (TMA through a 5-slot K/V ring).
 //
 // Why this shape: one thread issues a 128x128x16 tcgen05.mma only every ~115-160 SM cycles while the tensor pipe
 // finishes it in 64, and two to four issuing warps bring the aggregate back to 68-84 cycles (measured on B200). So
 // the S MMAs and the PV MMAs have an issuing thread each (warps 1 and 2), and S is double-buffered in TMEM, so
-// S_{j+1} is computed while the softmax of block j runs. The softmax itself is split across two warps per row:
-// warps 4-7 take keys 0-63, warps 8-11 keys 64-127 of the rows of their TMEM lane quarter, and exchange each row's
-// partial max through two spare TMEM columns. A cycle trace of this kernel on the attention workload puts a block
-// at ~2000-2250 SM cycles, set by the softmax (TMEM load ~250, max ~200, exchange ~300-550, exponentials ~950 --
-// the MUFU of a sub-partition shared by the two halves -- and ~200 per barrier wait), against 1024 cycles of tensor
-// work. Variants measured slower on B200: speculative exponentials before the exchange (735 vs 890 TFLOPS), P in
-// its own TMEM buffers with the exchange in shared memory and one Q buffer (832 vs 887), independent halves
-// with one O accumulator each (no exchange; P aliased onto S, so S_{j+2} waits for PV_j: 850 vs 876), and both
-// halves loading the whole S row to take the max without an exchange, P in its own TMEM buffers so S_{j+2} only
-// waits for S_j to be loaded (790 vs 917: the S row is read from TMEM twice, and the longer load costs more than
-// the exchange it removes), and suspend-hint waits (try_wait with a time hint) for the MMA issuers (872 vs 884) or
-// for the issuers and the softmax warps (867 vs 884): the re-polling waits stay. Two blocks per softmax step
-// (warps 4-7 take block 2t, warps 8-11 block 2t+1, each thread a whole 128-column row, the two blocks' maxima
-// exchanged once per pair, P in its own TMEM columns) ran at 744 vs 888: 128 live scores per thread spill under
-// the 176-register cap and the two warps of a sub-partition still run their exponentials in lockstep. The MUFU
-// computes 16 exp2 per clock per SM in the f32, f16x2 and bf16x2 forms alike (measured), so packed exponentials
-// do not raise that ceiling.
+// S_{j+1} is computed while the softmax of block j runs. The softmax itself is split across two warps per row: warps
+// 4-7 take keys 0-63, warps 8-11 keys 64-127 of the rows of their TMEM lane quarter, and exchange each row's partial
+// max through the last S column of their key range (63, 127: already loaded, not overwritten by P). A cycle trace of
+// this kernel on the attention workload puts a block at ~2000-2250 SM cycles, set by the softmax (TMEM load ~250, max
+// ~200, exchange ~300-550, exponentials ~950 -- the MUFU of a sub-partition shared by the two halves -- and ~200 per
+// barrier wait), against 1024 cycles of tensor work; the first two blocks of a row take ~2500 cycles more (a per-row
+// cost of ~4000 cycles in total, from a sweep of blocks per row). Variants measured slower on B200: speculative
+// exponentials before the exchange (735 vs 890 TFLOPS), P in its own TMEM buffers with the exchange in shared memory
+// and one Q buffer (832 vs 887), independent halves with one O accumulator each (no exchange; P aliased onto S, so
+// S_{j+2} waits for PV_j: 850 vs 876), and both halves loading the whole S row to take the max without an exchange, P
+// in its own TMEM buffers so S_{j+2} only waits for S_j to be loaded (790 vs 917: the S row is read from TMEM twice,
+// and the longer load costs more than the exchange it removes), and suspend-hint waits (try_wait with a time hint)
+// for the MMA issuers (872 vs 884) or for the issuers and the softmax warps (867 vs 884): the re-polling waits stay.
+// Two blocks per softmax step (warps 4-7 take block 2t, warps 8-11 block 2t+1, each thread a whole 128-column row,
+// the two blocks' maxima exchanged once per pair, P in its own TMEM columns) ran at 744 vs 888: 128 live scores per
+// thread spill under the 176-register cap and the two warps of a sub-partition still run their exponentials in
+// lockstep. The MUFU computes 16 exp2 per clock per SM in the f32, f16x2 and bf16x2 forms alike (measured), so packed
+// exponentials do not raise that ceiling. Output warps reading O 64 columns per TMEM round trip (903 vs 920), a
+// non-blocking test of the next block's S before the P store (914 vs 920), pacing the output warps' stores (within
+// 0.5 %) and loading the next row's column indices during a row's first block (901 vs 923) were no better.
 //
 // Roles (16 warps): warp 0 TMA producer, warp 1 TMEM owner + S issuer, warp 2 PV issuer, warp 3 idle, warps 4-11
 // softmax, warps 12-15 output (O / l from TMEM to global once a row's last PV completed, so the softmax warps go
-// straight on to the next row). TMEM: S buffers [0,128) and [128,256), O [256, 256 + D), exchange columns
-// [384, 392). Shared memory: Q x 2, the K/V ring, barriers, and the row sums / maxima handed to the output warps.
+// straight on to the next row). TMEM: S buffers [0,128) and [128,256), O of alternate rows [256, 256 + D) and
+// [384, 384 + D), so the first PV of a row never waits for the output warps to read the previous row's O (+1.3 %
+// on the attention workload). Each output thread writes its row of O with 32-byte stores (one sector each): its
+// stores run beside the softmax warps' shared-memory barrier traffic, and with 16-byte stores the output of a row
+// cost ~5 % of the kernel time (measured by leaving the stores out), with 32-byte stores ~2.5 % (staging the tile
+// in the row's freed Q buffer for a TMA store measured the same). Shared memory: Q x 2, the K/V ring, barriers,
+// and the row sums / maxima handed to the output warps.
 //
 // Softmax: the reference max moves only when a block raises it by more than 8 (log2 units), so P <= 2^8 and O is
 // rescaled in TMEM only on those moves. Scale, sums and the polynomial use packed fp32x2 FMA/ADD; row max uses
@@ -69,8 +77,7 @@ struct AttnShape {
 };
 constexpr int kAttnSmemBytes = AttnShape<false, 128>::kSmemBytes;  // largest instantiation
 constexpr int kAttnTmemCols = 512;
-constexpr uint32_t kAttnTmemO = 256;  // O accumulator columns [256, 256 + D)
-constexpr uint32_t kAttnTmemX = 384;  // exchange columns: 2 slots x 2 halves
+constexpr uint32_t kAttnTmemO = 256;  // O accumulators of alternate rows: columns [256 + 128 o, +D), o = 0, 1
 constexpr uint32_t kAttnRegsLaunch = 128;  // 65536 / 512
 constexpr uint32_t kAttnRegsLow = 80;      // producer and MMA issuers
 constexpr uint32_t kAttnRegsHigh = 168;    // softmax warpgroups
@@ -174,6 +181,13 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return kF16 ? pack_f16(lo, hi) : pack_bf16(lo, hi);
 }
 
+// 32-byte global store (sm_100 256-bit vector store); p 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t* v) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
   asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
 }
@@ -200,14 +214,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
   uint64_t* s_full = kv_empty + kAttnKVSlots;        // [2] S_j in TMEM buffer j % 2
   uint64_t* s_free = s_full + 2;                     // [2] PV_j completed: buffer j % 2 free, O holds block j
   uint64_t* p_full = s_free + 2;                     // [2] P_j written (8 softmax warps)
-  uint64_t* o_done = p_full + 2;                     // last PV of a row completed
-  uint64_t* xbar = o_done + 1;                       // [4 quarters][2 slots]: both halves stored their value
+  uint64_t* o_done = p_full + 2;                     // [2] last PV of a row into O buffer o completed
+  uint64_t* xbar = o_done + 2;                       // [4 quarters][2 slots]: both halves stored their value
   uint64_t* drain = xbar + 8;                        // [2] issuers' final commits
   uint64_t* l_ready = drain + 2;                     // a row's sums and max are in shared memory (8 warps)
-  uint64_t* o_free = l_ready + 1;                    // the output warps read a row's O (4 warps)
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(o_free + 1);
+  uint64_t* o_free = l_ready + 1;                    // [2] the output warps read O buffer o (4 warps)
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(o_free + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_holder + 1);
-  static_assert(4 + 2 * kAttnKVSlots + 2 + 2 + 2 + 1 + 8 + 2 + 2 <= 63, "barrier area exceeds its 512 bytes");
+  static_assert(4 + 2 * kAttnKVSlots + 2 + 2 + 2 + 2 + 8 + 2 + 1 + 2 <= 63, "barrier area exceeds its 512 bytes");
   float* l_part = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 512);  // [2 halves][128 rows]
   float* m_row = l_part + 256;                                                         // [128 rows]
 
@@ -227,9 +241,11 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       ptx::mbar_init(ptx::smem_u32(&kv_full[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&kv_empty[s]), 1);
     }
-    ptx::mbar_init(ptx::smem_u32(o_done), 1);
+    for (int s = 0; s < 2; ++s) {
+      ptx::mbar_init(ptx::smem_u32(&o_done[s]), 1);
+      ptx::mbar_init(ptx::smem_u32(&o_free[s]), 4);
+    }
     ptx::mbar_init(ptx::smem_u32(l_ready), 8);
-    ptx::mbar_init(ptx::smem_u32(o_free), 4);
     for (int s = 0; s < 8; ++s) ptx::mbar_init(ptx::smem_u32(&xbar[s]), 2);
     *abort_flag = 0;
     ptx::fence_mbar_init();
@@ -358,8 +374,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             ptx::mma_commit(ptx::smem_u32(&s_full[b]));
             if (j == n - 1) ptx::mma_commit(ptx::smem_u32(&q_empty[qbuf]));
           } else {
-            if (j == 0 && rows > 0) {  // the first PV of a row overwrites O: the previous row's O must be read
-              ok = wait_bounded(ptx::smem_u32(o_free), (rows - 1) & 1, ctl, 17);
+            if (j == 0 && rows > 1) {  // the first PV of a row overwrites O buffer rows % 2: row rows-2's O is read
+              ok = wait_bounded(ptx::smem_u32(&o_free[rows & 1]), ((rows >> 1) - 1) & 1, ctl, 17);
               if (!ok) break;
             }
             ok = wait_bounded(ptx::smem_u32(&p_full[b]), (g >> 1) & 1, ctl, 13);
@@ -370,13 +386,14 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
             if (!ok) break;
             ptx::tc_fence_after();
             const uint64_t vd = vdesc0 + ((sl * kAttnTile) >> 4);
+            const uint32_t t_o = tmem_base + kAttnTmemO + 128 * (rows & 1), t_p = tmem_base + 128 * b;
 #pragma unroll
-            for (int k = 0; k < 8; ++k)  // K step k: P columns [8k, 8k+8) hold key positions [16k, 16k+16)
-              ptx::mma_f16_ts(tmem_base + kAttnTmemO, tmem_base + 128 * b + 8 * k, vd + ((k * 2048) >> 4),
-                              IDESC_PV, (j == 0 && k == 0) ? 0u : 1u);
+            for (int k = 0; k < 8; ++k)  // K step k: keys [16k, 16k+16) in P columns 8k (+32 for the second half)
+              ptx::mma_f16_ts(t_o, t_p + 8 * k + (k >= 4 ? 32 : 0), vd + ((k * 2048) >> 4), IDESC_PV,
+                              (j == 0 && k == 0) ? 0u : 1u);
             ptx::mma_commit(ptx::smem_u32(&kv_empty[sl]));
             ptx::mma_commit(ptx::smem_u32(&s_free[b]));
-            if (j == n - 1) ptx::mma_commit(ptx::smem_u32(o_done));
+            if (j == n - 1) ptx::mma_commit(ptx::smem_u32(&o_done[rows & 1]));
           }
         }
         seq += 2 * n;
@@ -397,17 +414,17 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     const int q = warp & 3;         // TMEM lane quarter
     const int r = 32 * q + lane;    // query row within the block == TMEM lane
     const uint32_t lane_off = static_cast<uint32_t>(32 * q) << 16;
-    const uint32_t tO = tmem_base + kAttnTmemO + lane_off + h * kHalfD;  // this warp's O columns
-    const uint32_t tX = tmem_base + kAttnTmemX + lane_off;
+    const uint32_t tO0 = tmem_base + kAttnTmemO + lane_off + h * kHalfD;  // this warp's O columns (buffer 0)
     const float c = a.scale_log2;
     uint32_t g = 0, rows = 0, x_cnt = 0;
     bool ok = true;
-    // Row-wise exchange with the warp of the other key half (same rows): store this half's value in TMEM, meet on
-    // the quarter's barrier of this slot, read the other half's value. Slots alternate, so a value is read before
-    // its column is written again.
-    auto exchange = [&](float v, float& other) -> bool {
+    // Row-wise exchange with the warp of the other key half (same rows): store this half's value in the last column
+    // of its own key range of the S buffer (63 or 127: already loaded, and P lands in columns [0, 32) and [64, 96)),
+    // meet on the quarter's barrier, read the other half's column. The buffer is rewritten only after PV of this
+    // block, which follows both halves' P and so both reads.
+    auto exchange = [&](uint32_t tSb, float v, float& other) -> bool {
       const uint32_t slot = x_cnt & 1;
-      ptx::tmem_st_32x32b_x1(tX + 4 * slot + h, __float_as_uint(v));
+      ptx::tmem_st_32x32b_x1(tSb + 64 * h + 63, __float_as_uint(v));
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       __syncwarp();
@@ -416,7 +433,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       if (!warp_wait_bounded(xb, (x_cnt >> 1) & 1, ctl, 23)) return false;
       ++x_cnt;
       ptx::tc_fence_after();
-      other = __uint_as_float(ptx::tmem_ld_32x32b_x1(tX + 4 * slot + (h ^ 1)));
+      other = __uint_as_float(ptx::tmem_ld_32x32b_x1(tSb + 64 * (h ^ 1) + 63));
       ptx::tmem_wait_ld();
       return true;
     };
@@ -437,6 +454,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         continue;
       }
       float m_run = -INFINITY, l_run = 0.0f;  // m_run in scaled log2 units; l_run sums this half's keys
+      const uint32_t tO = tO0 + 128 * (rows & 1);  // this row's O buffer
       int cidx = 0;  // lane l: column index of nonzero (j & ~31) + l of the row (warp-level prefetch)
       for (int j = 0; j < rn; ++j, ++g) {
         if ((j & 31) == 0) cidx = (j + lane < rn) ? __ldg(&a.col_idx[rj0 + j + lane]) : 0;
@@ -450,7 +468,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
         uint32_t sv[64];  // this half of the S row, loaded straight into the registers the softmax works in
         ptx::tmem_ld_32x32b_x32(tS + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
         ptx::tmem_ld_32x32b_x32(tS + 64 * h + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
-        ptx::tmem_wait_ld();  // (before the exchange: the other half overwrites columns 32..63 with P after it)
+        ptx::tmem_wait_ld();
         float* v = reinterpret_cast<float*>(sv);
         if (diag) {
 #pragma unroll
@@ -467,7 +485,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           for (int k = 0; k < 8; ++k) pm[k] = max3f(pm[k], v[i + k], v[i + 8 + k]);
         const float mh = max3f(max3f(pm[0], pm[1], pm[2]), max3f(pm[3], pm[4], pm[5]), fmaxf(pm[6], pm[7]));
         float mo;
-        ok = exchange(mh, mo);
+        ok = exchange(tS, mh, mo);
         if (!ok) break;
         const float mbs = fmaxf(mh, mo) * c;
         const bool move = mbs > m_run + 8.0f;
@@ -517,7 +535,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
           }
         }
         // P of this half (32 packed columns) -> TMEM columns [32 h, 32 h + 32) of the S buffer.
-        ptx::tmem_st_32x32b_x32(tS + 32 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+        ptx::tmem_st_32x32b_x32(tS + 64 * h, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
@@ -527,7 +545,7 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       // Hand this half's row sum (and half 0's max, for the LSE) to the output warps. The previous row's values
       // must have been read first (its O read completes after them).
       if (rows > 0) {
-        ok = warp_wait_bounded(ptx::smem_u32(o_free), (rows - 1) & 1, ctl, 24);
+        ok = warp_wait_bounded(ptx::smem_u32(&o_free[(rows - 1) & 1]), ((rows - 1) >> 1) & 1, ctl, 24);
         if (!ok) break;
       }
       l_part[h * 128 + r] = l_run;
@@ -540,7 +558,8 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
     // ------------------------------------------------------------------ output (warps 12..15)
     const int q = warp & 3;
     const int r = 32 * q + lane;
-    const uint32_t tO = tmem_base + kAttnTmemO + (static_cast<uint32_t>(32 * q) << 16);
+    const uint32_t tO0 = tmem_base + kAttnTmemO + (static_cast<uint32_t>(32 * q) << 16);
+    const bool o_v8 = (reinterpret_cast<uintptr_t>(a.O) & 31) == 0;  // rows are multiples of 32 bytes apart
     uint32_t rows = 0;
     bool ok = true;
     for (int item = blockIdx.x; item < a.num_items && ok; item += gridDim.x) {
@@ -548,35 +567,45 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       attn_row(a, item, bh, qb, j0, n);
       if (n == 0) continue;  // written by the softmax warps
       ok = warp_wait_bounded<false, 256>(ptx::smem_u32(l_ready), rows & 1, ctl, 25);
-      if (ok) ok = warp_wait_bounded<false, 256>(ptx::smem_u32(o_done), rows & 1, ctl, 22);
+      if (ok) ok = warp_wait_bounded<false, 256>(ptx::smem_u32(&o_done[rows & 1]), (rows >> 1) & 1, ctl, 22);
       if (!ok) break;
+      const uint32_t tO = tO0 + 128 * (rows & 1);
+      const uint32_t ob = rows & 1;
       ++rows;
       ptx::tc_fence_after();
       const float l_tot = l_part[r] + l_part[128 + r];  // half 0 + half 1, a fixed order
       const float m_run = m_row[r];
       const int64_t grow = static_cast<int64_t>(bh) * a.S + qb * kAttnBlk + r;
-      uint16_t* orow = static_cast<uint16_t*>(a.O) + grow * kD;
       const float inv_l = l_tot > 0.0f ? 1.0f / l_tot : 0.0f;
       // l sums 2^(s*c - m_run) whatever m_run lagged behind, so m_run + log2(l) is exact
       if (a.lse) a.lse[grow] = l_tot > 0.0f ? (m_run + log2f(l_tot)) * 0.6931471805599453f : -INFINITY;
+      // O / l in 16 bits, 32-byte stores (one sector each): 32 columns of the row per TMEM load.
+      uint16_t* orow = static_cast<uint16_t*>(a.O) + grow * kD;
 #pragma unroll 1
       for (int cc = 0; cc < kD / 32; ++cc) {
+#if OUT_PACE_NS
+        if (cc) __nanosleep(OUT_PACE_NS);
+#endif
         uint32_t u[32];
         ptx::tmem_ld_32x32b_x32(tO + cc * 32, u);
         ptx::tmem_wait_ld();
-        uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+        uint32_t pk[16];
 #pragma unroll
-        for (int gg = 0; gg < 4; ++gg) {
-          dst[gg] = make_uint4(
-              pack2<kF16>(__uint_as_float(u[8 * gg + 0]) * inv_l, __uint_as_float(u[8 * gg + 1]) * inv_l),
-              pack2<kF16>(__uint_as_float(u[8 * gg + 2]) * inv_l, __uint_as_float(u[8 * gg + 3]) * inv_l),
-              pack2<kF16>(__uint_as_float(u[8 * gg + 4]) * inv_l, __uint_as_float(u[8 * gg + 5]) * inv_l),
-              pack2<kF16>(__uint_as_float(u[8 * gg + 6]) * inv_l, __uint_as_float(u[8 * gg + 7]) * inv_l));
+        for (int i = 0; i < 16; ++i)
+          pk[i] = pack2<kF16>(__uint_as_float(u[2 * i]) * inv_l, __uint_as_float(u[2 * i + 1]) * inv_l);
+        if (o_v8) {
+          st_global_v8(orow + cc * 32, pk);
+          st_global_v8(orow + cc * 32 + 16, pk + 8);
+        } else {
+          uint4* dst = reinterpret_cast<uint4*>(orow + cc * 32);
+#pragma unroll
+          for (int gg = 0; gg < 4; ++gg)
+            dst[gg] = make_uint4(pk[4 * gg], pk[4 * gg + 1], pk[4 * gg + 2], pk[4 * gg + 3]);
         }
       }
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(o_free));
+      if (lane == 0) ptx::mbar_arrive(ptx::smem_u32(&o_free[ob]));
     }
   }
 

@@ -114,3 +114,22 @@ def test_bsattn_rejects_head_dim(cuda_dev, dtype, D):
     with pytest.raises(_capi.BskError) as e:
         _fwd(q)(q, q, q, torch.empty_like(q), rp, ci, 0.125)
     assert e.value.code == _capi.BSK_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("dtype,D", [(torch.bfloat16, 128), (torch.float16, 64)])
+def test_bsattn_output_16_byte_aligned_only(no_device_error, dtype, D):
+    """O that starts 16 bytes past a 32-byte boundary (the ABI asks for 16-byte alignment only): the output warps
+    fall back from 32-byte to 16-byte stores and the result is the same as into an aligned O."""
+    cfg = wl.AttnCfg(1, 2, 1024, D, 128, 4, 8, 6)
+    q, k, v = wl.attn_inputs(cfg, "cpu", dtype)
+    rp, ci = wl.attn_mask_bsr(cfg)
+    dev = torch.device("cuda", 0)
+    big = torch.full((q.numel() + 64,), float("nan"), dtype=dtype, device=dev)
+    off = (32 - big.data_ptr() % 32) // 2 + 8  # elements: 16 bytes past a 32-byte boundary
+    O = big[off:off + q.numel()].view(q.shape)
+    assert O.data_ptr() % 32 == 16
+    _fwd(q)(q.to(dev), k.to(dev), v.to(dev), O, rp.to(torch.int32).to(dev), ci.to(torch.int32).to(dev), 0.0883, True,
+            0, 2)
+    torch.cuda.synchronize()
+    assert torch.equal(O.cpu(), _run(q, k, v, rp, ci, 0.0883))
+    assert torch.isnan(big[:off]).all() and torch.isnan(big[off + q.numel():]).all()  # nothing written outside O
