@@ -224,15 +224,23 @@ __global__ void attn_full_mask_kernel(int pairs, int nqb, int causal, int* __res
   }
 }
 
+// 32 scaled columns of this thread's row -> 16-bit values at dst (64 bytes): two 32-byte stores (one sector each)
+// when dst is 32-byte aligned (every row is, when the tensor is: rows are multiples of 32 bytes apart), else four
+// 16-byte stores. Each thread writes its own row, so fewer, wider stores mean fewer memory transactions per warp.
 template <bool kF16>
 __device__ __forceinline__ void store_row_half(uint16_t* dst, const uint32_t (&u)[32], float mul) {
-  uint4* d = reinterpret_cast<uint4*>(dst);
+  uint32_t pk[16];
 #pragma unroll
-  for (int g = 0; g < 4; ++g)
-    d[g] = make_uint4(pack2<kF16>(__uint_as_float(u[8 * g + 0]) * mul, __uint_as_float(u[8 * g + 1]) * mul),
-                      pack2<kF16>(__uint_as_float(u[8 * g + 2]) * mul, __uint_as_float(u[8 * g + 3]) * mul),
-                      pack2<kF16>(__uint_as_float(u[8 * g + 4]) * mul, __uint_as_float(u[8 * g + 5]) * mul),
-                      pack2<kF16>(__uint_as_float(u[8 * g + 6]) * mul, __uint_as_float(u[8 * g + 7]) * mul));
+  for (int i = 0; i < 16; ++i)
+    pk[i] = pack2<kF16>(__uint_as_float(u[2 * i]) * mul, __uint_as_float(u[2 * i + 1]) * mul);
+  if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+    st_global_v8(dst, pk);
+    st_global_v8(dst + 16, pk + 8);
+  } else {
+    uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+    for (int g = 0; g < 4; ++g) d[g] = make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+  }
 }
 
 // TMEM columns [t0 + 32 * (D/64) * x, ...) of this thread's row (kD/2 columns: warpgroup x's half of an
