@@ -181,17 +181,6 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
   return kF16 ? pack_f16(lo, hi) : pack_bf16(lo, hi);
 }
 
-// 32-byte global store (sm_100 256-bit vector store); p 32-byte aligned.
-__device__ __forceinline__ void st_global_v8(void* p, const uint32_t* v) {
-  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]),
-               "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
-               : "memory");
-}
-
-__device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-
 template <bool kF16, int kD>
 __global__ void __launch_bounds__(kAttnThreads, 1)
     bsattn_sm100_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,

@@ -258,7 +258,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kPairThreads, 1)
                                                        __uint_as_float(r[2 * i + 1]) * scale);
               pk[i] = *reinterpret_cast<uint32_t*>(&h);
             }
-            if (a.vec_ok && col0 + 32 <= a.N) {
+            if (a.vec_ok && col0 + 32 <= a.N && (reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+              st_global_v8(dst, pk);
+              st_global_v8(dst + 16, pk + 8);
+            } else if (a.vec_ok && col0 + 32 <= a.N) {
 #pragma unroll
               for (int v = 0; v < 4; ++v)
                 st_global_v4(reinterpret_cast<float*>(dst + 8 * v), pk[4 * v], pk[4 * v + 1], pk[4 * v + 2],

@@ -166,8 +166,13 @@ __device__ __forceinline__ void store_row32_f32(float* dst, uint32_t (&r)[32], b
         r[4 * v + 3] = __float_as_uint(c.w + __uint_as_float(r[4 * v + 3]));
       }
     }
+    if ((reinterpret_cast<uintptr_t>(dst) & 31) == 0) {  // 32-byte stores: one sector each
 #pragma unroll
-    for (int v = 0; v < 8; ++v) st_global_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+      for (int v = 0; v < 4; ++v) st_global_v8(dst + 8 * v, &r[8 * v]);
+    } else {
+#pragma unroll
+      for (int v = 0; v < 8; ++v) st_global_v4(dst + 4 * v, r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+    }
   } else {
     for (int i = 0; i < 32; ++i)
       if (i < valid) dst[i] = accumulate ? dst[i] + __uint_as_float(r[i]) : __uint_as_float(r[i]);
@@ -553,7 +558,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                                                      __uint_as_float(r[2 * i + 1]) * scale);
             pk[i] = *reinterpret_cast<uint32_t*>(&h);
           }
-          if (a.vec_ok && col0 + 32 <= a.N) {
+          if (a.vec_ok && col0 + 32 <= a.N && (reinterpret_cast<uintptr_t>(dst) & 31) == 0) {
+            st_global_v8(dst, pk);
+            st_global_v8(dst + 16, pk + 8);
+          } else if (a.vec_ok && col0 + 32 <= a.N) {
 #pragma unroll
             for (int v = 0; v < 4; ++v)
               st_global_v4(reinterpret_cast<float*>(dst + 8 * v), pk[4 * v], pk[4 * v + 1], pk[4 * v + 2],

@@ -429,6 +429,13 @@ __device__ __forceinline__ void setmaxnreg_dec() {
 
 }  // namespace ptx
 
+// 32-byte global store (sm_100 256-bit vector store, one sector); p 32-byte aligned.
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t* v) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
 // ---------------------------------------------------------------- bounded waits
 // Device-side error word layout (shared by every kernel of this library):
 //   bits [0,8)  error kind (kErrWaitTimeout, kErrBounds)
