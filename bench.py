@@ -60,7 +60,9 @@ def parse_args():
     p.add_argument("--tune-cache-out", default=None, metavar="PATH",
                    help="write the autotune op's results as a cache file at PATH")
     p.add_argument("--e2e-k-chunk", type=int, default=0, help="K per streamed chunk of the e2e GEMM (0 = auto)")
-    p.add_argument("--op-steps", type=int, default=20, help="timed steps of the fp8 / bsr / attn measurements")
+    p.add_argument("--op-steps", type=int, default=100,
+                   help="timed steps of the fp8 / bsr / attn / ... measurements (regions of ~15-200 ms, long enough for "
+                        "several clock samples each)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     return p.parse_args()
 
