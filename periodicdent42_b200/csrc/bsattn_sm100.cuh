@@ -31,7 +31,8 @@
 // lockstep. The MUFU computes 16 exp2 per clock per SM in the f32, f16x2 and bf16x2 forms alike (measured), so packed
 // exponentials do not raise that ceiling. Output warps reading O 64 columns per TMEM round trip (903 vs 920), a
 // non-blocking test of the next block's S before the P store (914 vs 920), pacing the output warps' stores (within
-// 0.5 %) and loading the next row's column indices during a row's first block (901 vs 923) were no better.
+// 0.5 %), loading the next row's column indices during a row's first block (901 vs 923) and exchanging bf16
+// maxima through the 1 KB of shared memory that the alignment pad would take (920 vs 928) were no better.
 //
 // Roles (16 warps): warp 0 TMA producer, warp 1 TMEM owner + S issuer, warp 2 PV issuer, warp 3 idle, warps 4-11
 // softmax, warps 12-15 output (O / l from TMEM to global once a row's last PV completed, so the softmax warps go
