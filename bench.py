@@ -60,6 +60,8 @@ def parse_args():
     p.add_argument("--tune-cache-out", default=None, metavar="PATH",
                    help="write the autotune op's results as a cache file at PATH")
     p.add_argument("--e2e-k-chunk", type=int, default=0, help="K per streamed chunk of the e2e GEMM (0 = auto)")
+    p.add_argument("--nshard-k-splits", type=int, default=0,
+                   help="K splits of each rank's N-shard GEMM (0 = automatic: nshard_k_splits)")
     p.add_argument("--op-steps", type=int, default=100,
                    help="timed steps of the fp8 / bsr / attn / ... measurements (regions of ~15-200 ms, long enough for "
                         "several clock samples each)")
@@ -292,6 +294,20 @@ def _check_entry(ctx: Ctx, err: float, tol: float, sample: str) -> dict:
 
 
 # ----------------------------------------------------------------------------------------- dense GEMM
+def nshard_k_splits(M: int, n_local: int, K: int, sm_count: int) -> int:
+    """K splits for one rank's N-shard of the headline GEMM: 2 when the shard has at least two waves of 256 x 512
+    tiles on the CTA pairs and splitting K in two fills the last wave markedly better (the 2-rank shard
+    8192 x 4096: 256 tiles on 74 pairs fill 86.5 % of the pairs' slots, 512 (tile, split) units 98.8 %; measured
+    1208 vs 1146 TFLOPS on one B200), else 1. Narrower shards measured no gain (8192 x 2048 with 4 splits) or a
+    loss (8192 x 1024 with 8), and long K is needed so each split keeps the long-K raster."""
+    pairs = max(1, sm_count // 2)
+    tiles = -(-M // 256) * -(-n_local // 512)
+    fill = lambda units: units / (-(-units // pairs) * pairs)  # noqa: E731
+    if tiles >= 2 * pairs and K >= 2 * 65536 and fill(2 * tiles) >= fill(tiles) + 0.05:
+        return 2
+    return 1
+
+
 def bench_cublas_dense(ctx: Ctx, args, res: dict):
     """Same-box yardstick, opt-in (`--ops dense,cublas`): the library GEMM (cuBLAS through torch.matmul, fp16 in,
     fp16 out) on the dense workload's shape and inputs. Not the product path. Its timed region gets its own clock
@@ -321,14 +337,24 @@ def dense_cfg(args) -> wl.DenseCfg:
 def bench_dense(ctx: Ctx, args, res: dict):
     cfg = dense_cfg(args)
     A, Bt = wl.dense_inputs(cfg, ctx.dev)
+    k_splits = 1
     if args.dense_mode == "nshard":
         n0, n1 = sharding.dense_nshard(cfg.N, ctx.world, ctx.rank)
         Bt_r = Bt[n0:n1]
         C_r = torch.empty(cfg.M, n1 - n0, device=ctx.dev)
+        k_splits = args.nshard_k_splits or nshard_k_splits(cfg.M, n1 - n0, cfg.K,
+                                                           torch.cuda.get_device_properties(ctx.dev).multi_processor_count)
+        if k_splits > 1:  # the shard's tiles leave the last wave of CTA pairs half empty: split K to fill it
+            ws = torch.empty(_capi.gemm_splitk_workspace_bytes(cfg.M, n1 - n0, cfg.K, k_splits), dtype=torch.uint8,
+                             device=ctx.dev)
 
-        def step():
-            _capi.gemm_f16f32(A, Bt_r, C_r, stream=ctx.stream)
-        launches = 1
+            def step():
+                _capi.gemm_f16f32_splitk(A, Bt_r, C_r, k_splits, workspace=ws, stream=ctx.stream)
+            launches = 2  # GEMM over (tile, split) units + the split reduction
+        else:
+            def step():
+                _capi.gemm_f16f32(A, Bt_r, C_r, stream=ctx.stream)
+            launches = 1
         comm = None
     elif args.dense_mode == "splitk_nccl":
         k0, k1 = sharding.dense_ksplit(cfg.K, ctx.world, ctx.rank)
@@ -360,7 +386,7 @@ def bench_dense(ctx: Ctx, args, res: dict):
     total_flops = cfg.flops
     tflops = total_flops / (ms * 1e-3) / 1e12
     res["dense"] = {"ms": ms, "tflops": tflops, "flops": total_flops, "launches_per_step": launches,
-                    "mode": args.dense_mode, "comm": comm,
+                    "mode": args.dense_mode, "comm": comm, "per_rank_k_splits": k_splits,
                     "per_rank_flops": total_flops / ctx.world}
     torch.cuda.synchronize()
     if args.dense_mode == "nshard":  # this rank's output columns [n0, n1)

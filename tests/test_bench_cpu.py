@@ -86,3 +86,11 @@ def test_self_check_helpers():
     p = bench._pick(100, 10, 1)
     assert p.numel() == 10 and torch.equal(p, torch.sort(p).values) and torch.equal(p, bench._pick(100, 10, 1))
     assert bench._pick(5, 10, 1).numel() == 5
+
+
+def test_nshard_k_splits_policy():
+    """The benchmark's per-rank split of K: only the 2-rank shard of the headline (half-empty last wave of CTA pairs,
+    long K) is split."""
+    bench = _bench_module()
+    assert [bench.nshard_k_splits(8192, n, 237568, 148) for n in (8192, 4096, 2048, 1024)] == [1, 2, 1, 1]
+    assert bench.nshard_k_splits(8192, 4096, 16384, 148) == 1  # short K: no split
