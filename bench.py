@@ -62,9 +62,10 @@ def parse_args():
     p.add_argument("--e2e-k-chunk", type=int, default=0, help="K per streamed chunk of the e2e GEMM (0 = auto)")
     p.add_argument("--nshard-k-splits", type=int, default=0,
                    help="K splits of each rank's N-shard GEMM (0 = automatic: nshard_k_splits)")
-    p.add_argument("--op-steps", type=int, default=100,
-                   help="timed steps of the fp8 / bsr / attn / ... measurements (regions of ~15-200 ms, long enough for "
-                        "several clock samples each)")
+    p.add_argument("--op-steps", type=int, default=20,
+                   help="timed steps of the fp8 / bsr / attn / ... measurements: short regions (~5-40 ms) that run "
+                        "at the full clock, like the burst peak they are compared with (100 steps: the clock sags "
+                        "under the load and FP8 / attention read 7-8 %% lower)")
     p.add_argument("--cpu-seconds", type=float, default=12.0, help="budget of the CPU baseline sample")
     return p.parse_args()
 
