@@ -573,9 +573,6 @@ __global__ void __launch_bounds__(kAttnThreads, 1)
       uint16_t* orow = static_cast<uint16_t*>(a.O) + grow * kD;
 #pragma unroll 1
       for (int cc = 0; cc < kD / 32; ++cc) {
-#if OUT_PACE_NS
-        if (cc) __nanosleep(OUT_PACE_NS);
-#endif
         uint32_t u[32];
         ptx::tmem_ld_32x32b_x32(tO + cc * 32, u);
         ptx::tmem_wait_ld();
