@@ -971,7 +971,7 @@ def main():
         line = {"metric": METRIC, "value": d["tflops"] if d else None, "unit": UNIT, "n_gpus": ctx.world,
                 "steps": args.steps, "warmup": args.warmup, "ms_per_step": d["ms"] if d else None,
                 "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
-                "data": "synthetic (seeded device RNG, BASELINE shapes and distributions)",
+                "data": "synthetic (seeded device RNG, the benchmark configurations' shapes and distributions)",
                 "config": {"workload": "dense fp16->fp32 GEMM M=8192 N=8192 K=237568 (A row-major, B col-major)"
                            if not args.shape else f"dense fp16->fp32 GEMM {args.shape} (profiling case)",
                            "parallelism": f"{args.dense_mode} x{ctx.world}",
