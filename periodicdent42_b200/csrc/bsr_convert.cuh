@@ -316,6 +316,92 @@ __global__ void __launch_bounds__(kConvThreads) bsr_compact_kernel(int* __restri
   }
 }
 
+// The whole index pass of a small block grid (Mb <= kIndexSmallMaxRows, Mb * Kb <= kIndexSmallMaxFlags) in one
+// CTA: per-block-row counts of the flags, their exclusive scan into row_ptr[0..Mb] and nnzb, then per block-row
+// the ascending ranks of the flagged blocks (col_idx / block_row below `cap`, flags turned into the block-index
+// map) -- what bsr_row_counts_kernel, bsr_row_ptr_kernel and bsr_compact_kernel do in three launches.
+constexpr int kIndexSmallThreads = 1024;
+constexpr int kIndexSmallMaxRows = 4096;
+constexpr int64_t kIndexSmallMaxFlags = int64_t(1) << 18;
+
+template <typename IdxOut>
+__global__ void __launch_bounds__(kIndexSmallThreads) bsr_index_small_kernel(int* __restrict__ flags, int Mb, int Kb,
+                                                                           IdxOut* __restrict__ row_ptr,
+                                                                           IdxOut* __restrict__ col_idx,
+                                                                           int* __restrict__ block_row, int64_t cap,
+                                                                           long long* __restrict__ nnzb_out) {
+  constexpr int kWarps = kIndexSmallThreads / 32;
+  constexpr int kPerThread = kIndexSmallMaxRows / kIndexSmallThreads;  // rows whose counts a thread scans
+  __shared__ int off[kIndexSmallMaxRows];
+  __shared__ int warp_tot[kWarps];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // 1. flagged blocks per block-row (a warp per row)
+  for (int br = warp; br < Mb; br += kWarps) {
+    const int* f = flags + static_cast<int64_t>(br) * Kb;
+    int c = 0;
+    for (int j = lane; j < Kb; j += 32) c += f[j] != 0;
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_xor_sync(0xFFFFFFFFu, c, o);
+    if (lane == 0) off[br] = c;
+  }
+  __syncthreads();
+  // 2. exclusive scan: thread t owns rows [kPerThread t, kPerThread t + kPerThread)
+  int local[kPerThread];
+  int sum = 0;
+#pragma unroll
+  for (int u = 0; u < kPerThread; ++u) {
+    const int br = kPerThread * threadIdx.x + u;
+    local[u] = br < Mb ? off[br] : 0;
+    sum += local[u];
+  }
+  int incl = sum;
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xFFFFFFFFu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  int before = incl - sum;
+  for (int w = 0; w < warp; ++w) before += warp_tot[w];
+#pragma unroll
+  for (int u = 0; u < kPerThread; ++u) {
+    const int br = kPerThread * threadIdx.x + u;
+    if (br < Mb) {
+      off[br] = before;
+      row_ptr[br] = static_cast<IdxOut>(before);
+    }
+    before += local[u];
+  }
+  if (threadIdx.x == kIndexSmallThreads - 1) {  // the last thread's running sum is the total
+    row_ptr[Mb] = static_cast<IdxOut>(before);
+    *nnzb_out = before;
+  }
+  __syncthreads();
+  // 3. ranks within each block-row (a warp per row, 32 flags per step)
+  for (int br = warp; br < Mb; br += kWarps) {
+    int* f = flags + static_cast<int64_t>(br) * Kb;
+    const int64_t start = off[br];
+    int carry = 0;
+    for (int base = 0; base < Kb; base += 32) {
+      const int j = base + lane;
+      const bool on = j < Kb && f[j] != 0;
+      const unsigned bal = __ballot_sync(0xFFFFFFFFu, on);
+      const int64_t pos = start + carry + __popc(bal & ((1u << lane) - 1u));
+      if (j < Kb) {
+        if (on) {
+          if (pos < cap) {  // positions past the caller's capacity are mapped but not written
+            col_idx[pos] = static_cast<IdxOut>(j);
+            block_row[pos] = br;
+          }
+          f[j] = static_cast<int>(pos);
+        } else {
+          f[j] = -1;
+        }
+      }
+      carry += __popc(bal);
+    }
+  }
+}
+
 // Fill, step 2 (dense): values[p] = the dense block of stored block p, reading only the stored blocks, for
 // p < min(nnzb, cap) (nnzb read from device memory). A warp task is kConvU x 32 units (16-byte chunks when kVec,
 // else elements) of one block; block p sits at block-row block_row[p] and block column col_idx[p].

@@ -1283,6 +1283,25 @@ int conv_compact(const ConvPlan& p, const ConvWs& w, const void* row_ptr, void* 
   return launch_status("bsr compact");
 }
 
+// Single-call converters on a small block grid: the index pass (counts, row_ptr, ranks) in one CTA.
+bool conv_small(const ConvPlan& p) {
+  return p.Mb > 0 && p.Mb <= bsk::kIndexSmallMaxRows && (int64_t)p.Mb * p.Kb <= bsk::kIndexSmallMaxFlags;
+}
+
+int conv_index_small(const ConvPlan& p, const ConvWs& w, void* row_ptr, void* col_idx, int index_bytes, int64_t cap,
+                     cudaStream_t s) {
+  using namespace bsk;
+  if (index_bytes == 4)
+    bsr_index_small_kernel<int32_t><<<1, kIndexSmallThreads, 0, s>>>(w.flags, p.Mb, p.Kb, static_cast<int32_t*>(row_ptr),
+                                                                     static_cast<int32_t*>(col_idx), w.block_row, cap,
+                                                                     &w.tail->nnzb);
+  else
+    bsr_index_small_kernel<int64_t><<<1, kIndexSmallThreads, 0, s>>>(w.flags, p.Mb, p.Kb, static_cast<int64_t*>(row_ptr),
+                                                                     static_cast<int64_t*>(col_idx), w.block_row, cap,
+                                                                     &w.tail->nnzb);
+  return launch_status("bsr index");
+}
+
 bool dense_vec_ok(const void* A, int64_t lda, int elem_bytes, int bs) {
   const int per = 16 / elem_bytes;
   return aligned16(A) && lda % per == 0 && bs % per == 0;
@@ -1296,7 +1315,7 @@ namespace {
 // and nnzb in the workspace tail.
 int dense_pattern_enqueue(const void* A, int64_t lda, int elem_bytes, int M, int K, int bs, void* row_ptr,
                           int index_bytes, const ConvPlan& p, void* workspace, const DeviceState* st, cudaStream_t s,
-                          const char* what) {
+                          const char* what, bool index = true) {
   using namespace bsk;
   if (int rc = conv_clear(p, workspace, s, what)) return rc;
   const ConvWs w = conv_ws(p, workspace);
@@ -1312,6 +1331,7 @@ int dense_pattern_enqueue(const void* A, int64_t lda, int elem_bytes, int M, int
       else dense_flags_scalar_kernel<4><<<g, kConvThreads, 0, s>>>(a, lda, M, K, bs, p.Kb, w.flags, counter);
     }
   }
+  if (!index) return launch_status(what);
   if (p.Mb > 0) {
     const int g = p.Mb < conv_grid(st) ? p.Mb : conv_grid(st);
     bsr_row_counts_kernel<<<g, kConvThreads, 0, s>>>(w.flags, p.Mb, p.Kb, w.counts);
@@ -1325,7 +1345,7 @@ int dense_pattern_enqueue(const void* A, int64_t lda, int elem_bytes, int M, int
 
 int csr_pattern_enqueue(const void* crow, const void* col, int index_bytes_in, const void* vals, int elem_bytes,
                         int64_t nnz, int M, int K, int bs, void* row_ptr, int index_bytes, const ConvPlan& p,
-                        void* workspace, const DeviceState* st, cudaStream_t s, const char* what) {
+                        void* workspace, const DeviceState* st, cudaStream_t s, const char* what, bool index = true) {
   using namespace bsk;
   if (int rc = conv_clear(p, workspace, s, what)) return rc;
   const ConvWs w = conv_ws(p, workspace);
@@ -1338,6 +1358,7 @@ int csr_pattern_enqueue(const void* crow, const void* col, int index_bytes_in, c
       launch_csr_flags<int64_t>(elem_bytes, crow, col, vals, nnz, M, K, bs, p.Kb, w.flags, &w.tail->nnz_elems,
                                 &w.tail->bad, g, s);
   }
+  if (!index) return launch_status(what);
   if (p.Mb > 0) {
     const int g = p.Mb < conv_grid(st) ? p.Mb : conv_grid(st);
     bsr_row_counts_kernel<<<g, kConvThreads, 0, s>>>(w.flags, p.Mb, p.Kb, w.counts);
@@ -1368,10 +1389,11 @@ int conv_read_tail(const ConvPlan& p, void* workspace, int index_bytes, int64_t*
 // Fill pass: col_idx, block_row and the map, then the values of the first min(nnzb, cap) blocks.
 int dense_fill_enqueue(const void* A, int64_t lda, int elem_bytes, int bs, const void* row_ptr, void* col_idx,
                        int index_bytes, void* values, int64_t cap, const ConvPlan& p, void* workspace,
-                       const DeviceState* st, cudaStream_t s, const char* what) {
+                       const DeviceState* st, cudaStream_t s, const char* what, bool compact = true) {
   using namespace bsk;
   const ConvWs w = conv_ws(p, workspace);
-  if (int rc = conv_compact(p, w, row_ptr, col_idx, index_bytes, cap, st, s)) return rc;
+  if (compact)
+    if (int rc = conv_compact(p, w, row_ptr, col_idx, index_bytes, cap, st, s)) return rc;
   const uint8_t* a = static_cast<const uint8_t*>(A);
   uint8_t* v = static_cast<uint8_t*>(values);
   const bool vec = dense_vec_ok(A, lda, elem_bytes, bs) && aligned16(values);
@@ -1394,10 +1416,11 @@ int dense_fill_enqueue(const void* A, int64_t lda, int elem_bytes, int bs, const
 int csr_fill_enqueue(const void* crow, const void* col, int index_bytes_in, const void* vals, int elem_bytes,
                      int64_t nnz, int M, int K, int bs, const void* row_ptr, void* col_idx, int index_bytes,
                      void* values, int64_t cap, const ConvPlan& p, void* workspace, const DeviceState* st,
-                     cudaStream_t s, const char* what) {
+                     cudaStream_t s, const char* what, bool compact = true) {
   using namespace bsk;
   const ConvWs w = conv_ws(p, workspace);
-  if (int rc = conv_compact(p, w, row_ptr, col_idx, index_bytes, cap, st, s)) return rc;
+  if (compact)
+    if (int rc = conv_compact(p, w, row_ptr, col_idx, index_bytes, cap, st, s)) return rc;
   const int g = conv_grid(st);
   zero_blocks_kernel<<<g, kConvThreads, 0, s>>>(static_cast<uint8_t*>(values), &w.tail->nnzb, cap,
                                                 (int64_t)bs * bs * elem_bytes);
@@ -1479,11 +1502,15 @@ int bsk_dense_to_bsr_bounded(const void* A, int64_t lda, int elem_bytes, int M, 
   DeviceState* st;
   if (int rc = device_state(&st)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (int rc = dense_pattern_enqueue(A, lda, elem_bytes, M, K, bs, row_ptr, index_bytes, p, workspace, st, s, what))
+  const bool small = conv_small(p);
+  if (int rc = dense_pattern_enqueue(A, lda, elem_bytes, M, K, bs, row_ptr, index_bytes, p, workspace, st, s, what,
+                                     !small))
     return rc;
+  if (small)
+    if (int rc = conv_index_small(p, conv_ws(p, workspace), row_ptr, col_idx, index_bytes, max_nnzb, s)) return rc;
   if (max_nnzb == 0 || (int64_t)M * K == 0) return BSK_OK;
   return dense_fill_enqueue(A, lda, elem_bytes, bs, row_ptr, col_idx, index_bytes, values, max_nnzb, p, workspace,
-                            st, s, what);
+                            st, s, what, !small);
 }
 
 int bsk_csr_to_bsr_pattern(const void* crow, const void* col, int index_bytes_in, const void* vals, int elem_bytes,
@@ -1535,12 +1562,15 @@ int bsk_csr_to_bsr_bounded(const void* crow, const void* col, int index_bytes_in
   DeviceState* st;
   if (int rc = device_state(&st)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const bool small = conv_small(p);
   if (int rc = csr_pattern_enqueue(crow, col, index_bytes_in, vals, elem_bytes, nnz, M, K, bs, row_ptr, index_bytes, p,
-                                   workspace, st, s, what))
+                                   workspace, st, s, what, !small))
     return rc;
+  if (small)
+    if (int rc = conv_index_small(p, conv_ws(p, workspace), row_ptr, col_idx, index_bytes, max_nnzb, s)) return rc;
   if (max_nnzb == 0) return BSK_OK;
   return csr_fill_enqueue(crow, col, index_bytes_in, vals, elem_bytes, nnz, M, K, bs, row_ptr, col_idx, index_bytes,
-                          values, max_nnzb, p, workspace, st, s, what);
+                          values, max_nnzb, p, workspace, st, s, what, !small);
 }
 
 int bsk_bsattn_fwd_ex(int dtype, const void* Q, const void* K, const void* V, void* O, float* lse,

@@ -187,14 +187,15 @@ def test_sparse_mm_with_csr_input(no_device_error, cuda_dev):
 
 
 @pytest.mark.parametrize("kind", ["dense", "csr"])
-def test_bounded_single_call_matches_two_phase(no_device_error, cuda_dev, kind):
-    M, K, bs = 512, 768, 16
+# 32 x 48 blocks: the one-CTA index pass; 1024 x 1024 blocks (more than 2^18): the three-launch index pass
+@pytest.mark.parametrize("M,K,bs", [(512, 768, 16), (4096, 4096, 4)])
+def test_bounded_single_call_matches_two_phase(no_device_error, cuda_dev, kind, M, K, bs):
     x = _sparse_dense(M, K, bs, torch.float16, 31, block_density=0.3, elem_density=0.4)
     csr = x.to_sparse_csr()
     want = (csr.to_dense() if kind == "csr" else x).to_sparse_bsr((bs, bs))
     nnzb = want.col_indices().numel()
     ws = torch.empty(_capi.bsr_convert_workspace_bytes(M, K, bs), dtype=torch.uint8, device=cuda_dev)
-    for cap in (nnzb, nnzb + 50, nnzb - 7):  # exact, roomy, too small (truncated in BSR order)
+    for cap in (nnzb, nnzb + 50, nnzb - 7, 0):  # exact, roomy, too small (truncated in BSR order), none
         rp = torch.full((M // bs + 1,), -1, dtype=torch.int64, device=cuda_dev)
         ci = torch.full((cap,), -1, dtype=torch.int64, device=cuda_dev)
         v = torch.full((cap, bs, bs), 7.0, dtype=torch.float16, device=cuda_dev)
