@@ -18,7 +18,7 @@
 // this kernel on the attention workload puts a block at ~2000-2250 SM cycles, set by the softmax (TMEM load ~250, max
 // ~200, exchange ~300-550, exponentials ~950 -- the MUFU of a sub-partition shared by the two halves -- and ~200 per
 // barrier wait), against 1024 cycles of tensor work; the first two blocks of a row take ~2500 cycles more (a per-row
-// cost of ~4000 cycles in total, from a sweep of blocks per row). Variants measured slower on B200: speculative
+// cost of ~3300 cycles in total from a sweep of blocks per row, while the output warps write the previous row). Variants measured slower on B200: speculative
 // exponentials before the exchange (735 vs 890 TFLOPS), P in its own TMEM buffers with the exchange in shared memory
 // and one Q buffer (832 vs 887), independent halves with one O accumulator each (no exchange; P aliased onto S, so
 // S_{j+2} waits for PV_j: 850 vs 876), and both halves loading the whole S row to take the max without an exchange, P
