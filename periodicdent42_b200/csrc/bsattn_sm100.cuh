@@ -18,21 +18,22 @@
 // this kernel on the attention workload puts a block at ~2000-2250 SM cycles, set by the softmax (TMEM load ~250, max
 // ~200, exchange ~300-550, exponentials ~950 -- the MUFU of a sub-partition shared by the two halves -- and ~200 per
 // barrier wait), against 1024 cycles of tensor work; the first two blocks of a row take ~2500 cycles more (a per-row
-// cost of ~3300 cycles in total from a sweep of blocks per row, while the output warps write the previous row). Variants measured slower on B200: speculative
-// exponentials before the exchange (735 vs 890 TFLOPS), P in its own TMEM buffers with the exchange in shared memory
-// and one Q buffer (832 vs 887), independent halves with one O accumulator each (no exchange; P aliased onto S, so
-// S_{j+2} waits for PV_j: 850 vs 876), and both halves loading the whole S row to take the max without an exchange, P
-// in its own TMEM buffers so S_{j+2} only waits for S_j to be loaded (790 vs 917: the S row is read from TMEM twice,
-// and the longer load costs more than the exchange it removes), and suspend-hint waits (try_wait with a time hint)
-// for the MMA issuers (872 vs 884) or for the issuers and the softmax warps (867 vs 884): the re-polling waits stay.
-// Two blocks per softmax step (warps 4-7 take block 2t, warps 8-11 block 2t+1, each thread a whole 128-column row,
-// the two blocks' maxima exchanged once per pair, P in its own TMEM columns) ran at 744 vs 888: 128 live scores per
-// thread spill under the 176-register cap and the two warps of a sub-partition still run their exponentials in
-// lockstep. The MUFU computes 16 exp2 per clock per SM in the f32, f16x2 and bf16x2 forms alike (measured), so packed
-// exponentials do not raise that ceiling. Output warps reading O 64 columns per TMEM round trip (903 vs 920), a
-// non-blocking test of the next block's S before the P store (914 vs 920), pacing the output warps' stores (within
-// 0.5 %), loading the next row's column indices during a row's first block (901 vs 923) and exchanging bf16
-// maxima through the 1 KB of shared memory that the alignment pad would take (920 vs 928) were no better.
+// cost of ~3300 cycles in total from a sweep of blocks per row, while the output warps write the previous row).
+// Variants measured slower on B200: speculative exponentials before the exchange (735 vs 890 TFLOPS), P in its own
+// TMEM buffers with the exchange in shared memory and one Q buffer (832 vs 887), independent halves with one O
+// accumulator each (no exchange; P aliased onto S, so S_{j+2} waits for PV_j: 850 vs 876), and both halves loading
+// the whole S row to take the max without an exchange, P in its own TMEM buffers so S_{j+2} only waits for S_j to be
+// loaded (790 vs 917: the S row is read from TMEM twice, and the longer load costs more than the exchange it
+// removes), and suspend-hint waits (try_wait with a time hint) for the MMA issuers (872 vs 884) or for the issuers
+// and the softmax warps (867 vs 884): the re-polling waits stay. Two blocks per softmax step (warps 4-7 take block
+// 2t, warps 8-11 block 2t+1, each thread a whole 128-column row, the two blocks' maxima exchanged once per pair, P in
+// its own TMEM columns) ran at 744 vs 888: 128 live scores per thread spill under the 176-register cap and the two
+// warps of a sub-partition still run their exponentials in lockstep. The MUFU computes 16 exp2 per clock per SM in
+// the f32, f16x2 and bf16x2 forms alike (measured), so packed exponentials do not raise that ceiling. Output warps
+// reading O 64 columns per TMEM round trip (903 vs 920), a non-blocking test of the next block's S before the P store
+// (914 vs 920), pacing the output warps' stores (within 0.5 %), loading the next row's column indices during a row's
+// first block (901 vs 923) and exchanging bf16 maxima through the 1 KB of shared memory that the alignment pad would
+// take (920 vs 928) were no better.
 //
 // Roles (16 warps): warp 0 TMA producer, warp 1 TMEM owner + S issuer, warp 2 PV issuer, warp 3 idle, warps 4-11
 // softmax, warps 12-15 output (O / l from TMEM to global once a row's last PV completed, so the softmax warps go
