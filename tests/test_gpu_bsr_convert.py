@@ -189,15 +189,16 @@ def test_sparse_mm_with_csr_input(no_device_error, cuda_dev):
 @pytest.mark.parametrize("kind", ["dense", "csr"])
 # 32 x 48 blocks: the one-CTA index pass; 1024 x 1024 blocks (more than 2^18): the three-launch index pass
 @pytest.mark.parametrize("M,K,bs", [(512, 768, 16), (4096, 4096, 4)])
-def test_bounded_single_call_matches_two_phase(no_device_error, cuda_dev, kind, M, K, bs):
+@pytest.mark.parametrize("idx", [torch.int64, torch.int32])
+def test_bounded_single_call_matches_two_phase(no_device_error, cuda_dev, kind, M, K, bs, idx):
     x = _sparse_dense(M, K, bs, torch.float16, 31, block_density=0.3, elem_density=0.4)
     csr = x.to_sparse_csr()
     want = (csr.to_dense() if kind == "csr" else x).to_sparse_bsr((bs, bs))
     nnzb = want.col_indices().numel()
     ws = torch.empty(_capi.bsr_convert_workspace_bytes(M, K, bs), dtype=torch.uint8, device=cuda_dev)
     for cap in (nnzb, nnzb + 50, nnzb - 7, 0):  # exact, roomy, too small (truncated in BSR order), none
-        rp = torch.full((M // bs + 1,), -1, dtype=torch.int64, device=cuda_dev)
-        ci = torch.full((cap,), -1, dtype=torch.int64, device=cuda_dev)
+        rp = torch.full((M // bs + 1,), -1, dtype=idx, device=cuda_dev)
+        ci = torch.full((cap,), -1, dtype=idx, device=cuda_dev)
         v = torch.full((cap, bs, bs), 7.0, dtype=torch.float16, device=cuda_dev)
         if kind == "dense":
             _capi.dense_to_bsr_bounded(x.to(cuda_dev), bs, rp, ci, v, ws)
@@ -206,8 +207,8 @@ def test_bounded_single_call_matches_two_phase(no_device_error, cuda_dev, kind, 
                                      csr.values().to(cuda_dev), (M, K), bs, rp, ci, v, ws)
         torch.cuda.synchronize()
         n = min(cap, nnzb)
-        assert torch.equal(rp.cpu(), want.crow_indices())
-        assert torch.equal(ci.cpu()[:n], want.col_indices()[:n])
+        assert torch.equal(rp.cpu().long(), want.crow_indices())
+        assert torch.equal(ci.cpu().long()[:n], want.col_indices()[:n])
         assert torch.equal(_bits(v.cpu()[:n]), _bits(want.values()[:n]))
         if cap > nnzb:  # untouched beyond the true count
             assert torch.all(ci.cpu()[nnzb:] == -1) and torch.all(v.cpu()[nnzb:] == 7.0)
