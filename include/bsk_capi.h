@@ -266,8 +266,9 @@ int bsk_bsattn_fwd_f16(const void* Q, const void* K, const void* V, void* O, con
  * must get the workspace, row_ptr and nnzb its pattern call produced, unchanged (col_idx and values may be NULL
  * when nnzb is 0).
  * The pattern call synchronises `stream` to return *nnzb (stored blocks) and *nnz_elems (nonzero elements).
- * CSR input: crow [M + 1], col [nnz] (index_bytes_in 4 or 8), vals [nnz]; a column index outside [0, K) fails the
- * pattern call with BSK_ERR_INVALID_ARG. Entries stored twice for one (row, col) are not summed (one value wins).
+ * CSR input: crow [M + 1], col [nnz] (index_bytes_in 4 or 8), vals [nnz]; row r holds entries [crow[r], crow[r+1])
+ * and entries outside [crow[0], crow[M]) are ignored; a column index outside [0, K) fails the pattern call with
+ * BSK_ERR_INVALID_ARG. Entries stored twice for one (row, col) are not summed (one value wins).
  */
 int64_t bsk_bsr_convert_workspace_bytes(int M, int K, int bs);
 int bsk_dense_to_bsr_pattern(const void* A, int64_t lda, int elem_bytes, int M, int K, int bs, void* row_ptr,

@@ -510,6 +510,240 @@ __global__ void __launch_bounds__(kConvThreads) csr_scatter_kernel(const IdxIn* 
   }
 }
 
+// Quad path of the two CSR passes, taken when col is 16-byte aligned and vals is aligned to 4 elements: a lane
+// handles whole quads (4 consecutive entries, quad q = entries [4q, 4q + 4)) with one vector load of 4 columns and
+// one of 4 values, a warp owns a contiguous run of quads and walks it in trips of 32 x kConvQuadU lane-contiguous
+// quads. Entries outside [crow[0], crow[M]) that share a quad with entries inside are loaded and skipped; a quad
+// that runs past the end of the arrays (nnz) is loaded entry by entry.
+constexpr int kConvQuadU = 4;
+constexpr int kConvQuadCtas = 4;  // resident CTAs per SM at the kernels' register budget (<= 64 per thread)
+
+template <typename E>
+__device__ __forceinline__ void warp_quads(E eb, E ee, int64_t w, int64_t nw, E& Q0, E& Q1) {
+  const int64_t qa = static_cast<int64_t>(eb) >> 2, qb = (static_cast<int64_t>(ee) + 3) >> 2;
+  const int64_t n = qb - qa;
+  const int64_t per = ((n + nw - 1) / nw + 31) / 32 * 32;
+  const int64_t a = w * per, b = a + per;
+  Q0 = static_cast<E>(qa + (a < n ? a : n));
+  Q1 = static_cast<E>(qa + (b < n ? b : n));
+}
+
+// Last r in [0, M) with crow[r] <= e, by a 32-way search over the warp (three rounds for M <= 32768). All lanes
+// pass the same e.
+template <typename IdxIn, typename E>
+__device__ __forceinline__ int csr_row_of_warp(const IdxIn* crow, int M, E e, E nnz, int lane) {
+  int lo = 0, hi = M;
+  while (hi - lo > 1) {
+    const int64_t span = hi - lo;
+    const bool le = crow_at(crow, lo + static_cast<int>(span * lane / 32), nnz) <= e;
+    const int L = 31 - __clz(__ballot_sync(0xFFFFFFFFu, le) | 1u);
+    const int nlo = lo + static_cast<int>(span * L / 32);
+    hi = L == 31 ? hi : lo + static_cast<int>(span * (L + 1) / 32);
+    lo = nlo;
+  }
+  return lo;
+}
+
+template <typename IdxIn>
+__device__ __forceinline__ int clamp_col(IdxIn v) {
+  return static_cast<int>(max(min(static_cast<int64_t>(v), static_cast<int64_t>(INT32_MAX)), static_cast<int64_t>(-1)));
+}
+
+// Columns (clamped to [-1, INT32_MAX]) and value bits of quad q; entries at or past nnz read as (-1, 0).
+template <int kElemBytes, typename IdxIn, typename E>
+__device__ __forceinline__ void load_quad(const IdxIn* __restrict__ col, const uint8_t* __restrict__ vals, E q, E nnz,
+                                          int (&c)[4], uint32_t (&bits)[4], uint4& raw) {
+  const int64_t p0 = static_cast<int64_t>(q) * 4;
+  if (p0 + 4 <= static_cast<int64_t>(nnz)) {
+    if (sizeof(IdxIn) == 4) {
+      const int4 v = *reinterpret_cast<const int4*>(col + p0);
+      c[0] = clamp_col(v.x); c[1] = clamp_col(v.y); c[2] = clamp_col(v.z); c[3] = clamp_col(v.w);
+    } else {
+      const longlong2 v0 = *reinterpret_cast<const longlong2*>(col + p0);
+      const longlong2 v1 = *reinterpret_cast<const longlong2*>(col + p0 + 2);
+      c[0] = clamp_col(v0.x); c[1] = clamp_col(v0.y); c[2] = clamp_col(v1.x); c[3] = clamp_col(v1.y);
+    }
+    if (kElemBytes == 2) {
+      const uint2 v = *reinterpret_cast<const uint2*>(vals + p0 * 2);
+      raw = make_uint4(v.x, v.y, 0u, 0u);
+      bits[0] = v.x & 0xFFFFu; bits[1] = v.x >> 16; bits[2] = v.y & 0xFFFFu; bits[3] = v.y >> 16;
+    } else {
+      raw = *reinterpret_cast<const uint4*>(vals + p0 * 4);
+      bits[0] = raw.x; bits[1] = raw.y; bits[2] = raw.z; bits[3] = raw.w;
+    }
+  } else {
+    raw = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const bool in = p0 + j < static_cast<int64_t>(nnz);
+      c[j] = in ? clamp_col(col[p0 + j]) : -1;
+      bits[j] = in ? load_bits<kElemBytes>(vals + (p0 + j) * kElemBytes) : 0u;
+    }
+  }
+}
+
+// Pattern pass, quad path (same results as csr_flags_kernel).
+template <int kElemBytes, typename IdxIn, typename E, bool kPow2>
+__global__ void __launch_bounds__(kConvThreads, kConvQuadCtas)
+    csr_flags_quad_kernel(const IdxIn* __restrict__ crow, const IdxIn* __restrict__ col,
+                          const uint8_t* __restrict__ vals, E nnz, int M, int K, int bs, int lg, int Kb,
+                          int* __restrict__ flags, unsigned long long* __restrict__ nnz_out, int* __restrict__ bad) {
+  const int lane = threadIdx.x & 31;
+  const E eb = crow_at(crow, 0, nnz), ee = crow_at(crow, M, nnz);
+  E Q0, Q1;
+  warp_quads(eb, ee, (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5,
+             (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5, Q0, Q1);
+  unsigned long long count = 0;
+  if (Q0 < Q1) {
+    const E E0 = max(eb, static_cast<E>(4 * Q0)), E1 = min(ee, static_cast<E>(4 * Q1));
+    int row = csr_row_of_warp(crow, M, E0, nnz, lane);
+    E row_end = crow_at(crow, row + 1, nnz);
+    int* frow = flags + static_cast<int64_t>(div_bs<kPow2>(row, bs, lg)) * Kb;
+    int* last = nullptr;
+    bool any_bad = false;
+    auto visit = [&](E p, int c, uint32_t b) {
+      if (p >= row_end) {
+        while (p >= row_end && row + 1 < M) row_end = crow_at(crow, ++row + 1, nnz);
+        frow = flags + static_cast<int64_t>(div_bs<kPow2>(row, bs, lg)) * Kb;
+      }
+      if (static_cast<unsigned>(c) >= static_cast<unsigned>(K)) {
+        any_bad = true;
+      } else if (elem_nonzero<kElemBytes>(b)) {
+        ++count;
+        int* f = frow + div_bs<kPow2>(c, bs, lg);
+        if (f != last) {  // a lane's consecutive entries usually share a block: store each flag once per run
+          *f = 1;
+          last = f;
+        }
+      }
+    };
+    for (E qb = Q0 + lane; qb < Q1 + lane; qb += 32 * kConvQuadU) {
+      int c[kConvQuadU][4];
+      uint32_t bits[kConvQuadU][4];
+      uint4 raw[kConvQuadU];
+#pragma unroll
+      for (int u = 0; u < kConvQuadU; ++u) {
+        const E q = qb + 32 * u;
+        if (q < Q1) {
+          load_quad<kElemBytes>(col, vals, q, nnz, c[u], bits[u], raw[u]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) { c[u][j] = -1; bits[u][j] = 0u; }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kConvQuadU; ++u) {
+        const E q = qb + 32 * u;
+        if (q >= Q1) break;
+        const E p0 = 4 * q;
+        if (p0 >= E0 && p0 + 4 <= E1) {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) visit(p0 + j, c[u][j], bits[u][j]);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (p0 + j >= E0 && p0 + j < E1) visit(p0 + j, c[u][j], bits[u][j]);
+        }
+      }
+    }
+    if (any_bad) *bad = 1;
+  }
+  for (int o = 16; o > 0; o >>= 1) count += __shfl_xor_sync(0xFFFFFFFFu, count, o);
+  if (lane == 0 && count) atomicAdd(nnz_out, count);
+}
+
+// Fill step 2, quad path (same results as csr_scatter_kernel). A warp walks its quads last trip first and each
+// lane its entries in descending order, so that the entries the pattern pass read last, the ones most likely
+// still in L2, are read first. A quad of 4 consecutive in-range columns starting at a multiple of 4 (one block,
+// one row) is written with one 4-element store when `values` is aligned to 4 elements and bs % 4 == 0 (kStore4).
+template <int kElemBytes, typename IdxIn, typename E, bool kPow2, bool kStore4>
+__global__ void __launch_bounds__(kConvThreads, kConvQuadCtas)
+    csr_scatter_quad_kernel(const IdxIn* __restrict__ crow, const IdxIn* __restrict__ col,
+                            const uint8_t* __restrict__ vals, E nnz, int M, int K, int bs, int lg, int Kb,
+                            const int* __restrict__ map, int64_t cap, uint8_t* __restrict__ values) {
+  const int lane = threadIdx.x & 31;
+  const E eb = crow_at(crow, 0, nnz), ee = crow_at(crow, M, nnz);
+  E Q0, Q1;
+  warp_quads(eb, ee, (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5,
+             (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5, Q0, Q1);
+  if (Q0 >= Q1) return;
+  const E E0 = max(eb, static_cast<E>(4 * Q0)), E1 = min(ee, static_cast<E>(4 * Q1));
+  // rows move backwards only: every entry a lane visits lies below the previous one (row_end stays above it)
+  int row = csr_row_of_warp(crow, M, static_cast<E>(E1 - 1), nnz, lane);
+  E row_start = crow_at(crow, row, nnz);
+  const int* mrow = map + static_cast<int64_t>(div_bs<kPow2>(row, bs, lg)) * Kb;
+  int r_in = mod_bs<kPow2>(row, bs, lg);
+  auto seek = [&](E p) {
+    if (p < row_start) {
+      while (p < row_start && row > 0) row_start = crow_at(crow, --row, nnz);
+      mrow = map + static_cast<int64_t>(div_bs<kPow2>(row, bs, lg)) * Kb;
+      r_in = mod_bs<kPow2>(row, bs, lg);
+    }
+  };
+  auto put = [&](int c, uint32_t b) {
+    if (static_cast<unsigned>(c) >= static_cast<unsigned>(K)) return;
+    const int pos = mrow[div_bs<kPow2>(c, bs, lg)];
+    if (pos < 0 || pos >= cap) return;  // block of explicit zeros only (not stored), or past capacity
+    uint8_t* dst = values + ((static_cast<int64_t>(pos) * bs + r_in) * bs + mod_bs<kPow2>(c, bs, lg)) * kElemBytes;
+    if (kElemBytes == 2)
+      *reinterpret_cast<uint16_t*>(dst) = static_cast<uint16_t>(b);
+    else
+      *reinterpret_cast<uint32_t*>(dst) = b;
+  };
+  const int64_t trips = (static_cast<int64_t>(Q1 - Q0) + 32 * kConvQuadU - 1) / (32 * kConvQuadU);
+  for (int64_t t = trips - 1; t >= 0; --t) {
+    const E qb = Q0 + static_cast<E>(t * 32 * kConvQuadU) + lane;
+    int c[kConvQuadU][4];
+    uint32_t bits[kConvQuadU][4];
+    uint4 raw[kConvQuadU];
+#pragma unroll
+    for (int u = 0; u < kConvQuadU; ++u) {
+      const E q = qb + 32 * u;
+      if (q < Q1) {
+        load_quad<kElemBytes>(col, vals, q, nnz, c[u], bits[u], raw[u]);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) { c[u][j] = -1; bits[u][j] = 0u; }
+        raw[u] = make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+#pragma unroll
+    for (int u = kConvQuadU - 1; u >= 0; --u) {
+      const E q = qb + 32 * u;
+      if (q >= Q1) continue;
+      const E p0 = 4 * q;
+      if (p0 >= E0 && p0 + 4 <= E1) {
+        seek(p0 + 3);
+        if (kStore4 && p0 >= row_start && (c[u][0] & 3) == 0 && c[u][1] == c[u][0] + 1 &&
+            c[u][2] == c[u][0] + 2 && c[u][3] == c[u][0] + 3 && c[u][0] >= 0 && c[u][3] < K) {
+          const int pos = mrow[div_bs<kPow2>(c[u][0], bs, lg)];
+          if (pos >= 0 && pos < cap) {
+            uint8_t* dst = values +
+                           ((static_cast<int64_t>(pos) * bs + r_in) * bs + mod_bs<kPow2>(c[u][0], bs, lg)) * kElemBytes;
+            if (kElemBytes == 2)
+              *reinterpret_cast<uint2*>(dst) = make_uint2(raw[u].x, raw[u].y);
+            else
+              *reinterpret_cast<uint4*>(dst) = raw[u];
+          }
+          continue;
+        }
+#pragma unroll
+        for (int j = 3; j >= 0; --j) {
+          seek(p0 + j);
+          put(c[u][j], bits[u][j]);
+        }
+      } else {
+#pragma unroll
+        for (int j = 3; j >= 0; --j) {
+          if (p0 + j < E0 || p0 + j >= E1) continue;
+          seek(p0 + j);
+          put(c[u][j], bits[u][j]);
+        }
+      }
+    }
+  }
+}
+
 // values[0 .. min(nnzb, cap) blocks) = 0 (nnzb read from device memory): 16-byte stores when the span allows.
 __global__ void __launch_bounds__(kConvThreads) zero_blocks_kernel(uint8_t* __restrict__ values,
                                                                   const long long* __restrict__ nnzb_dev, int64_t cap,
@@ -531,17 +765,29 @@ inline int log2_exact(int bs) {
   return (1 << lg) == bs ? lg : -1;
 }
 
+inline bool csr_quad_ok(const void* col, const void* vals, int elem_bytes) {
+  return reinterpret_cast<uintptr_t>(col) % 16 == 0 && reinterpret_cast<uintptr_t>(vals) % (4 * elem_bytes) == 0;
+}
+
 template <typename IdxIn>
 void launch_csr_flags(int elem_bytes, const void* crow, const void* col, const void* vals, int64_t nnz, int M, int K,
-                      int bs, int Kb, int* flags, unsigned long long* counter, int* bad, int grid, cudaStream_t s) {
+                      int bs, int Kb, int* flags, unsigned long long* counter, int* bad, int sm_count,
+                      cudaStream_t s) {
   const IdxIn* c = static_cast<const IdxIn*>(crow);
   const IdxIn* ci = static_cast<const IdxIn*>(col);
   const uint8_t* v = static_cast<const uint8_t*>(vals);
   const int lg = log2_exact(bs);
   const bool small = nnz < (int64_t(1) << 31) - 32 * kConvCsrU * 2;
-#define BSK_CF(EB, E, P) \
-  csr_flags_kernel<EB, IdxIn, E, P><<<grid, kConvThreads, 0, s>>>(c, ci, v, static_cast<E>(nnz), M, K, bs, lg, Kb, \
-                                                                  flags, counter, bad)
+  const bool quad = csr_quad_ok(col, vals, elem_bytes);
+#define BSK_CF(EB, E, P)                                                                                              \
+  do {                                                                                                                \
+    if (quad)                                                                                                         \
+      csr_flags_quad_kernel<EB, IdxIn, E, P><<<sm_count * kConvQuadCtas, kConvThreads, 0, s>>>(                      \
+          c, ci, v, static_cast<E>(nnz), M, K, bs, lg, Kb, flags, counter, bad);                                      \
+    else                                                                                                              \
+      csr_flags_kernel<EB, IdxIn, E, P><<<sm_count * 8, kConvThreads, 0, s>>>(c, ci, v, static_cast<E>(nnz), M, K,   \
+                                                                              bs, lg, Kb, flags, counter, bad);       \
+  } while (0)
   if (elem_bytes == 2) {
     if (small) { if (lg >= 0) BSK_CF(2, int, true); else BSK_CF(2, int, false); }
     else { if (lg >= 0) BSK_CF(2, int64_t, true); else BSK_CF(2, int64_t, false); }
@@ -554,16 +800,29 @@ void launch_csr_flags(int elem_bytes, const void* crow, const void* col, const v
 
 template <typename IdxIn>
 void launch_csr_scatter(int elem_bytes, const void* crow, const void* col, const void* vals, int64_t nnz, int M,
-                        int K, int bs, int Kb, const int* map, int64_t cap, void* values, int grid, cudaStream_t s) {
+                        int K, int bs, int Kb, const int* map, int64_t cap, void* values, int sm_count,
+                        cudaStream_t s) {
   const IdxIn* c = static_cast<const IdxIn*>(crow);
   const IdxIn* ci = static_cast<const IdxIn*>(col);
   const uint8_t* v = static_cast<const uint8_t*>(vals);
   uint8_t* out = static_cast<uint8_t*>(values);
   const int lg = log2_exact(bs);
   const bool small = nnz < (int64_t(1) << 31) - 32 * kConvCsrU * 2;
-#define BSK_CS(EB, E, P) \
-  csr_scatter_kernel<EB, IdxIn, E, P><<<grid, kConvThreads, 0, s>>>(c, ci, v, static_cast<E>(nnz), M, K, bs, lg, Kb, \
-                                                                    map, cap, out)
+  const bool quad = csr_quad_ok(col, vals, elem_bytes);
+  const bool store4 = reinterpret_cast<uintptr_t>(values) % (4 * elem_bytes) == 0 && bs % 4 == 0;
+#define BSK_CS(EB, E, P)                                                                                              \
+  do {                                                                                                                \
+    const int g = sm_count * kConvQuadCtas;                                                                           \
+    if (quad && store4)                                                                                               \
+      csr_scatter_quad_kernel<EB, IdxIn, E, P, true><<<g, kConvThreads, 0, s>>>(c, ci, v, static_cast<E>(nnz), M, K, \
+                                                                                bs, lg, Kb, map, cap, out);           \
+    else if (quad)                                                                                                    \
+      csr_scatter_quad_kernel<EB, IdxIn, E, P, false><<<g, kConvThreads, 0, s>>>(c, ci, v, static_cast<E>(nnz), M,   \
+                                                                                 K, bs, lg, Kb, map, cap, out);       \
+    else                                                                                                              \
+      csr_scatter_kernel<EB, IdxIn, E, P><<<sm_count * 8, kConvThreads, 0, s>>>(c, ci, v, static_cast<E>(nnz), M, K, \
+                                                                                bs, lg, Kb, map, cap, out);           \
+  } while (0)
   if (elem_bytes == 2) {
     if (small) { if (lg >= 0) BSK_CS(2, int, true); else BSK_CS(2, int, false); }
     else { if (lg >= 0) BSK_CS(2, int64_t, true); else BSK_CS(2, int64_t, false); }

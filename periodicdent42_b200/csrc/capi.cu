@@ -1350,13 +1350,12 @@ int csr_pattern_enqueue(const void* crow, const void* col, int index_bytes_in, c
   if (int rc = conv_clear(p, workspace, s, what)) return rc;
   const ConvWs w = conv_ws(p, workspace);
   if (M > 0 && nnz > 0) {
-    const int g = conv_grid(st);
     if (index_bytes_in == 4)
       launch_csr_flags<int32_t>(elem_bytes, crow, col, vals, nnz, M, K, bs, p.Kb, w.flags, &w.tail->nnz_elems,
-                                &w.tail->bad, g, s);
+                                &w.tail->bad, st->sm_count, s);
     else
       launch_csr_flags<int64_t>(elem_bytes, crow, col, vals, nnz, M, K, bs, p.Kb, w.flags, &w.tail->nnz_elems,
-                                &w.tail->bad, g, s);
+                                &w.tail->bad, st->sm_count, s);
   }
   if (!index) return launch_status(what);
   if (p.Mb > 0) {
@@ -1426,9 +1425,11 @@ int csr_fill_enqueue(const void* crow, const void* col, int index_bytes_in, cons
                                                 (int64_t)bs * bs * elem_bytes);
   if (M > 0 && nnz > 0) {
     if (index_bytes_in == 4)
-      launch_csr_scatter<int32_t>(elem_bytes, crow, col, vals, nnz, M, K, bs, p.Kb, w.flags, cap, values, g, s);
+      launch_csr_scatter<int32_t>(elem_bytes, crow, col, vals, nnz, M, K, bs, p.Kb, w.flags, cap, values, st->sm_count,
+                                  s);
     else
-      launch_csr_scatter<int64_t>(elem_bytes, crow, col, vals, nnz, M, K, bs, p.Kb, w.flags, cap, values, g, s);
+      launch_csr_scatter<int64_t>(elem_bytes, crow, col, vals, nnz, M, K, bs, p.Kb, w.flags, cap, values, st->sm_count,
+                                  s);
   }
   return launch_status(what);
 }

@@ -124,6 +124,55 @@ def test_csr_matches_to_dense_path(no_device_error, cuda_dev, idx, dtype, bs):
     assert got[0].dtype == idx
 
 
+def _shifted(t: torch.Tensor, k: int) -> torch.Tensor:
+    """A copy of t whose storage starts k elements into a larger buffer (a pointer off the vector alignment)."""
+    buf = torch.zeros(t.numel() + k, dtype=t.dtype, device=t.device)
+    buf[k:] = t
+    return buf[k:]
+
+
+# The CSR passes take a quad path (4 entries per vector load) when col is 16-byte aligned and vals 4-element
+# aligned, with one 4-element store per quad when the values output is 4-element aligned and bs % 4 == 0; these
+# cases cover both paths and the quad path's boundaries: entries outside [crow[0], crow[M]) at either end (partial
+# quads, out-of-range junk that must be ignored), rows shorter than a quad (row changes inside a quad, empty rows),
+# columns unsorted within rows, block sizes that are not powers of two or not multiples of 4, an unaligned output.
+@pytest.mark.parametrize("idx", [torch.int32, torch.int64])
+@pytest.mark.parametrize("dtype", [torch.float16, torch.float32])
+@pytest.mark.parametrize("case", ["aligned", "offset_inputs", "junk_ends", "short_rows", "unsorted", "bs6", "bs12",
+                                  "offset_output"])
+def test_csr_quad_and_scalar_paths(no_device_error, cuda_dev, idx, dtype, case):
+    M, K, bs, ed = {"short_rows": (1024, 64, 8, 0.03), "bs6": (96, 120, 6, 0.5),
+                    "bs12": (240, 96, 12, 0.5)}.get(case, (384, 256, 16, 0.4))
+    x = _sparse_dense(M, K, bs, dtype, 101 + len(case), block_density=0.4, elem_density=ed)
+    csr = x.to_sparse_csr()
+    crow, col, vals = csr.crow_indices().to(idx), csr.col_indices().to(idx), csr.values()
+    want = csr.to_dense().to_sparse_bsr((bs, bs))
+    if case == "junk_ends":  # 3 entries before crow[0], 5 after crow[M]; their columns are out of range
+        col = torch.cat([torch.tensor([-5, K + 7, 2], dtype=idx), col, torch.tensor([K, -1, 0, 1, K + 3], dtype=idx)])
+        vals = torch.cat([torch.ones(3, dtype=dtype), vals, torch.ones(5, dtype=dtype)])
+        crow = crow + 3
+    elif case == "unsorted":
+        for r in range(M):
+            a, b = int(crow[r]), int(crow[r + 1])
+            col[a:b] = col[a:b].flip(0).clone()
+            vals[a:b] = vals[a:b].flip(0).clone()
+    crow, col, vals = crow.to(cuda_dev), col.to(cuda_dev), vals.to(cuda_dev)
+    if case == "offset_inputs":
+        col, vals = _shifted(col, 1), _shifted(vals, 1)
+    if case != "offset_output":
+        got = _capi.csr_to_bsr(crow, col, vals, (M, K), bs, index_dtype=idx)
+        _assert_same(got, want)
+        assert got[3] == int(torch.count_nonzero(x))
+        return
+    nnzb = want.col_indices().numel()
+    ws = torch.empty(_capi.bsr_convert_workspace_bytes(M, K, bs), dtype=torch.uint8, device=cuda_dev)
+    rp = torch.empty(M // bs + 1, dtype=idx, device=cuda_dev)
+    ci = torch.empty(nnzb, dtype=idx, device=cuda_dev)
+    v = torch.empty(nnzb * bs * bs + 1, dtype=dtype, device=cuda_dev)[1:].view(nnzb, bs, bs)
+    _capi.csr_to_bsr_bounded(crow, col, vals, (M, K), bs, rp, ci, v, ws)
+    _assert_same((rp, ci, v), want)
+
+
 def test_csr_explicit_zeros_drop_blocks(no_device_error, cuda_dev):
     crow = torch.tensor([0, 2, 3, 3, 3])
     col = torch.tensor([0, 3, 5])
