@@ -17,6 +17,8 @@
 
 #include <cstdint>
 
+#include "ptx_sm100.cuh"
+
 namespace bsk {
 
 constexpr int kConvThreads = 256;
@@ -68,7 +70,7 @@ __global__ void __launch_bounds__(kConvThreads) dense_flags_vec_kernel(const uin
 #pragma unroll
     for (int u = 0; u < kConvU; ++u) {
       const int c = c0 + 32 * u;
-      v[u] = c < cpr ? rp[c] : make_uint4(0, 0, 0, 0);
+      v[u] = c < cpr ? ptx::ldg_stream_16(rp + c) : make_uint4(0, 0, 0, 0);
     }
   };
   int64_t task = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -556,19 +558,22 @@ __device__ __forceinline__ void load_quad(const IdxIn* __restrict__ col, const u
   const int64_t p0 = static_cast<int64_t>(q) * 4;
   if (p0 + 4 <= static_cast<int64_t>(nnz)) {
     if (sizeof(IdxIn) == 4) {
-      const int4 v = *reinterpret_cast<const int4*>(col + p0);
-      c[0] = clamp_col(v.x); c[1] = clamp_col(v.y); c[2] = clamp_col(v.z); c[3] = clamp_col(v.w);
+      const uint4 v = ptx::ldg_stream_16(col + p0);
+      c[0] = clamp_col(static_cast<int>(v.x)); c[1] = clamp_col(static_cast<int>(v.y));
+      c[2] = clamp_col(static_cast<int>(v.z)); c[3] = clamp_col(static_cast<int>(v.w));
     } else {
-      const longlong2 v0 = *reinterpret_cast<const longlong2*>(col + p0);
-      const longlong2 v1 = *reinterpret_cast<const longlong2*>(col + p0 + 2);
-      c[0] = clamp_col(v0.x); c[1] = clamp_col(v0.y); c[2] = clamp_col(v1.x); c[3] = clamp_col(v1.y);
+      const uint4 v0 = ptx::ldg_stream_16(col + p0), v1 = ptx::ldg_stream_16(col + p0 + 2);
+      c[0] = clamp_col(static_cast<long long>((static_cast<uint64_t>(v0.y) << 32) | v0.x));
+      c[1] = clamp_col(static_cast<long long>((static_cast<uint64_t>(v0.w) << 32) | v0.z));
+      c[2] = clamp_col(static_cast<long long>((static_cast<uint64_t>(v1.y) << 32) | v1.x));
+      c[3] = clamp_col(static_cast<long long>((static_cast<uint64_t>(v1.w) << 32) | v1.z));
     }
     if (kElemBytes == 2) {
-      const uint2 v = *reinterpret_cast<const uint2*>(vals + p0 * 2);
+      const uint2 v = ptx::ldg_stream_8(vals + p0 * 2);
       raw = make_uint4(v.x, v.y, 0u, 0u);
       bits[0] = v.x & 0xFFFFu; bits[1] = v.x >> 16; bits[2] = v.y & 0xFFFFu; bits[3] = v.y >> 16;
     } else {
-      raw = *reinterpret_cast<const uint4*>(vals + p0 * 4);
+      raw = ptx::ldg_stream_16(vals + p0 * 4);
       bits[0] = raw.x; bits[1] = raw.y; bits[2] = raw.z; bits[3] = raw.w;
     }
   } else {

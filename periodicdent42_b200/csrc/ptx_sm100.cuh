@@ -94,6 +94,22 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
+// ---------------------------------------------------------------- streaming loads
+// Read-only global loads that skip L1 allocation and ask L2 to fetch the whole 256-byte span around the address
+// (more DRAM requests in flight per load for inputs read once, front to back). p must be 16- (8-) byte aligned.
+__device__ __forceinline__ uint4 ldg_stream_16(const void* p) {
+  uint4 v;
+  asm("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0, %1, %2, %3}, [%4];"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p));
+  return v;
+}
+__device__ __forceinline__ uint2 ldg_stream_8(const void* p) {
+  uint2 v;
+  asm("ld.global.nc.L1::no_allocate.L2::256B.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
+  return v;
+}
+
 // ---------------------------------------------------------------- TMA (bulk tensor)
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m)) : "memory");
